@@ -1,0 +1,453 @@
+// C ABI of libace_b200.so: argument checks, bin tables, launch configuration.
+// The kernels themselves are in ace_kernels.cuh.
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <unordered_map>
+
+#include "ace_kernels.cuh"
+
+namespace ace {
+
+// The kernel instances live in ace_kern_{f32,bf16,f16}.cu.
+#define ACE_EXTERN(T)                                                                      \
+  extern template cudaError_t launch_hist<T>(const FwdParams&, const Variant&, dim3, int, \
+                                             cudaStream_t);                                \
+  extern template cudaError_t launch_grad<T>(const BwdParams&, const Variant&, dim3, int, \
+                                             cudaStream_t);                                \
+  extern template int hist_occupancy<T>(const Variant&, int);                              \
+  extern template int grad_occupancy<T>(const Variant&, int);                              \
+  extern template cudaError_t launch_probs<T>(const void*, float*, int64_t, int, int64_t, \
+                                              int, cudaStream_t);
+ACE_EXTERN(float)
+ACE_EXTERN(__nv_bfloat16)
+ACE_EXTERN(__half)
+#undef ACE_EXTERN
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(ACE_B200_ECUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+// torch.linspace(0, 1 + eps32, steps) in fp32, element i. ATen computes
+// step = (end - start) / (steps - 1) in fp32 and start + step * i for the first
+// half, end - step * (steps - 1 - i) for the second, each with one rounding (a
+// fused multiply-add); a CPU test checks the tables against torch.linspace.
+float linspace_at(int steps, int i) {
+  const float start = 0.0f;
+  const float end = 1.0f + 1.1920928955078125e-07f;
+  const float step = (end - start) / (float)(steps - 1);
+  const int halfway = steps / 2;
+  if (i < halfway) return fmaf(step, (float)i, start);
+  return fmaf(-step, (float)(steps - 1 - i), end);
+}
+
+// Hard: the K upper edges linspace(K + 1)[1:]; soft: the K centres
+// linspace(2K + 1)[1::2] (ace_kernels/common.py:17-25).
+void table_values(int K, bool soft, float* out) {
+  for (int j = 0; j < K; ++j)
+    out[j] = soft ? linspace_at(2 * K + 1, 2 * j + 1) : linspace_at(K + 1, j + 1);
+}
+
+void build_table(int K, bool soft, BinTable& t) {
+  float v[kMaxBins];
+  table_values(K, soft, v);
+  t.K = K;
+  for (int i = 0; i <= K; ++i) {
+    t.pair[i].x = i == 0 ? -10000.0f : v[i - 1];
+    t.pair[i].y = i == K ? 10000.0f : v[i];
+  }
+}
+
+struct DeviceInfo {
+  int sms = 0;
+};
+
+int sm_count(int dev) {
+  static int cache[64] = {0};
+  if (dev >= 0 && dev < 64 && cache[dev]) return cache[dev];
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+    n = 148;
+  if (dev >= 0 && dev < 64) cache[dev] = n;
+  return n;
+}
+
+size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+size_t accum_bytes(int64_t b_total, int64_t cl, int K) {
+  return round_up((size_t)3 * b_total * cl * K * sizeof(float), 256);
+}
+
+// Per-variant occupancy, cached (the query costs a few microseconds).
+struct OccKey {
+  int kind, dtype, V, CM, sm, soft, labels, smem, dev;
+  bool operator==(const OccKey& o) const { return memcmp(this, &o, sizeof(*this)) == 0; }
+};
+struct OccHash {
+  size_t operator()(const OccKey& k) const {
+    size_t h = 1469598103934665603ull;
+    const unsigned char* p = reinterpret_cast<const unsigned char*>(&k);
+    for (size_t i = 0; i < sizeof(k); ++i) h = (h ^ p[i]) * 1099511628211ull;
+    return h;
+  }
+};
+
+int occupancy(int kind, int dtype, const Variant& v, int smem, int dev) {
+  static std::mutex mu;
+  static std::unordered_map<OccKey, int, OccHash> cache;
+  OccKey key;
+  memset(&key, 0, sizeof(key));
+  key.kind = kind;
+  key.dtype = dtype;
+  key.V = v.V;
+  key.CM = v.CM;
+  key.sm = v.softmax;
+  key.soft = v.soft;
+  key.labels = v.labels;
+  key.smem = smem;
+  key.dev = dev;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  int n = 1;
+  if (kind == 0) {
+    if (dtype == ACE_B200_F32) n = hist_occupancy<float>(v, smem);
+    else if (dtype == ACE_B200_BF16) n = hist_occupancy<__nv_bfloat16>(v, smem);
+    else n = hist_occupancy<__half>(v, smem);
+  } else {
+    if (dtype == ACE_B200_F32) n = grad_occupancy<float>(v, smem);
+    else if (dtype == ACE_B200_BF16) n = grad_occupancy<__nv_bfloat16>(v, smem);
+    else n = grad_occupancy<__half>(v, smem);
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  cache[key] = n;
+  return n;
+}
+
+int elem_size(int dtype) { return dtype == ACE_B200_F32 ? 4 : 2; }
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// Checks shared by all entry points. Fills the loss-channel count.
+int check_common(const ace_b200_inputs* in, const ace_b200_options* opt, int& CL) {
+  if (!in || !opt) return fail(ACE_B200_EINVAL, "null inputs or options");
+  if (!in->x) return fail(ACE_B200_EINVAL, "x is null");
+  if (in->x_dtype != ACE_B200_F32 && in->x_dtype != ACE_B200_BF16 && in->x_dtype != ACE_B200_F16)
+    return fail(ACE_B200_EINVAL, "x_dtype %d is not fp32/bf16/fp16", in->x_dtype);
+  if (in->B < 1 || in->C < 1 || in->N < 0)
+    return fail(ACE_B200_EINVAL, "bad shape B=%lld C=%lld N=%lld", (long long)in->B,
+                (long long)in->C, (long long)in->N);
+  if (in->B > 65535) return fail(ACE_B200_EUNSUPPORTED, "B=%lld > 65535", (long long)in->B);
+  if (in->C > kMaxClasses)
+    return fail(ACE_B200_EUNSUPPORTED, "C=%lld channels > %d", (long long)in->C, kMaxClasses);
+  if (in->N > ((int64_t)1 << 40)) return fail(ACE_B200_EUNSUPPORTED, "N too large");
+  if (opt->num_bins < 1 || opt->num_bins > kMaxBins)
+    return fail(ACE_B200_EUNSUPPORTED, "num_bins=%d outside 1..%d", opt->num_bins, kMaxBins);
+  if (opt->offset != 0 && opt->offset != 1) return fail(ACE_B200_EINVAL, "offset must be 0 or 1");
+  if (opt->offset == 1 && in->C < 2)
+    return fail(ACE_B200_EINVAL, "offset=1 needs C > 1 (the reference ignores it for C = 1)");
+  if (opt->activation < 0 || opt->activation > 2) return fail(ACE_B200_EINVAL, "bad activation");
+  if (opt->reduction < 0 || opt->reduction > 2) return fail(ACE_B200_EINVAL, "bad reduction");
+  if (in->target_kind != ACE_B200_TARGET_LABELS && in->target_kind != ACE_B200_TARGET_DENSE)
+    return fail(ACE_B200_EINVAL, "bad target_kind");
+  if (in->target_kind == ACE_B200_TARGET_LABELS && in->C < 2)
+    return fail(ACE_B200_EINVAL, "label targets need C > 1 (one channel takes dense targets)");
+  if (!in->target) return fail(ACE_B200_EINVAL, "target is null");
+  if (!aligned(in->x, elem_size(in->x_dtype)) || !aligned(in->target, 4))
+    return fail(ACE_B200_EINVAL, "misaligned x or target");
+  if (in->target_kind == ACE_B200_TARGET_LABELS && !aligned(in->target, 8))
+    return fail(ACE_B200_EINVAL, "int64 labels must be 8-byte aligned");
+  CL = (int)in->C - opt->offset;
+  if (in->b_offset < 0 || in->b_total < in->b_offset + in->B)
+    return fail(ACE_B200_EINVAL, "b_offset=%lld b_total=%lld do not cover B=%lld",
+                (long long)in->b_offset, (long long)in->b_total, (long long)in->B);
+  if (in->b_total * CL > (int64_t)1 << 24)
+    return fail(ACE_B200_EUNSUPPORTED, "too many statistics rows");
+  return ACE_B200_OK;
+}
+
+// Kernel variant and vector width for this launch (see ACE_VARIANT_CASES).
+Variant choose_variant(const ace_b200_inputs* in, const ace_b200_options* opt, const void* out) {
+  Variant v;
+  v.softmax = opt->activation == ACE_B200_ACT_SOFTMAX && in->C > 1;
+  v.soft = opt->soft != 0;
+  v.labels = in->target_kind == ACE_B200_TARGET_LABELS;
+  const int es = elem_size(in->x_dtype);
+  const int vmax = 16 / es;
+  int V;
+  if (v.softmax) {
+    const int C = (int)in->C;
+    v.CM = C <= 4 ? 4 : C <= 8 ? 8 : C <= 16 ? 16 : C <= 32 ? 32 : 64;
+    V = v.CM == 4 ? vmax : v.CM == 8 ? (vmax < 4 ? vmax : 4) : v.CM == 16 ? 2 : 1;
+  } else {
+    v.CM = 1;
+    V = vmax;
+  }
+  bool ok = V > 1 && in->N % V == 0 && aligned(in->x, (size_t)V * es);
+  if (ok && !v.labels) ok = aligned(in->target, (size_t)V * 4);
+  if (ok && v.labels) ok = aligned(in->target, 16);
+  if (ok && out) ok = aligned(out, (size_t)V * es);
+  v.V = ok ? V : 1;
+  return v;
+}
+
+// One wave of CTAs, split over the batches; each CTA gets a contiguous run of
+// tiles of one batch.
+Grid make_grid(const ace_b200_inputs* in, int CL, int offset, int V, int ctas_per_sm, int dev) {
+  Grid g;
+  g.N = in->N;
+  g.B = (int)in->B;
+  g.C = (int)in->C;
+  g.CL = CL;
+  g.offset = offset;
+  const int64_t tile = (int64_t)kThreads * V;
+  g.tiles = (in->N + tile - 1) / tile;
+  const int64_t wave = (int64_t)sm_count(dev) * ctas_per_sm;
+  int64_t chunks = (wave + g.B - 1) / g.B;
+  if (chunks > g.tiles) chunks = g.tiles;
+  if (chunks < 1) chunks = 1;
+  g.tiles_per_chunk = (g.tiles + chunks - 1) / chunks;
+  if (g.tiles_per_chunk < 1) g.tiles_per_chunk = 1;
+  chunks = (g.tiles + g.tiles_per_chunk - 1) / g.tiles_per_chunk;
+  if (chunks < 1) chunks = 1;
+  g.chunks = (int)chunks;
+  return g;
+}
+
+int fill_epi(EpiParams& e, int64_t b_total, int CL, double rows_global,
+             const ace_b200_options* opt, const ace_b200_epilogue_out& out) {
+  if (!out.coef || !out.d || !out.jac || !out.f || !out.loss)
+    return fail(ACE_B200_EINVAL, "null epilogue output");
+  e.B_total = (int)b_total;
+  e.CL = CL;
+  e.K = opt->num_bins;
+  e.soft = opt->soft != 0;
+  e.empty_weight = opt->empty_weight;
+  e.ignore_empty = opt->ignore_empty != 0;
+  e.reduction = opt->reduction;
+  e.rows_global = rows_global > 0 ? rows_global : (double)(b_total * CL);
+  if (CL > kMaxClasses) return fail(ACE_B200_EUNSUPPORTED, "too many loss channels");
+  for (int c = 0; c < CL; ++c) {
+    const float w = opt->class_weights ? opt->class_weights[c] : 1.0f;
+    if (!(w >= 0.0f)) return fail(ACE_B200_EINVAL, "class weight %d is negative or NaN", c);
+    e.class_w[c] = w;
+  }
+  e.coef = out.coef;
+  e.d = out.d;
+  e.jac = out.jac;
+  e.f = out.f;
+  e.loss = out.loss;
+  return ACE_B200_OK;
+}
+
+int hist_impl(const ace_b200_inputs* in, const ace_b200_options* opt, float* hist,
+              const ace_b200_epilogue_out* out, void* workspace, size_t ws_bytes, void* stream) {
+  int CL = 0;
+  int rc = check_common(in, opt, CL);
+  if (rc) return rc;
+  if (!hist) return fail(ACE_B200_EINVAL, "hist is null");
+  const int K = opt->num_bins;
+  const size_t need = ace_b200_workspace_bytes(in->b_total, CL, K);
+  if (!workspace || ws_bytes < need)
+    return fail(ACE_B200_EINVAL, "workspace of %zu bytes needed, %zu given", need, ws_bytes);
+  if (!aligned(workspace, 256)) return fail(ACE_B200_EINVAL, "workspace must be 256-byte aligned");
+
+  FwdParams p;
+  memset(&p, 0, sizeof(p));
+  if (out) {
+    rc = fill_epi(p.epi, in->b_total, CL, in->rows_global, opt, *out);
+    if (rc) return rc;
+    p.do_epilogue = 1;
+  }
+  const Variant v = choose_variant(in, opt, nullptr);
+  // Lane replicas of the shared-memory table: as many as fit in 48 KB (32 =
+  // conflict-free), so several CTAs stay resident per SM.
+  const int entries = 3 * CL * K;
+  int R = 32;
+  while (R > 1 && (size_t)entries * R * 4 > 48 * 1024) R >>= 1;
+  const int smem = (int)(2 * (kMaxBins + 1) * sizeof(float) + (size_t)entries * R * 4);
+  if (smem > 227 * 1024) return fail(ACE_B200_EUNSUPPORTED, "statistics do not fit in shared memory");
+
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  const int occ = occupancy(0, in->x_dtype, v, smem, dev);
+  p.x = in->x;
+  p.target = in->target;
+  p.g = make_grid(in, CL, opt->offset, v.V, occ, dev);
+  p.act = opt->activation;
+  p.right = opt->right != 0;
+  p.soft = opt->soft != 0;
+  p.R = R;
+  p.b_offset = (int)in->b_offset;
+  p.B_total = (int)in->b_total;
+  p.accum = static_cast<float*>(workspace);
+  p.counter = reinterpret_cast<unsigned*>(static_cast<char*>(workspace) +
+                                          accum_bytes(in->b_total, CL, K));
+  p.hist_out = hist;
+  build_table(K, p.soft, p.tab);
+
+  const dim3 grid((unsigned)p.g.chunks, (unsigned)p.g.B);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (in->x_dtype == ACE_B200_F32) e = launch_hist<float>(p, v, grid, smem, s);
+  else if (in->x_dtype == ACE_B200_BF16) e = launch_hist<__nv_bfloat16>(p, v, grid, smem, s);
+  else e = launch_hist<__half>(p, v, grid, smem, s);
+  if (e != cudaSuccess) return cuda_fail(e, "histogram kernel launch");
+  return ACE_B200_OK;
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(kThreads) epilogue_kernel(const float* __restrict__ hist,
+                                                            const __grid_constant__ EpiParams E) {
+  epilogue_block(E, hist);
+}
+
+cudaError_t launch_epilogue(const float* hist, const EpiParams& e, cudaStream_t s) {
+  epilogue_kernel<<<1, kThreads, 0, s>>>(hist, e);
+  return cudaGetLastError();
+}
+
+}  // namespace ace
+
+using namespace ace;
+
+extern "C" {
+
+size_t ace_b200_workspace_bytes(int64_t b_total, int64_t cl, int32_t num_bins) {
+  if (b_total < 1 || cl < 1 || num_bins < 1) return 512;
+  return accum_bytes(b_total, cl, num_bins) + 256;
+}
+
+int ace_b200_forward(const ace_b200_inputs* in, const ace_b200_options* opt, float* hist,
+                     ace_b200_epilogue_out out, void* workspace, size_t workspace_bytes,
+                     void* stream) {
+  return hist_impl(in, opt, hist, &out, workspace, workspace_bytes, stream);
+}
+
+int ace_b200_hist(const ace_b200_inputs* in, const ace_b200_options* opt, float* hist,
+                  void* workspace, size_t workspace_bytes, void* stream) {
+  return hist_impl(in, opt, hist, nullptr, workspace, workspace_bytes, stream);
+}
+
+int ace_b200_epilogue(const float* hist, int64_t b_total, int64_t cl, double rows_global,
+                      const ace_b200_options* opt, ace_b200_epilogue_out out, void* stream) {
+  if (!hist || !opt) return fail(ACE_B200_EINVAL, "null hist or options");
+  if (b_total < 1 || cl < 1 || cl > kMaxClasses)
+    return fail(ACE_B200_EINVAL, "bad b_total=%lld cl=%lld", (long long)b_total, (long long)cl);
+  if (b_total * cl > (int64_t)1 << 24) return fail(ACE_B200_EUNSUPPORTED, "too many rows");
+  if (opt->num_bins < 1 || opt->num_bins > kMaxBins)
+    return fail(ACE_B200_EUNSUPPORTED, "num_bins=%d outside 1..%d", opt->num_bins, kMaxBins);
+  if (opt->reduction < 0 || opt->reduction > 2) return fail(ACE_B200_EINVAL, "bad reduction");
+  EpiParams e;
+  memset(&e, 0, sizeof(e));
+  int rc = fill_epi(e, b_total, (int)cl, rows_global, opt, out);
+  if (rc) return rc;
+  cudaError_t err = launch_epilogue(hist, e, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "epilogue kernel launch");
+  return ACE_B200_OK;
+}
+
+int ace_b200_backward(const ace_b200_inputs* in, const ace_b200_options* opt,
+                      const float* coef, const float* d, const float* jac,
+                      const float* grad_output, int32_t grad_per_row, void* dx, void* stream) {
+  int CL = 0;
+  int rc = check_common(in, opt, CL);
+  if (rc) return rc;
+  if (!coef || !d || !jac || !grad_output || !dx)
+    return fail(ACE_B200_EINVAL, "null coef, d, jac, grad_output or dx");
+  if (!aligned(dx, elem_size(in->x_dtype))) return fail(ACE_B200_EINVAL, "misaligned dx");
+  const int K = opt->num_bins;
+  BwdParams p;
+  memset(&p, 0, sizeof(p));
+  const Variant v = choose_variant(in, opt, dx);
+  const int smem = (int)(2 * (kMaxBins + 1) * sizeof(float) + (size_t)CL * K * 8 + CL * 4);
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  const int occ = occupancy(1, in->x_dtype, v, smem, dev);
+  p.x = in->x;
+  p.target = in->target;
+  p.dx = dx;
+  p.g = make_grid(in, CL, opt->offset, v.V, occ, dev);
+  p.act = opt->activation;
+  p.right = opt->right != 0;
+  p.soft = opt->soft != 0;
+  p.b_offset = (int)in->b_offset;
+  p.coef = coef;
+  p.d = d;
+  p.jac = jac;
+  p.grad_out = grad_output;
+  p.grad_per_row = grad_per_row != 0;
+  build_table(K, p.soft, p.tab);
+  const dim3 grid((unsigned)p.g.chunks, (unsigned)p.g.B);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (in->x_dtype == ACE_B200_F32) e = launch_grad<float>(p, v, grid, smem, s);
+  else if (in->x_dtype == ACE_B200_BF16) e = launch_grad<__nv_bfloat16>(p, v, grid, smem, s);
+  else e = launch_grad<__half>(p, v, grid, smem, s);
+  if (e != cudaSuccess) return cuda_fail(e, "gradient kernel launch");
+  return ACE_B200_OK;
+}
+
+int ace_b200_probs(const ace_b200_inputs* in, int32_t activation, float* probs, void* stream) {
+  if (!in || !in->x || !probs) return fail(ACE_B200_EINVAL, "null x or probs");
+  if (in->B < 1 || in->C < 1 || in->C > kMaxClasses || in->N < 0)
+    return fail(ACE_B200_EINVAL, "bad shape");
+  if (activation < 0 || activation > 2) return fail(ACE_B200_EINVAL, "bad activation");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (in->x_dtype == ACE_B200_F32)
+    e = launch_probs<float>(in->x, probs, in->B, (int)in->C, in->N, activation, s);
+  else if (in->x_dtype == ACE_B200_BF16)
+    e = launch_probs<__nv_bfloat16>(in->x, probs, in->B, (int)in->C, in->N, activation, s);
+  else if (in->x_dtype == ACE_B200_F16)
+    e = launch_probs<__half>(in->x, probs, in->B, (int)in->C, in->N, activation, s);
+  else
+    return fail(ACE_B200_EINVAL, "bad x_dtype");
+  if (e != cudaSuccess) return cuda_fail(e, "probability kernel launch");
+  return ACE_B200_OK;
+}
+
+int ace_b200_bin_table(int32_t num_bins, int32_t soft, float* out) {
+  if (!out) return fail(ACE_B200_EINVAL, "out is null");
+  if (num_bins < 1 || num_bins > kMaxBins)
+    return fail(ACE_B200_EUNSUPPORTED, "num_bins=%d outside 1..%d", num_bins, kMaxBins);
+  table_values(num_bins, soft != 0, out);
+  return ACE_B200_OK;
+}
+
+int ace_b200_bin_index_host(const float* p, int64_t n, int32_t num_bins, int32_t soft,
+                            int32_t right, int32_t* out) {
+  if ((!p || !out) && n > 0) return fail(ACE_B200_EINVAL, "null p or out");
+  if (num_bins < 1 || num_bins > kMaxBins)
+    return fail(ACE_B200_EUNSUPPORTED, "num_bins=%d outside 1..%d", num_bins, kMaxBins);
+  BinTable t;
+  build_table(num_bins, soft != 0, t);
+  for (int64_t i = 0; i < n; ++i) {
+    float2 lohi;
+    out[i] = ace_locate(p[i], t.pair, num_bins, soft != 0, right != 0, lohi);
+  }
+  return ACE_B200_OK;
+}
+
+const char* ace_b200_last_error(void) { return g_err; }
+
+const char* ace_b200_version(void) { return "ace_b200 0.1.0 (sm_100a)"; }
+
+}  // extern "C"

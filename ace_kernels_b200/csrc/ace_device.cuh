@@ -1,0 +1,259 @@
+// Device-side building blocks shared by the histogram, epilogue and gradient
+// kernels of the mL1-ACE loss (sm_100a).
+//
+// Everything that decides which bin a voxel lands in lives here, so the forward
+// and the backward kernels run the same instruction sequence on the same logits
+// and a voxel always falls in the same bin in both passes (the reference states
+// the same contract for its Triton kernels: ace_kernels/kernels/act.py:1-7,
+// ace_kernels/kernels/hard_bwd.py:9-11).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "ace_types.h"
+
+namespace ace {
+
+// ---------------------------------------------------------------------------
+// Rounding-explicit fp32 arithmetic.
+//
+// The probability and bin-index path must not be contracted into FMAs by the
+// compiler (it would round differently in different kernels). On the device the
+// *_rn intrinsics are never fused; on the host (used by the CPU test hook for the
+// bin index) a volatile store forces one rounding per operation.
+// ---------------------------------------------------------------------------
+#ifdef __CUDA_ARCH__
+#define ACE_FMUL(a, b) __fmul_rn((a), (b))
+#define ACE_FADD(a, b) __fadd_rn((a), (b))
+#define ACE_FSUB(a, b) __fsub_rn((a), (b))
+#define ACE_FDIV(a, b) __fdiv_rn((a), (b))
+#else
+static inline float ace_host_round(float v) {
+  volatile float r = v;
+  return r;
+}
+#define ACE_FMUL(a, b) ace_host_round((a) * (b))
+#define ACE_FADD(a, b) ace_host_round((a) + (b))
+#define ACE_FSUB(a, b) ace_host_round((a) - (b))
+#define ACE_FDIV(a, b) ace_host_round((a) / (b))
+#endif
+
+// ---------------------------------------------------------------------------
+// Bin index.
+//
+// Hard binning: the bin of p is torch.bucketize(p, edges, right) = the number of
+// edges e_j with e_j < p (e_j <= p when `right`), edges = fp32
+// linspace(0, 1 + eps32, K + 1)[1:] (reference: ace_kernels/binning.py:47-51,
+// ace_reference/hardl1ace.py:70-90).
+//
+// Soft binning: the reference computes a half-bin index h against
+// linspace(0, 1 + eps32, 2K + 1)[1:] and derives the two neighbouring bins and the
+// distances to the replicated centre table (ace_kernels/common.py:43-61,
+// ace_reference/softl1ace.py:87-110). Since the 2K boundaries interleave centres
+// and edges, (h + 1) / 2 equals j = the number of centres counted for p, and the
+// reference's left/right bins are max(j - 1, 0) and min(j, K - 1), with the
+// distances taken to (centre j-1 or the -10000 sentinel) and (centre j or the
+// +10000 sentinel). So both binnings need one search over a sorted K-entry table.
+//
+// The search is O(1): a guess from p*K (hard) or p*K + 0.5 (soft), which is
+// within one of the answer because entry j is (j+1)/K (hard) or (j+0.5)/K (soft)
+// up to a few ulp, then a verified correction against the table itself. The
+// correction loop terminates after one or two passes; its bound only guards the
+// loop. The table is stored as pairs pair[i] = {t[i-1], t[i]} (sentinels at both
+// ends) so one 8-byte shared-memory load fetches both neighbours, which the soft
+// binning also needs as its interval ends.
+// ---------------------------------------------------------------------------
+__host__ __device__ __forceinline__ bool ace_counted(float p, float t, bool right) {
+  return right ? (t <= p) : (t < p);
+}
+
+__host__ __device__ __forceinline__ int ace_guess(float p, int n, bool soft) {
+  float g = ACE_FMUL(p, (float)n);
+  if (soft) g = ACE_FADD(g, 0.5f);
+  // fmaxf returns the non-NaN operand: NaN -> 0, as the reference's kernels.
+  g = fminf(fmaxf(g, 0.0f), (float)n);
+  return (int)g;  // g >= 0: truncation is floor
+}
+
+// Returns the count j in [0, n] and the pair {t[j-1], t[j]} (sentinels at the
+// ends). `pair` has n + 1 entries.
+__host__ __device__ __forceinline__ int ace_locate(float p, const float2* pair, int n,
+                                                   bool soft, bool right, float2& lohi) {
+  int i = ace_guess(p, n, soft);
+  float2 pr = pair[i];
+#pragma unroll 1
+  for (int it = 0; it <= n + 1; ++it) {
+    const bool lo_ok = (i == 0) || ace_counted(p, pr.x, right);
+    const bool hi_ok = (i == n) || !ace_counted(p, pr.y, right);
+    if (lo_ok && hi_ok) break;
+    i += lo_ok ? 1 : -1;
+    pr = pair[i];
+  }
+  lohi = pr;
+  return i;
+}
+
+#ifdef __CUDACC__
+
+// ---------------------------------------------------------------------------
+// Element loads. Logits are read natively (fp32 / bf16 / fp16) and widened to
+// fp32; all arithmetic after the load is fp32, as the reference's kernels
+// (ace_kernels/kernels/act.py:38-50).
+// ---------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ float ace_to_float(T v);
+template <>
+__device__ __forceinline__ float ace_to_float<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float ace_to_float<__nv_bfloat16>(__nv_bfloat16 v) {
+  return __bfloat162float(v);
+}
+template <>
+__device__ __forceinline__ float ace_to_float<__half>(__half v) { return __half2float(v); }
+
+template <typename T>
+__device__ __forceinline__ T ace_from_float(float v);
+template <>
+__device__ __forceinline__ float ace_from_float<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 ace_from_float<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+template <>
+__device__ __forceinline__ __half ace_from_float<__half>(float v) { return __float2half_rn(v); }
+
+// Read-only vector load of V consecutive elements (V * sizeof(T) in {2..16}
+// bytes), widened to fp32. The address must be aligned to V * sizeof(T).
+template <typename T, int V>
+struct VecIO {
+  static constexpr int BYTES = V * (int)sizeof(T);
+  static_assert(BYTES == 2 || BYTES == 4 || BYTES == 8 || BYTES == 16 || BYTES == 32,
+                "unsupported vector width");
+
+  __device__ __forceinline__ static void load(const T* __restrict__ p, float (&out)[V]) {
+    if constexpr (BYTES == 32) {
+      const uint4* q = reinterpret_cast<const uint4*>(p);
+      uint4 a = __ldg(q), b = __ldg(q + 1);
+      T tmp[V];
+      *reinterpret_cast<uint4*>(&tmp[0]) = a;
+      *reinterpret_cast<uint4*>(&tmp[V / 2]) = b;
+#pragma unroll
+      for (int i = 0; i < V; ++i) out[i] = ace_to_float<T>(tmp[i]);
+    } else if constexpr (BYTES == 16) {
+      uint4 a = __ldg(reinterpret_cast<const uint4*>(p));
+      T tmp[V];
+      *reinterpret_cast<uint4*>(&tmp[0]) = a;
+#pragma unroll
+      for (int i = 0; i < V; ++i) out[i] = ace_to_float<T>(tmp[i]);
+    } else if constexpr (BYTES == 8) {
+      uint2 a = __ldg(reinterpret_cast<const uint2*>(p));
+      T tmp[V];
+      *reinterpret_cast<uint2*>(&tmp[0]) = a;
+#pragma unroll
+      for (int i = 0; i < V; ++i) out[i] = ace_to_float<T>(tmp[i]);
+    } else if constexpr (BYTES == 4) {
+      unsigned a = __ldg(reinterpret_cast<const unsigned*>(p));
+      T tmp[V];
+      *reinterpret_cast<unsigned*>(&tmp[0]) = a;
+#pragma unroll
+      for (int i = 0; i < V; ++i) out[i] = ace_to_float<T>(tmp[i]);
+    } else {
+      out[0] = ace_to_float<T>(p[0]);
+    }
+  }
+
+  // Streaming store (the gradient is written once and not re-read).
+  __device__ __forceinline__ static void store(T* __restrict__ p, const float (&in)[V]) {
+    T tmp[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) tmp[i] = ace_from_float<T>(in[i]);
+    if constexpr (BYTES == 32) {
+      __stcs(reinterpret_cast<uint4*>(p), *reinterpret_cast<uint4*>(&tmp[0]));
+      __stcs(reinterpret_cast<uint4*>(p) + 1, *reinterpret_cast<uint4*>(&tmp[V / 2]));
+    } else if constexpr (BYTES == 16) {
+      __stcs(reinterpret_cast<uint4*>(p), *reinterpret_cast<uint4*>(&tmp[0]));
+    } else if constexpr (BYTES == 8) {
+      __stcs(reinterpret_cast<uint2*>(p), *reinterpret_cast<uint2*>(&tmp[0]));
+    } else if constexpr (BYTES == 4) {
+      __stcs(reinterpret_cast<unsigned*>(p), *reinterpret_cast<unsigned*>(&tmp[0]));
+    } else {
+      p[0] = tmp[0];
+    }
+  }
+};
+
+// V int64 class labels -> int32 (labels are class indices; values outside
+// [0, C) select no channel).
+template <int V>
+__device__ __forceinline__ void ace_load_labels(const int64_t* __restrict__ p, int (&out)[V]) {
+  if constexpr (V >= 2) {
+#pragma unroll
+    for (int i = 0; i < V; i += 2) {
+      longlong2 a = __ldg(reinterpret_cast<const longlong2*>(p + i));
+      out[i] = (int)max(min(a.x, (long long)0x7fffffff), (long long)-1);
+      out[i + 1] = (int)max(min(a.y, (long long)0x7fffffff), (long long)-1);
+    }
+  } else {
+    long long a = __ldg(reinterpret_cast<const long long*>(p));
+    out[0] = (int)max(min(a, (long long)0x7fffffff), (long long)-1);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Activation. Softmax over channels: m = max_c x_c, e_c = exp(x_c - m),
+// s = sum_c e_c (ascending c), p_c = e_c / s with IEEE round-to-nearest division,
+// as torch.softmax and the reference's fused kernels
+// (ace_kernels/kernels/act.py:38-62). exp is CUDA's expf (not the fast
+// approximation), compiled without fast-math. Sigmoid: 1 / (1 + exp(-x)).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float ace_sigmoid(float x) {
+  return ACE_FDIV(1.0f, ACE_FADD(1.0f, expf(-x)));
+}
+
+// In place: x[c] (c < C, C <= CM) logits -> exp(x - max); returns the sum.
+template <int CM>
+__device__ __forceinline__ float ace_softmax_exp(float (&x)[CM], int C) {
+  float m = x[0];
+#pragma unroll
+  for (int c = 1; c < CM; ++c)
+    if (c < C) m = fmaxf(m, x[c]);
+  float s = 0.0f;
+#pragma unroll
+  for (int c = 0; c < CM; ++c) {
+    if (c < C) {
+      const float e = expf(ACE_FSUB(x[c], m));
+      x[c] = e;
+      s = ACE_FADD(s, e);
+    }
+  }
+  return s;
+}
+
+// ---------------------------------------------------------------------------
+// Soft-binning weights (ace_kernels/common.py:43-61): distances to the interval
+// ends, span S = ld + rd, weights lw = rd / S (left bin), rw = ld / S (right
+// bin), IEEE division as the reference.
+// ---------------------------------------------------------------------------
+struct SoftW {
+  int l, r;
+  float lw, rw, span;
+};
+
+__device__ __forceinline__ SoftW ace_soft_weights(float p, int j, float2 lohi, int K) {
+  SoftW w;
+  const float ld = ACE_FSUB(p, lohi.x);
+  const float rd = ACE_FSUB(lohi.y, p);
+  w.span = ACE_FADD(ld, rd);
+  w.lw = ACE_FDIV(rd, w.span);
+  w.rw = ACE_FDIV(ld, w.span);
+  w.l = max(j - 1, 0);
+  w.r = min(j, K - 1);
+  return w;
+}
+
+#endif  // __CUDACC__
+
+}  // namespace ace

@@ -1,0 +1,93 @@
+// Parameter blocks passed by value to the mL1-ACE kernels (kernel parameter
+// space: no device allocation, no host->device copy, so every launch can be
+// captured in a CUDA graph).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/ace_b200.h"
+
+namespace ace {
+
+constexpr int kMaxBins = ACE_B200_MAX_BINS;        // num_bins limit of the kernels
+constexpr int kMaxClasses = ACE_B200_MAX_CLASSES;  // channels limit of the kernels
+constexpr int kThreads = 256;                      // threads per CTA, all kernels
+
+// Sorted search table with its neighbours paired (see ace_locate): hard binning
+// uses the K upper bin edges, soft binning the K bin centres; pair[i] =
+// {t[i-1], t[i]} with -10000 / +10000 at the two ends (the reference's soft
+// sentinels, ace_reference/softl1ace.py:99-105).
+struct BinTable {
+  int K;
+  float2 pair[kMaxBins + 1];
+};
+
+// Where one launch's voxels sit in the statistics: rows b_offset .. b_offset+B-1
+// of a [3, B_total, CL, K] buffer (batch sharding across ranks), and which slice
+// of the voxel axis (spatial sharding) is local.
+struct Grid {
+  int64_t N;           // voxels per (b, c) slice in this launch
+  int B;               // batches in this launch
+  int C;               // channels of x
+  int CL;              // loss channels: C - offset
+  int offset;          // 1 when the background channel is dropped
+  int chunks;          // CTAs per batch
+  int64_t tiles;       // tiles of kThreads * V voxels per batch
+  int64_t tiles_per_chunk;
+};
+
+struct EpiParams {
+  int B_total;         // rows of the statistics buffer = B_total * CL
+  int CL;
+  int K;
+  int soft;
+  float empty_weight;
+  int ignore_empty;
+  int reduction;       // ACE_B200_REDUCTION_*
+  double rows_global;  // divisor of the "mean" reduction
+  float class_w[kMaxClasses];
+  // outputs (device)
+  float* coef;         // [B_total, CL, K]
+  float* d;            // [B_total, CL, K]
+  float* jac;          // [B_total, CL]
+  float* f;            // [B_total, CL]
+  float* loss;         // [1]
+};
+
+struct FwdParams {
+  const void* x;       // [B, C, N] logits / probabilities (fp32, bf16, fp16)
+  const void* target;  // [B, N] int64 labels or [B, C, N] fp32 dense targets
+  Grid g;
+  int act;             // ACE_B200_ACT_*
+  bool right;
+  int soft;
+  int R;               // lane replicas of the shared-memory histogram (power of 2)
+  int b_offset;        // first statistics row of this launch
+  int B_total;
+  float* accum;        // workspace: [3, B_total, CL, K] running sums (self-cleaning)
+  unsigned* counter;   // workspace: finished-CTA counter (self-cleaning)
+  float* hist_out;     // [3, B_total, CL, K] statistics (W, P, G)
+  int do_epilogue;
+  BinTable tab;
+  EpiParams epi;
+};
+
+struct BwdParams {
+  const void* x;
+  const void* target;
+  void* dx;            // [B, C, N], dtype of x
+  Grid g;
+  int act;
+  bool right;
+  int soft;
+  int b_offset;        // first row of coef / d / jac used by this launch
+  const float* coef;   // [B_total, CL, K]
+  const float* d;      // [B_total, CL, K]
+  const float* jac;    // [B_total, CL]
+  const float* grad_out;  // scalar, or [B_total, CL] when grad_per_row
+  int grad_per_row;
+  BinTable tab;
+};
+
+}  // namespace ace

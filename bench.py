@@ -1,0 +1,434 @@
+#!/usr/bin/env python
+"""Benchmark of the mL1-ACE loss fwd+bwd on B200: voxels/s and % of HBM peak.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (N > 1)
+
+Workload: 2 x 3 x 128^3 fp32 logits, int64 labels, soft binning, K = 20 (the
+headline configuration), seeded synthetic inputs (``ace_kernels_b200.workloads``).
+With N GPUs every rank holds its own 2 x 3 x 128^3 shard of a 2N-sample batch
+(weak scaling); the per-bin statistics are all-reduced with NCCL before the
+epilogue and the local backward.
+
+One step = forward + backward of ``ace_loss(..., impl="b200_cuda")`` through
+``torch.autograd.grad``, inputs resident in HBM, replayed from a CUDA graph; L2 is
+flushed (512 MiB write) before every step, outside the step's events. ``value`` =
+voxels of all ranks / (max over ranks of the summed device time of K steps).
+``e2e`` = the same call per step with the inputs copied from pinned host memory
+and the loss read back, inside the timed region. ``roofline`` = the dominant
+kernel timed alone (algorithmic bytes / CUDA-event time). ``cpu_baseline`` = the
+reference's CPU path (the oracle restatement) on the host cores.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+WORKLOAD = "c2_soft_2x3x128c"
+FLUSH_BYTES = 512 << 20
+METRIC = "fwd+bwd voxels/s, 2x3x128^3 soft binning (K=20)"
+UNIT = "voxels/s"
+
+
+def parse() -> argparse.Namespace:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default=WORKLOAD)
+    ap.add_argument("--eager", action="store_true", help="no CUDA graph for the value leg")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0,
+                    help="bounded CPU sample of the cpu_baseline leg")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def env_rank() -> tuple[int, int, int]:
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
+            int(os.environ.get("LOCAL_RANK", 0)))
+
+
+# ---------------------------------------------------------------------------
+# reference arm: the reference's CPU path (oracle restatement), host cores
+# ---------------------------------------------------------------------------
+def cpu_reference(w, cfg, seconds: float, max_steps: int, slab: int = 8) -> dict:  # type: ignore[no-untyped-def]
+    """Times fwd+bwd of the CPU restatement of the reference on a bounded sample
+    of the workload: the first ``slab`` planes of the last spatial axis of every
+    sample (same distributions; the CPU path's cost is linear in voxels)."""
+    from ace_kernels_b200 import workloads as wl
+    from oracle import ace_oracle as oracle
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    x, y = wl.make(w)
+    x = x[..., :slab].contiguous().float()
+    y = y[..., :slab].contiguous()
+    voxels = x.shape[0] * x[0, 0].numel()
+    oracle.loss_and_grad(x, y, cfg)  # warm-up
+    times = []
+    t_end = time.perf_counter() + seconds
+    while len(times) < max_steps and (not times or time.perf_counter() < t_end):
+        t0 = time.perf_counter()
+        oracle.loss_and_grad(x, y, cfg)
+        times.append(time.perf_counter() - t0)
+    per_step = sum(times) / len(times)
+    return {
+        "value": voxels / per_step,
+        "unit": UNIT,
+        "cores": torch.get_num_threads(),
+        "kind": "port",
+        "sample": (f"{len(times)} fwd+bwd steps of the CPU restatement of the reference "
+                   f"(per-(b,c) bucketize/scatter + autograd, fp32) on {voxels} voxels "
+                   f"({list(x.shape)}: the first {slab} planes of the workload)"),
+        "steps": len(times),
+        "sec_per_step": per_step,
+    }
+
+
+def run_reference(args: argparse.Namespace) -> None:
+    rank, world, _ = env_rank()
+    if rank != 0:
+        return
+    from ace_kernels_b200 import workloads as wl
+
+    w = wl.WORKLOADS[args.workload]
+    for _ in range(max(0, min(args.warmup, 3))):
+        pass
+    res = cpu_reference(w, w.config, seconds=120.0, max_steps=max(1, args.steps))
+    line = {
+        "metric": METRIC, "value": res["value"], "unit": UNIT, "n_gpus": args.gpus,
+        "steps": res["steps"], "warmup": 1, "ms_per_step": res["sec_per_step"] * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded generator, BASELINE distributions)",
+        "config": {"workload": args.workload, "sample": res["sample"]},
+        "impl": "reference",
+        "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    """NVML samples of SM clock and clock-event reasons while running."""
+
+    def __init__(self, device_index: int, period_s: float = 0.005) -> None:
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self.period = period_s
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.handle = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+        except Exception:  # no NVML: clocks reported as unavailable
+            self.nvml = None
+
+    def _run(self) -> None:
+        n = self.nvml
+        while not self._stop.is_set():
+            try:
+                mhz = n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM)
+                reasons = n.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                self.samples.append((mhz, reasons))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self) -> ClockSampler:
+        if self.nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc: object) -> None:
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self) -> dict:
+        if self.nvml is None or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"],
+                    "samples": len(self.samples)}
+        n = self.nvml
+        names = {
+            "gpu_idle": getattr(n, "nvmlClocksEventReasonGpuIdle", 0x1),
+            "applications_clocks_setting": 0x2,
+            "sw_power_cap": 0x4,
+            "hw_slowdown": 0x8,
+            "sync_boost": 0x10,
+            "sw_thermal_slowdown": 0x20,
+            "hw_thermal_slowdown": 0x40,
+            "hw_power_brake_slowdown": 0x80,
+        }
+        mhz = sorted(s[0] for s in self.samples)
+        seen = 0
+        for _, r in self.samples:
+            seen |= r
+        reasons = [k for k, bit in names.items() if seen & bit and k != "gpu_idle"]
+        return {"sm_mhz": mhz[len(mhz) // 2], "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(self.samples)}
+
+
+def measured_peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+        except Exception:
+            pass
+    return 6650.0, "fallback 6.65 TB/s"
+
+
+def profiled_traffic(kernel: str, workload: str) -> float | None:
+    """Per-launch DRAM bytes of ``kernel`` from the committed ncu summary."""
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    try:
+        data = json.loads(p.read_text())
+        return float(data[workload][kernel]["dram_bytes_per_launch"])
+    except Exception:
+        return None
+
+
+def time_events(fn, flush: torch.Tensor, reps: int) -> float:  # type: ignore[no-untyped-def]
+    """Summed device milliseconds of ``reps`` calls, L2 flushed before each."""
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
+    for i in range(reps):
+        flush.zero_()
+        starts[i].record()
+        fn()
+        ends[i].record()
+    torch.cuda.synchronize()
+    return sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+
+
+def capture(fn, warmup: int = 3) -> torch.cuda.CUDAGraph:  # type: ignore[no-untyped-def]
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(warmup):
+            fn()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    # capture on the warm-up stream: per-stream state (the kernels' workspace) is
+    # then created outside the graph
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        fn()
+    torch.cuda.synchronize()
+    return g
+
+
+def run_ours(args: argparse.Namespace) -> None:
+    from ace_kernels_b200 import ace_loss
+    from ace_kernels_b200 import workloads as wl
+    from ace_kernels_b200.distributed import sharded_ace_loss
+    from ace_kernels_b200.loss import kernel_args, run_backward, run_forward
+
+    rank, world, local = env_rank()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    w = wl.WORKLOADS[args.workload]
+    cfg = w.config
+    # inputs resident in HBM: rank r holds samples 2r, 2r+1 of a 2N-sample batch
+    if world == 1:
+        x, y = wl.make(w, dev)
+    else:
+        x, y = wl.make_on_device(w, dev, seed_offset=rank)
+    b_local = w.batch
+    b_total = b_local * world
+    voxels_rank = w.voxels
+    voxels_all = voxels_rank * world
+    x.requires_grad_(True)
+
+    def step() -> torch.Tensor:
+        if world == 1:
+            loss = ace_loss(x, y, cfg, impl="b200_cuda")
+        else:
+            loss = sharded_ace_loss(x, y, cfg, b_offset=rank * b_local, b_total=b_total)
+        (g,) = torch.autograd.grad(loss, x)
+        return g
+
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    # NCCL inside a captured graph is left for later: N > 1 runs eagerly
+    graph = None if (args.eager or world > 1) else capture(step)
+    run = step if graph is None else graph.replay
+
+    # ---- value: K steps, device time, max over ranks
+    for _ in range(max(3, args.warmup)):
+        run()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    with sampler:
+        total_ms = time_events(run, flush, args.steps)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+        t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    ms_per_step = total_ms / args.steps
+    value = voxels_all / (ms_per_step * 1e-3)
+
+    # eager (no graph) for information
+    eager_ms = time_events(step, flush, min(args.steps, 100)) / min(args.steps, 100)
+    if world > 1:
+        t = torch.tensor([eager_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        eager_ms = float(t.item())
+
+    # ---- e2e through the public call with host buffers
+    xh = x.detach().cpu().pin_memory()
+    yh = y.cpu().pin_memory()
+    xd = torch.empty_like(x).requires_grad_(True)
+    yd = torch.empty_like(y)
+    loss_h = torch.empty((), dtype=torch.float32).pin_memory()
+
+    def e2e_step() -> None:
+        with torch.no_grad():
+            xd.copy_(xh, non_blocking=True)
+            yd.copy_(yh, non_blocking=True)
+        if world == 1:
+            loss = ace_loss(xd, yd, cfg, impl="b200_cuda")
+        else:
+            loss = sharded_ace_loss(xd, yd, cfg, b_offset=rank * b_local, b_total=b_total)
+        torch.autograd.grad(loss, xd)
+        loss_h.copy_(loss.detach(), non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    e2e_reps = min(args.steps, 50)
+    if world > 1:
+        dist.barrier()
+    e2e_ms = time_events(e2e_step, flush, e2e_reps) / e2e_reps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    h2d = xh.numel() * xh.element_size() + yh.numel() * yh.element_size()
+
+    # ---- roofline: each kernel timed alone (graph-replayed, L2 flushed)
+    kargs = kernel_args(x.detach(), y, cfg)
+    fwd_out = run_forward(kargs)
+    grad1 = torch.ones((), device=dev)
+    g_hist = capture(lambda: run_forward(kargs))
+    g_grad = capture(lambda: run_backward(kargs, fwd_out.coef, fwd_out.d, fwd_out.jac, grad1))
+    reps = min(args.steps, 200)
+    hist_ms = time_events(g_hist.replay, flush, reps) / reps
+    grad_ms = time_events(g_grad.replay, flush, reps) / reps
+    in_b = w.input_bytes()
+    tgt_b = w.target_bytes()
+    hist_bytes = in_b + tgt_b
+    grad_bytes = in_b + in_b + (tgt_b if cfg.binning == "soft" else 0)
+    peak, peak_src = measured_peaks()
+    kernels = {
+        "hist_fwd": {"ms": hist_ms, "bytes": hist_bytes, "gbs": hist_bytes / hist_ms / 1e6},
+        "grad_bwd": {"ms": grad_ms, "bytes": grad_bytes, "gbs": grad_bytes / grad_ms / 1e6},
+    }
+    dom = max(kernels, key=lambda k: kernels[k]["ms"])
+    achieved = kernels[dom]["gbs"]
+    step_bytes = w.ideal_bytes()
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": max(3, args.warmup),
+        "ms_per_step": ms_per_step,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded generator: labels 0.90/0.08/0.02, logits N(0,1.5^2)+2 on the true class)",
+        "config": {
+            "workload": args.workload,
+            "shape_per_rank": list(w.shape),
+            "global_batch": b_total,
+            "binning": cfg.binning,
+            "num_bins": cfg.num_bins,
+            "parallelism": f"batch-sharded dp{world}" if world > 1 else "single GPU",
+            "mode": "eager" if graph is None else "cuda_graph",
+            "l2": "flushed before every step (512 MiB write, outside the events)",
+        },
+        "hbm_frac_of_ideal_bytes": (step_bytes * world / (ms_per_step * 1e-3) / 1e9) / (peak * world),
+        "eager_ms_per_step": eager_ms,
+        "roofline": {
+            "bound": "hbm",
+            "kernel": dom,
+            "achieved": achieved,
+            "peak": peak,
+            "unit": "GB/s",
+            "frac": achieved / peak,
+            "traffic": profiled_traffic(dom, args.workload),
+            "peak_source": peak_src,
+            "algorithmic_bytes_per_launch": kernels[dom]["bytes"],
+        },
+        "kernels": kernels,
+        "gpu_launches": args.steps * (2 if world == 1 else 3),
+        "clocks": sampler.summary(),
+        "e2e": {
+            "value": voxels_all / (e2e_ms * 1e-3),
+            "unit": UNIT,
+            "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": 4,
+            "ms_per_step": e2e_ms,
+        },
+    }
+    if world > 1:
+        del graph, g_hist, g_grad
+        torch.cuda.synchronize()
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = {
+                k: v for k, v in cpu_reference(w, cfg, args.cpu_seconds, 50).items()
+                if k in ("value", "unit", "cores", "kind", "sample")
+            }
+        print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

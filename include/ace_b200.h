@@ -1,0 +1,205 @@
+/*
+ * ace_b200.h - C ABI of the B200 (sm_100a) mL1-ACE loss library (libace_b200.so).
+ *
+ * The mL1-ACE calibration loss (hard or soft binning) forward and backward for
+ * logits x[B, C, N] (N = product of the spatial sizes), in one fused read-once
+ * histogram pass, a tiny epilogue and one gradient pass that recomputes the
+ * activation instead of saving it.
+ *
+ * Conventions, for every entry point:
+ *   - all tensor pointers are DEVICE memory owned by the caller, contiguous,
+ *     row-major, in the layouts stated below; `stream` is a cudaStream_t (NULL =
+ *     the legacy default stream);
+ *   - every call is asynchronous on `stream`, allocates nothing and never
+ *     synchronises the host, so a sequence of calls can be captured in a CUDA
+ *     graph;
+ *   - the return value is ACE_B200_OK (0) or a negative ACE_B200_E* code;
+ *     ace_b200_last_error() then gives a message (thread-local);
+ *   - the library keeps no per-call state: calls are thread-safe, except that
+ *     two calls sharing one `workspace` must not run concurrently.
+ *
+ * Reference interfaces replaced (kapitan05/ace-kernels, paths inside that
+ * project): see each declaration.
+ */
+#ifndef ACE_B200_H
+#define ACE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define ACE_B200_OK 0
+#define ACE_B200_EINVAL (-1)       /* bad argument (shape, dtype, pointer) */
+#define ACE_B200_EUNSUPPORTED (-2) /* valid but outside the kernels' limits */
+#define ACE_B200_ECUDA (-3)        /* a CUDA runtime call failed */
+
+/* Limits of the kernels. */
+#define ACE_B200_MAX_BINS 128
+#define ACE_B200_MAX_CLASSES 64
+
+/* Logit dtypes. */
+#define ACE_B200_F32 0
+#define ACE_B200_BF16 1
+#define ACE_B200_F16 2
+
+/* Activations (ACEConfig.activation; softmax over one channel is the identity). */
+#define ACE_B200_ACT_NONE 0
+#define ACE_B200_ACT_SOFTMAX 1
+#define ACE_B200_ACT_SIGMOID 2
+
+/* Target forms. */
+#define ACE_B200_TARGET_LABELS 0 /* int64 [B, N] class index per voxel */
+#define ACE_B200_TARGET_DENSE 1  /* fp32 [B, C, N] (one-hot or soft targets) */
+
+/* Reductions (ACEConfig.reduction). */
+#define ACE_B200_REDUCTION_MEAN 0
+#define ACE_B200_REDUCTION_SUM 1
+#define ACE_B200_REDUCTION_NONE 2
+
+/*
+ * Loss options shared by the forward, statistics and backward calls; mirrors
+ * ACEConfig (ace_kernels/config.py:12-31).
+ *   num_bins      K, 1..ACE_B200_MAX_BINS
+ *   soft          0 hard binning, 1 soft binning
+ *   activation    ACE_B200_ACT_*
+ *   offset        1 drops channel 0 (include_background=False with C > 1), else 0
+ *   right         bucketize convention (ACEConfig.right)
+ *   empty_weight  soft binning: a bin with weight below this is empty
+ *   ignore_empty  mask classes absent from the target (ACEConfig.ignore_empty_classes)
+ *   reduction     ACE_B200_REDUCTION_*
+ *   class_weights HOST array of C - offset weights, or NULL (unweighted); read
+ *                 during the call only
+ */
+typedef struct ace_b200_options {
+  int32_t num_bins;
+  int32_t soft;
+  int32_t activation;
+  int32_t offset;
+  int32_t right;
+  float empty_weight;
+  int32_t ignore_empty;
+  int32_t reduction;
+  const float* class_weights;
+} ace_b200_options;
+
+/*
+ * Inputs of one launch.
+ *   x            [B, C, N] logits (probabilities with ACE_B200_ACT_NONE), dtype x_dtype
+ *   target       labels int64 [B, N] or dense fp32 [B, C, N], per target_kind
+ *   b_offset     first row of the statistics this launch covers (batch sharding:
+ *                rank r passes the index of its first sample), 0 otherwise
+ *   b_total      batches covered by the statistics buffer (>= b_offset + B)
+ *   rows_global  divisor of the "mean" reduction; 0 = b_total * (C - offset)
+ */
+typedef struct ace_b200_inputs {
+  const void* x;
+  int32_t x_dtype;
+  int64_t B;
+  int64_t C;
+  int64_t N;
+  const void* target;
+  int32_t target_kind;
+  int64_t b_offset;
+  int64_t b_total;
+  double rows_global;
+} ace_b200_inputs;
+
+/* Outputs of the epilogue, all fp32 device arrays (R = b_total * (C - offset)):
+ *   coef [R, K]  sign(d) / (K_nonempty * W), 0 for empty bins
+ *   d    [R, K]  mean p - mean target per bin, 0 for empty bins
+ *   jac  [R]     d loss / d f (mask, class weight, reduction)
+ *   f    [R]     per-class error after mask and weight (the "none" reduction)
+ *   loss [1]     mean or sum of f (written for every reduction)
+ */
+typedef struct ace_b200_epilogue_out {
+  float* coef;
+  float* d;
+  float* jac;
+  float* f;
+  float* loss;
+} ace_b200_epilogue_out;
+
+/* Bytes of the workspace for a statistics buffer of b_total * cl rows and
+ * num_bins bins. The workspace must be zero-filled before its first use; every
+ * call leaves it zero-filled again. */
+size_t ace_b200_workspace_bytes(int64_t b_total, int64_t cl, int32_t num_bins);
+
+/*
+ * Forward: fused activation + W/P/G statistics + epilogue, one launch.
+ * Replaces v6_triton._forward (ace_kernels/impls/v6_triton.py:43-65), i.e.
+ * hard_hist_fused / soft_hist_fused (ace_kernels/kernels/hard_hist.py:186-233,
+ * ace_kernels/kernels/soft_hist.py:229-271) followed by epilogue_triton
+ * (ace_kernels/kernels/epilogue.py:93-129); the statistics are
+ * binning.hard_stats / soft_stats (ace_kernels/binning.py:54-116).
+ *   hist  [3, b_total, C - offset, K] fp32 out: W (count / weight sum), P, G
+ */
+int ace_b200_forward(const ace_b200_inputs* in, const ace_b200_options* opt, float* hist,
+                     ace_b200_epilogue_out out, void* workspace, size_t workspace_bytes,
+                     void* stream);
+
+/*
+ * Statistics only (the first half of ace_b200_forward), for callers that reduce
+ * the statistics across ranks (NCCL all-reduce of `hist`) before the epilogue.
+ * Replaces hard_hist_fused / soft_hist_fused (ace_kernels/kernels/hard_hist.py:186-233,
+ * ace_kernels/kernels/soft_hist.py:229-271).
+ */
+int ace_b200_hist(const ace_b200_inputs* in, const ace_b200_options* opt, float* hist,
+                  void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Epilogue on [3, b_total, cl, K] statistics. Replaces epilogue_triton
+ * (ace_kernels/kernels/epilogue.py:23-129), i.e. v2_autograd.coefficients
+ * (ace_kernels/impls/v2_autograd.py:66-76) + common.reduce_classes
+ * (ace_kernels/common.py:184-207) + the reduction jacobian
+ * (ace_kernels/impls/v2_autograd.py:138-151).
+ */
+int ace_b200_epilogue(const float* hist, int64_t b_total, int64_t cl, double rows_global,
+                      const ace_b200_options* opt, ace_b200_epilogue_out out, void* stream);
+
+/*
+ * Backward: d loss / d x for this launch's x (dx has x's dtype and shape).
+ * coef, d, jac are the epilogue outputs (rows b_offset.. are used); grad_output
+ * is a device scalar, or [b_total, C - offset] when grad_per_row (reduction
+ * "none"). Replaces hard_input_grad_triton / soft_input_grad_triton
+ * (ace_kernels/kernels/hard_bwd.py:98-149, ace_kernels/kernels/soft_bwd.py:251-312)
+ * with the formulas of v2_autograd._df_dprobs / _activation_backward
+ * (ace_kernels/impls/v2_autograd.py:88-118).
+ */
+int ace_b200_backward(const ace_b200_inputs* in, const ace_b200_options* opt,
+                      const float* coef, const float* d, const float* jac,
+                      const float* grad_output, int32_t grad_per_row, void* dx, void* stream);
+
+/*
+ * Activated probabilities p[B, C, N] (fp32) exactly as the histogram and gradient
+ * kernels compute them: a test hook that lets the parity tests bin the kernel's
+ * own probabilities on the host. Replaces the activation half of
+ * common.prepare (ace_kernels/common.py:80-140).
+ */
+int ace_b200_probs(const ace_b200_inputs* in, int32_t activation, float* probs, void* stream);
+
+/* Host: the search table of the kernels (hard: the K upper edges, soft: the K
+ * centres), bit-identical to the reference's fp32 linspace tables
+ * (ace_kernels/common.py:17-25). `out` has num_bins floats. */
+int ace_b200_bin_table(int32_t num_bins, int32_t soft, float* out);
+
+/* Host: the kernels' bin index for n probabilities, computed by the same code
+ * the device runs (hard: the bin; soft: the count j of centres below p, so the
+ * bins are max(j-1, 0) and min(j, K-1)). A CPU test hook. */
+int ace_b200_bin_index_host(const float* p, int64_t n, int32_t num_bins, int32_t soft,
+                            int32_t right, int32_t* out);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* ace_b200_last_error(void);
+
+/* Library version string. */
+const char* ace_b200_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ACE_B200_H */
