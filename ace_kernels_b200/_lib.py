@@ -89,7 +89,8 @@ SIGNATURES: list[tuple[str, object, list[object]]] = [
     (
         "ace_b200_epilogue",
         c_int,
-        [c_void_p, c_int64, c_int64, c_double, POINTER(Options), EpilogueOut, c_void_p],
+        [c_void_p, c_int64, c_int64, c_double, POINTER(Options), EpilogueOut, c_void_p,
+         c_size_t, c_void_p],
     ),
     (
         "ace_b200_backward",

@@ -1,6 +1,7 @@
 // C ABI of libace_b200.so: argument checks, bin tables, launch configuration.
 // The kernels themselves are in ace_kernels.cuh.
 
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -62,9 +63,13 @@ void table_values(int K, bool soft, float* out) {
     out[j] = soft ? linspace_at(2 * K + 1, 2 * j + 1) : linspace_at(K + 1, j + 1);
 }
 
-void build_table(int K, bool soft, BinTable& t) {
+// With `right`, every entry becomes the next float below it (nextafterf toward
+// -inf), so that the kernels' test t < p means t <= p for the true entry.
+void build_table(int K, bool soft, bool right, BinTable& t) {
   float v[kMaxBins];
   table_values(K, soft, v);
+  if (right)
+    for (int j = 0; j < K; ++j) v[j] = nextafterf(v[j], -INFINITY);
   t.K = K;
   for (int i = 0; i <= K; ++i) {
     t.pair[i].x = i == 0 ? -10000.0f : v[i - 1];
@@ -88,8 +93,31 @@ int sm_count(int dev) {
 
 size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// Workspace layout: [accumulators: 3 * b_total * cl * K 32-bit words][histogram
+// counter][epilogue counter][epilogue partial sums: one per epilogue CTA], each
+// part 256-byte aligned. Counters and accumulators are zero between calls.
 size_t accum_bytes(int64_t b_total, int64_t cl, int K) {
   return round_up((size_t)3 * b_total * cl * K * sizeof(float), 256);
+}
+
+int64_t epi_ctas(int64_t rows) { return (rows + kEpiRowsPerCta - 1) / kEpiRowsPerCta; }
+
+struct Workspace {
+  float* accum;
+  unsigned* hist_counter;
+  unsigned* epi_counter;
+  float* epi_partial;
+};
+
+Workspace carve(void* ws, int64_t b_total, int64_t cl, int K) {
+  char* base = static_cast<char*>(ws);
+  const size_t a = accum_bytes(b_total, cl, K);
+  Workspace w;
+  w.accum = reinterpret_cast<float*>(base);
+  w.hist_counter = reinterpret_cast<unsigned*>(base + a);
+  w.epi_counter = reinterpret_cast<unsigned*>(base + a + 256);
+  w.epi_partial = reinterpret_cast<float*>(base + a + 512);
+  return w;
 }
 
 // Per-variant occupancy, cached (the query costs a few microseconds).
@@ -192,9 +220,10 @@ Variant choose_variant(const ace_b200_inputs* in, const ace_b200_options* opt, c
   const int vmax = 16 / es;
   int V;
   if (v.softmax) {
+    // exact channel count up to 4 (no per-channel guards), capacity buckets above
     const int C = (int)in->C;
-    v.CM = C <= 4 ? 4 : C <= 8 ? 8 : C <= 16 ? 16 : C <= 32 ? 32 : 64;
-    V = v.CM == 4 ? vmax : v.CM == 8 ? (vmax < 4 ? vmax : 4) : v.CM == 16 ? 2 : 1;
+    v.CM = C <= 4 ? C : C <= 8 ? 8 : C <= 16 ? 16 : C <= 32 ? 32 : 64;
+    V = v.CM <= 4 ? vmax : v.CM == 8 ? (vmax < 4 ? vmax : 4) : v.CM == 16 ? 2 : 1;
   } else {
     v.CM = 1;
     V = vmax;
@@ -273,15 +302,16 @@ int hist_impl(const ace_b200_inputs* in, const ace_b200_options* opt, float* his
   if (out) {
     rc = fill_epi(p.epi, in->b_total, CL, in->rows_global, opt, *out);
     if (rc) return rc;
-    p.do_epilogue = 1;
   }
   const Variant v = choose_variant(in, opt, nullptr);
-  // Lane replicas of the shared-memory table: as many as fit in 48 KB (32 =
+  // Lane replicas of the shared-memory table: as many as fit in ~56 KB (32 =
   // conflict-free), so several CTAs stay resident per SM.
-  const int entries = 3 * CL * K;
+  const bool soft = opt->soft != 0;
+  const int entries = CL * K * 3;
+  const size_t table_bytes = 2 * (kMaxBins + 1) * sizeof(float);
   int R = 32;
-  while (R > 1 && (size_t)entries * R * 4 > 48 * 1024) R >>= 1;
-  const int smem = (int)(2 * (kMaxBins + 1) * sizeof(float) + (size_t)entries * R * 4);
+  while (R > 1 && table_bytes + (size_t)entries * R * 4 > 44 * 1024) R >>= 1;
+  const int smem = (int)(table_bytes + (size_t)entries * R * 4);
   if (smem > 227 * 1024) return fail(ACE_B200_EUNSUPPORTED, "statistics do not fit in shared memory");
 
   int dev = 0;
@@ -292,16 +322,22 @@ int hist_impl(const ace_b200_inputs* in, const ace_b200_options* opt, float* his
   p.target = in->target;
   p.g = make_grid(in, CL, opt->offset, v.V, occ, dev);
   p.act = opt->activation;
-  p.right = opt->right != 0;
-  p.soft = opt->soft != 0;
+  p.soft = soft;
   p.R = R;
   p.b_offset = (int)in->b_offset;
   p.B_total = (int)in->b_total;
-  p.accum = static_cast<float*>(workspace);
-  p.counter = reinterpret_cast<unsigned*>(static_cast<char*>(workspace) +
-                                          accum_bytes(in->b_total, CL, K));
+  const Workspace w = carve(workspace, in->b_total, CL, K);
+  p.accum = w.accum;
+  p.counter = w.hist_counter;
   p.hist_out = hist;
-  build_table(K, p.soft, p.tab);
+  build_table(K, soft, opt->right != 0, p.tab);
+  // The last CTA runs the epilogue itself when all statistics fit in its (then
+  // free) shared-memory table and the rows are few; otherwise a multi-CTA
+  // epilogue kernel follows.
+  const int64_t stats = 3 * in->b_total * CL * K;
+  const int64_t rows = in->b_total * CL;
+  const bool fused = out && stats <= (int64_t)entries * R && rows <= 8 * kEpiRowsPerCta;
+  p.do_epilogue = fused ? 1 : 0;
 
   const dim3 grid((unsigned)p.g.chunks, (unsigned)p.g.B);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -309,18 +345,55 @@ int hist_impl(const ace_b200_inputs* in, const ace_b200_options* opt, float* his
   else if (in->x_dtype == ACE_B200_BF16) e = launch_hist<__nv_bfloat16>(p, v, grid, smem, s);
   else e = launch_hist<__half>(p, v, grid, smem, s);
   if (e != cudaSuccess) return cuda_fail(e, "histogram kernel launch");
+  if (out && !fused) {
+    e = launch_epilogue(hist, p.epi, w.epi_counter, w.epi_partial, s);
+    if (e != cudaSuccess) return cuda_fail(e, "epilogue kernel launch");
+  }
   return ACE_B200_OK;
 }
 
 }  // namespace
 
+// ---------------------------------------------------------------------------
+// Epilogue over many rows: CTA x takes rows [x * rpc, (x + 1) * rpc); each CTA
+// writes its sum of f to the workspace, and the last CTA to finish adds the
+// partial sums in CTA order into the loss (no waiting; the counter is left at
+// zero for the next call).
+// ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kThreads) epilogue_kernel(const float* __restrict__ hist,
+                                                            float* __restrict__ partial,
+                                                            unsigned* __restrict__ counter,
+                                                            int rows_per_cta,
                                                             const __grid_constant__ EpiParams E) {
-  epilogue_block(E, hist);
+  const int rows = E.B_total * E.CL;
+  const int r0 = blockIdx.x * rows_per_cta;
+  const int r1 = min(r0 + rows_per_cta, rows);
+  const float mine = epilogue_rows(E, hist, rows, 0, r0, r1);
+  if (gridDim.x == 1) {
+    write_loss_if0(E, mine);
+    return;
+  }
+  __shared__ bool s_last;
+  if (threadIdx.x == 0) {
+    partial[blockIdx.x] = mine;
+    __threadfence();
+    s_last = atomicAdd(counter, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!s_last || threadIdx.x != 0) return;
+  __threadfence();
+  float total = 0.0f;
+  for (unsigned i = 0; i < gridDim.x; ++i) total = ACE_FADD(total, __ldcg(partial + i));
+  *counter = 0u;
+  write_loss(E, total);
 }
 
-cudaError_t launch_epilogue(const float* hist, const EpiParams& e, cudaStream_t s) {
-  epilogue_kernel<<<1, kThreads, 0, s>>>(hist, e);
+cudaError_t launch_epilogue(const float* hist, const EpiParams& e, unsigned* counter,
+                            float* partial, cudaStream_t s) {
+  const int rows = e.B_total * e.CL;
+  const int ctas = (rows + kEpiRowsPerCta - 1) / kEpiRowsPerCta;
+  epilogue_kernel<<<ctas > 0 ? ctas : 1, kThreads, 0, s>>>(hist, partial, counter, kEpiRowsPerCta,
+                                                           e);
   return cudaGetLastError();
 }
 
@@ -331,8 +404,9 @@ using namespace ace;
 extern "C" {
 
 size_t ace_b200_workspace_bytes(int64_t b_total, int64_t cl, int32_t num_bins) {
-  if (b_total < 1 || cl < 1 || num_bins < 1) return 512;
-  return accum_bytes(b_total, cl, num_bins) + 256;
+  if (b_total < 1 || cl < 1 || num_bins < 1) return 1024;
+  return accum_bytes(b_total, cl, num_bins) + 512 +
+         round_up((size_t)epi_ctas(b_total * cl) * sizeof(float), 256);
 }
 
 int ace_b200_forward(const ace_b200_inputs* in, const ace_b200_options* opt, float* hist,
@@ -347,7 +421,8 @@ int ace_b200_hist(const ace_b200_inputs* in, const ace_b200_options* opt, float*
 }
 
 int ace_b200_epilogue(const float* hist, int64_t b_total, int64_t cl, double rows_global,
-                      const ace_b200_options* opt, ace_b200_epilogue_out out, void* stream) {
+                      const ace_b200_options* opt, ace_b200_epilogue_out out, void* workspace,
+                      size_t workspace_bytes, void* stream) {
   if (!hist || !opt) return fail(ACE_B200_EINVAL, "null hist or options");
   if (b_total < 1 || cl < 1 || cl > kMaxClasses)
     return fail(ACE_B200_EINVAL, "bad b_total=%lld cl=%lld", (long long)b_total, (long long)cl);
@@ -359,7 +434,13 @@ int ace_b200_epilogue(const float* hist, int64_t b_total, int64_t cl, double row
   memset(&e, 0, sizeof(e));
   int rc = fill_epi(e, b_total, (int)cl, rows_global, opt, out);
   if (rc) return rc;
-  cudaError_t err = launch_epilogue(hist, e, static_cast<cudaStream_t>(stream));
+  const size_t need = ace_b200_workspace_bytes(b_total, cl, opt->num_bins);
+  if (!workspace || workspace_bytes < need)
+    return fail(ACE_B200_EINVAL, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+  if (!aligned(workspace, 256)) return fail(ACE_B200_EINVAL, "workspace must be 256-byte aligned");
+  const Workspace w = carve(workspace, b_total, cl, opt->num_bins);
+  cudaError_t err = launch_epilogue(hist, e, w.epi_counter, w.epi_partial,
+                                    static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess) return cuda_fail(err, "epilogue kernel launch");
   return ACE_B200_OK;
 }
@@ -377,7 +458,9 @@ int ace_b200_backward(const ace_b200_inputs* in, const ace_b200_options* opt,
   BwdParams p;
   memset(&p, 0, sizeof(p));
   const Variant v = choose_variant(in, opt, dx);
-  const int smem = (int)(2 * (kMaxBins + 1) * sizeof(float) + (size_t)CL * K * 8 + CL * 4);
+  const bool soft = opt->soft != 0;
+  const int smem = (int)((size_t)(soft ? 16 : 4) * CL * (K + 1) + 8 + (size_t)(K + 1) * 8);
+  if (smem > 227 * 1024) return fail(ACE_B200_EUNSUPPORTED, "gradient tables do not fit");
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
@@ -387,15 +470,14 @@ int ace_b200_backward(const ace_b200_inputs* in, const ace_b200_options* opt,
   p.dx = dx;
   p.g = make_grid(in, CL, opt->offset, v.V, occ, dev);
   p.act = opt->activation;
-  p.right = opt->right != 0;
-  p.soft = opt->soft != 0;
+  p.soft = soft;
   p.b_offset = (int)in->b_offset;
   p.coef = coef;
   p.d = d;
   p.jac = jac;
   p.grad_out = grad_output;
   p.grad_per_row = grad_per_row != 0;
-  build_table(K, p.soft, p.tab);
+  build_table(K, soft, opt->right != 0, p.tab);
   const dim3 grid((unsigned)p.g.chunks, (unsigned)p.g.B);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (in->x_dtype == ACE_B200_F32) e = launch_grad<float>(p, v, grid, smem, s);
@@ -438,10 +520,10 @@ int ace_b200_bin_index_host(const float* p, int64_t n, int32_t num_bins, int32_t
   if (num_bins < 1 || num_bins > kMaxBins)
     return fail(ACE_B200_EUNSUPPORTED, "num_bins=%d outside 1..%d", num_bins, kMaxBins);
   BinTable t;
-  build_table(num_bins, soft != 0, t);
+  build_table(num_bins, soft != 0, right != 0, t);
   for (int64_t i = 0; i < n; ++i) {
     float2 lohi;
-    out[i] = ace_locate(p[i], t.pair, num_bins, soft != 0, right != 0, lohi);
+    out[i] = ace_locate(p[i], t.pair, num_bins, (float)num_bins, soft != 0, lohi);
   }
   return ACE_B200_OK;
 }

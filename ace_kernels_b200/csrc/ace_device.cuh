@@ -12,6 +12,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
+#include <string.h>
 
 #include "ace_types.h"
 
@@ -66,31 +67,66 @@ static inline float ace_host_round(float v) {
 // ends) so one 8-byte shared-memory load fetches both neighbours, which the soft
 // binning also needs as its interval ends.
 // ---------------------------------------------------------------------------
-__host__ __device__ __forceinline__ bool ace_counted(float p, float t, bool right) {
-  return right ? (t <= p) : (t < p);
+// Guess of the count: round(p*n - 0.5) (hard) or round(p*n) (soft), via the
+// 1.5 * 2^23 bias (adding it leaves the nearest integer in the low mantissa
+// bits), so the guess costs FMA-pipe work only and no float<->int conversion.
+// Any guess within one of the answer is corrected by the search below; NaN and
+// out-of-range values are clamped to the table and corrected the same way.
+__host__ __device__ __forceinline__ int ace_guess(float p, float nf, int n, bool soft) {
+  const float g = soft ? ACE_FMUL(p, nf) : ACE_FSUB(ACE_FMUL(p, nf), 0.5f);
+  const float b = ACE_FADD(g, 12582912.0f);
+  int i;
+#ifdef __CUDA_ARCH__
+  i = __float_as_int(b) - 0x4B400000;
+#else
+  memcpy(&i, &b, sizeof(i));
+  i -= 0x4B400000;
+#endif
+  return i < 0 ? 0 : (i > n ? n : i);
 }
 
-__host__ __device__ __forceinline__ int ace_guess(float p, int n, bool soft) {
-  float g = ACE_FMUL(p, (float)n);
-  if (soft) g = ACE_FADD(g, 0.5f);
-  // fmaxf returns the non-NaN operand: NaN -> 0, as the reference's kernels.
-  g = fminf(fmaxf(g, 0.0f), (float)n);
-  return (int)g;  // g >= 0: truncation is floor
+// Is i the count for p, given pr = pair[i]? (The table is `right`-adjusted, so
+// "entry counted" is always t < p.)
+__host__ __device__ __forceinline__ bool ace_is_count(float p, int i, int n, float2 pr) {
+  return (i == 0 || pr.x < p) && (i == n || !(pr.y < p));
 }
 
-// Returns the count j in [0, n] and the pair {t[j-1], t[j]} (sentinels at the
-// ends). `pair` has n + 1 entries.
-__host__ __device__ __forceinline__ int ace_locate(float p, const float2* pair, int n,
-                                                   bool soft, bool right, float2& lohi) {
-  int i = ace_guess(p, n, soft);
+// Rare path: walk from a guess that failed ace_is_count to the count (one or two
+// steps for probabilities; the bound only guards against NaN / invalid input).
+// Returns the count and its pair by value, so the caller's registers never need
+// a memory address (a reference argument would force them to local memory).
+struct Located {
+  int i;
+  float2 pr;
+};
+
+static __host__ __device__ __noinline__ Located ace_fix_count(float p, int i, int n,
+                                                              const float2* pair) {
   float2 pr = pair[i];
 #pragma unroll 1
   for (int it = 0; it <= n + 1; ++it) {
-    const bool lo_ok = (i == 0) || ace_counted(p, pr.x, right);
-    const bool hi_ok = (i == n) || !ace_counted(p, pr.y, right);
-    if (lo_ok && hi_ok) break;
+    const bool lo_ok = (i == 0) || pr.x < p;
+    if (lo_ok && (i == n || !(pr.y < p))) break;
     i += lo_ok ? 1 : -1;
+    i = i < 0 ? 0 : (i > n ? n : i);
     pr = pair[i];
+  }
+  Located r;
+  r.i = i;
+  r.pr = pr;
+  return r;
+}
+
+// The count j in [0, n] of table entries counted for p, and pair[j] =
+// {t[j-1], t[j]}. `pair` has n + 1 entries; nf = (float)n.
+__host__ __device__ __forceinline__ int ace_locate(float p, const float2* pair, int n, float nf,
+                                                   bool soft, float2& lohi) {
+  int i = ace_guess(p, nf, n, soft);
+  float2 pr = pair[i];
+  if (!ace_is_count(p, i, n, pr)) {
+    const Located r = ace_fix_count(p, i, n, pair);
+    i = r.i;
+    pr = r.pr;
   }
   lohi = pr;
   return i;
@@ -204,13 +240,40 @@ __device__ __forceinline__ void ace_load_labels(const int64_t* __restrict__ p, i
 
 // ---------------------------------------------------------------------------
 // Activation. Softmax over channels: m = max_c x_c, e_c = exp(x_c - m),
-// s = sum_c e_c (ascending c), p_c = e_c / s with IEEE round-to-nearest division,
-// as torch.softmax and the reference's fused kernels
-// (ace_kernels/kernels/act.py:38-62). exp is CUDA's expf (not the fast
-// approximation), compiled without fast-math. Sigmoid: 1 / (1 + exp(-x)).
+// s = sum_c e_c (ascending c), p_c = e_c / s, as torch.softmax and the
+// reference's fused kernels (ace_kernels/kernels/act.py:38-62). exp is CUDA's
+// expf (not the fast approximation), compiled without fast-math. Sigmoid:
+// 1 / (1 + exp(-x)) with IEEE division.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float ace_sigmoid(float x) {
   return ACE_FDIV(1.0f, ACE_FADD(1.0f, expf(-x)));
+}
+
+// Approximate reciprocal (the hardware's, max 1 ulp error). s > 0 finite.
+__device__ __forceinline__ float ace_rcp_approx(float s) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(s));
+  return y;
+}
+
+// Reciprocal of s in [1, 2^64) to about half an ulp: the hardware approximation
+// refined by one Newton-Raphson step, y += y (1 - s y).
+__device__ __forceinline__ float ace_rcp_refined(float s) {
+  const float y = ace_rcp_approx(s);
+  return __fmaf_rn(__fmaf_rn(-s, y, 1.0f), y, y);
+}
+
+// a / s from y ~ 1/s with Markstein's correction step (P. Markstein,
+// "Computation of elementary functions on the IBM RISC System/6000 processor",
+// IBM J. Res. Dev. 34(1), 1990): q0 = a y, the remainder r = a - s q0 is exact
+// with an FMA, and q = q0 + r y carries an error of about |q - q0| |1 - s y|
+// before its single rounding, so q is the correctly rounded quotient unless a/s
+// lies within ~2^-23 ulp of a rounding midpoint. One reciprocal per voxel then
+// serves all C channels of the softmax.
+__device__ __forceinline__ float ace_div_corrected(float a, float s, float y) {
+  const float q0 = __fmul_rn(a, y);
+  const float r = __fmaf_rn(-s, q0, a);
+  return __fmaf_rn(r, y, q0);
 }
 
 // In place: x[c] (c < C, C <= CM) logits -> exp(x - max); returns the sum.
@@ -232,23 +295,39 @@ __device__ __forceinline__ float ace_softmax_exp(float (&x)[CM], int C) {
   return s;
 }
 
+// In place: x[c] (c < C) logits -> softmax probabilities, the one routine every
+// kernel uses (so a voxel's probabilities, hence its bins, are bit-identical in
+// the forward and the backward). The division by the sum uses one refined
+// reciprocal per voxel and the corrected quotient per channel (see
+// ace_div_corrected): s is in [1, C], so no special cases arise.
+template <int CM>
+__device__ __forceinline__ void ace_softmax(float (&x)[CM], int C) {
+  const float s = ace_softmax_exp<CM>(x, C);
+  const float y = ace_rcp_refined(s);
+#pragma unroll
+  for (int c = 0; c < CM; ++c)
+    if (c < C) x[c] = ace_div_corrected(x[c], s, y);
+}
+
 // ---------------------------------------------------------------------------
 // Soft-binning weights (ace_kernels/common.py:43-61): distances to the interval
 // ends, span S = ld + rd, weights lw = rd / S (left bin), rw = ld / S (right
-// bin), IEEE division as the reference.
+// bin). The weights only feed floating-point sums compared with a tolerance, so
+// they take one approximate reciprocal of the span (shared with the backward's
+// 1/S) instead of the reference's two IEEE divisions: lw, rw within 2 ulp.
 // ---------------------------------------------------------------------------
 struct SoftW {
   int l, r;
-  float lw, rw, span;
+  float lw, rw, inv_span;
 };
 
 __device__ __forceinline__ SoftW ace_soft_weights(float p, int j, float2 lohi, int K) {
   SoftW w;
   const float ld = ACE_FSUB(p, lohi.x);
   const float rd = ACE_FSUB(lohi.y, p);
-  w.span = ACE_FADD(ld, rd);
-  w.lw = ACE_FDIV(rd, w.span);
-  w.rw = ACE_FDIV(ld, w.span);
+  w.inv_span = ace_rcp_approx(ACE_FADD(ld, rd));
+  w.lw = ACE_FMUL(rd, w.inv_span);
+  w.rw = ACE_FMUL(ld, w.inv_span);
   w.l = max(j - 1, 0);
   w.r = min(j, K - 1);
   return w;

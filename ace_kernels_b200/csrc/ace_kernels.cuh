@@ -35,12 +35,16 @@ int hist_occupancy(const Variant& v, int smem);
 template <typename T>
 int grad_occupancy(const Variant& v, int smem);
 
-cudaError_t launch_epilogue(const float* hist, const EpiParams& e, cudaStream_t s);
+// Multi-CTA epilogue on [3, B_total, CL, K] statistics; `ws` holds a counter
+// (left at zero) and one partial sum per CTA.
+cudaError_t launch_epilogue(const float* hist, const EpiParams& e, unsigned* counter,
+                            float* partial, cudaStream_t s);
+constexpr int kEpiRowsPerCta = 32;
 
 #ifdef __CUDACC__
 
 // ---------------------------------------------------------------------------
-// Epilogue (one CTA): per row (b, c) and bin k, from W, P, G:
+// Epilogue: per row (b, c) and bin k, from W, P, G:
 //   nonempty = W != 0 (hard) / W >= empty_weight (soft)
 //   d = P / W - G / W (two IEEE divisions, then subtract; 0 if empty)
 //   f = sum_nonempty |d| / K_ne (NaN if K_ne = 0)
@@ -50,45 +54,73 @@ cudaError_t launch_epilogue(const float* hist, const EpiParams& e, cudaStream_t 
 // Same formulas and operation order as v2_autograd.coefficients
 // (ace_kernels/impls/v2_autograd.py:66-76), common.reduce_classes
 // (ace_kernels/common.py:184-207) and the fused Triton epilogue
-// (ace_kernels/kernels/epilogue.py:23-82). The loss is summed in a fixed order
-// (per thread ascending rows, then a fixed tree), so it is deterministic.
+// (ace_kernels/kernels/epilogue.py:23-82). One warp per row, lanes over bins
+// (K <= 128: up to four bins a lane), butterfly reductions; the loss is summed in
+// a fixed order (rows ascending per warp, warps ascending, then CTAs ascending),
+// so it is deterministic.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void epilogue_block(const EpiParams& E, const float* __restrict__ hist) {
-  __shared__ float red[kThreads];
-  const int tid = threadIdx.x;
-  const int R = E.B_total * E.CL;
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = ACE_FADD(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ int warp_sum_i(int v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Rows [r0, r1) of the epilogue; `st` points at [3, R_total, K] statistics
+// (shared or global memory) and row r of it is statistics row r - st_row0.
+// Returns (on every thread) this CTA's sum of f over its rows, in fixed order.
+__device__ __forceinline__ float epilogue_rows(const EpiParams& E, const float* st, int st_rows,
+                                               int st_row0, int r0, int r1) {
+  __shared__ float wsum[kThreads / 32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int K = E.K;
-  const int64_t RK = (int64_t)R * K;
-  const float* W = hist;
-  const float* P = hist + RK;
-  const float* G = hist + 2 * RK;
+  const int64_t RK = (int64_t)st_rows * K;
   const float nan = __int_as_float(0x7fc00000);
   const float rows = (float)E.rows_global;
   float mine = 0.0f;
-  for (int r = tid; r < R; r += kThreads) {
-    const int64_t base = (int64_t)r * K;
+  for (int r = r0 + warp; r < r1; r += kThreads / 32) {
+    const int64_t base = (int64_t)(r - st_row0) * K;
+    float dk[4], wk[4];
+    bool ne[4];
     int kne = 0;
     float err = 0.0f, gsum = 0.0f;
-    for (int k = 0; k < K; ++k) {
-      const float w = W[base + k];
-      const float g = G[base + k];
-      gsum = ACE_FADD(gsum, g);
-      const bool ne = E.soft ? (w >= E.empty_weight) : (w != 0.0f);
-      float dk = 0.0f;
-      if (ne) {
-        dk = ACE_FSUB(ACE_FDIV(P[base + k], w), ACE_FDIV(g, w));
-        err = ACE_FADD(err, fabsf(dk));
-        ++kne;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int k = lane + 32 * q;
+      dk[q] = 0.0f;
+      wk[q] = 1.0f;
+      ne[q] = false;
+      if (k < K) {
+        const float w = st[base + k];
+        const float pp = st[RK + base + k];
+        const float g = st[2 * RK + base + k];
+        gsum = ACE_FADD(gsum, g);
+        ne[q] = E.soft ? (w >= E.empty_weight) : (w != 0.0f);
+        if (ne[q]) {
+          wk[q] = w;
+          dk[q] = ACE_FSUB(ACE_FDIV(pp, w), ACE_FDIV(g, w));
+          err = ACE_FADD(err, fabsf(dk[q]));
+          ++kne;
+        }
       }
-      E.d[base + k] = dk;
     }
+    kne = warp_sum_i(kne);
+    err = warp_sum(err);
+    gsum = warp_sum(gsum);
     const float kf = (float)kne;
-    for (int k = 0; k < K; ++k) {
-      const float w = W[base + k];
-      const bool ne = E.soft ? (w >= E.empty_weight) : (w != 0.0f);
-      const float dk = E.d[base + k];
-      const float sg = dk > 0.0f ? 1.0f : (dk < 0.0f ? -1.0f : 0.0f);
-      E.coef[base + k] = ne ? ACE_FDIV(sg, ACE_FMUL(kf, w)) : 0.0f;
+    const int64_t out = (int64_t)r * K;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int k = lane + 32 * q;
+      if (k < K) {
+        const float sg = dk[q] > 0.0f ? 1.0f : (dk[q] < 0.0f ? -1.0f : 0.0f);
+        E.d[out + k] = dk[q];
+        E.coef[out + k] = ne[q] ? ACE_FDIV(sg, ACE_FMUL(kf, wk[q])) : 0.0f;
+      }
     }
     float f = kne > 0 ? ACE_FDIV(err, kf) : nan;
     const float present = gsum > 0.0f ? 1.0f : 0.0f;
@@ -100,88 +132,88 @@ __device__ __forceinline__ void epilogue_block(const EpiParams& E, const float* 
     }
     f = ACE_FMUL(f, wc);
     if (E.reduction == ACE_B200_REDUCTION_MEAN) scale = ACE_FDIV(scale, rows);
-    E.f[r] = f;
-    E.jac[r] = scale;
+    if (lane == 0) {
+      E.f[r] = f;
+      E.jac[r] = scale;
+    }
     mine = ACE_FADD(mine, f);
   }
-  red[tid] = mine;
+  if (lane == 0) wsum[warp] = mine;
   __syncthreads();
+  float total = 0.0f;
 #pragma unroll
-  for (int s = kThreads / 2; s > 0; s >>= 1) {
-    if (tid < s) red[tid] = ACE_FADD(red[tid], red[tid + s]);
-    __syncthreads();
-  }
-  if (tid == 0) {
-    float total = red[0];
-    if (E.reduction == ACE_B200_REDUCTION_MEAN) total = ACE_FDIV(total, rows);
-    E.loss[0] = total;
-  }
+  for (int w = 0; w < kThreads / 32; ++w) total = ACE_FADD(total, wsum[w]);
+  __syncthreads();
+  return total;
+}
+
+__device__ __forceinline__ void write_loss(const EpiParams& E, float total) {
+  if (E.reduction == ACE_B200_REDUCTION_MEAN) total = ACE_FDIV(total, (float)E.rows_global);
+  E.loss[0] = total;
+}
+
+__device__ __forceinline__ void write_loss_if0(const EpiParams& E, float total) {
+  if (threadIdx.x == 0) write_loss(E, total);
 }
 
 // ---------------------------------------------------------------------------
-// Shared-memory histogram with lane-replicated columns.
+// Shared-memory statistics table, lane-replicated.
 //
-// Layout [stat][row][bin][R]: entry (stat, row, bin) has R consecutive words and
-// lane l updates word l % R, so with R = 32 the 32 lanes of a warp always hit 32
-// different banks whatever their bins are (no intra-warp conflicts, no
-// serialisation on hot bins such as p < 0.05). Warps of a CTA share the table and
-// update it with shared-memory atomics; hard-binning counts (W, and G with label
-// targets) are exact u32 counts, the rest fp32.
+// Layout [row][bin][stat][R] 32-bit words, stat 0 W, 1 P, 2 G; lane l updates
+// replica l % R, so with R = 32 every warp-wide update is conflict-free whatever
+// the bins are (no serialisation on hot bins such as p < 0.05). Hard-binning
+// counts (W, and G with label targets) are exact u32 counts; every other
+// statistic is an fp32 sum (shared-memory atomic adds, fire-and-forget).
+// Soft binning adds, per value, its two interpolation weights lw, rw (and lw p,
+// rw p, lw y, rw y) to the two neighbouring bins, exactly as the reference's
+// scatters (ace_kernels/binning.py:74-116, ace_reference/softl1ace.py:112-140).
 // ---------------------------------------------------------------------------
-struct SmemHist {
-  float* h;
-  int SS;     // stride between the three statistics: CL * K * R
-  int RS;     // stride between rows: K * R
-  int shift;  // log2(R)
-  int col;    // this lane's column
+__device__ __forceinline__ void sadd_f(float* h, int a, float v) { atomicAdd(h + a, v); }
+__device__ __forceinline__ void sadd_u(float* h, int a, unsigned v) {
+  atomicAdd(reinterpret_cast<unsigned*>(h) + a, v);
+}
 
-  __device__ __forceinline__ int at(int row, int bin) const {
-    return row * RS + (bin << shift) + col;
-  }
-  __device__ __forceinline__ void add_u(int a, unsigned v) const {
-    atomicAdd(reinterpret_cast<unsigned*>(h + a), v);
-  }
-  __device__ __forceinline__ void add_f(int a, float v) const { atomicAdd(h + a, v); }
-};
-
-// One probability of loss row `row` into the histogram. `y` is the target value
-// (labels: 1 for the true class, else 0).
+// Is statistic `stat` an exact count?
 template <bool SOFT, bool LABELS>
-__device__ __forceinline__ void accumulate(const SmemHist& H, const float2* __restrict__ pairs,
-                                           int K, bool right, int row, float p, float y) {
-  float2 lohi;
-  const int j = ace_locate(p, pairs, K, SOFT, right, lohi);
-  if constexpr (!SOFT) {
-    if (j < K) {  // p above the last edge (only for invalid p > 1 + eps) is dropped
-      const int a = H.at(row, j);
-      H.add_u(a, 1u);
-      H.add_f(a + H.SS, p);
-      if constexpr (LABELS) {
-        if (y != 0.0f) H.add_u(a + 2 * H.SS, 1u);
+__device__ __forceinline__ constexpr bool stat_is_count(int stat) {
+  return !SOFT && (stat == 0 || (stat == 2 && LABELS));
+}
+
+// Folds this CTA's table into the workspace and clears it: one warp per
+// (row, bin), lane l reading replica l of the three statistics (conflict-free),
+// a warp reduction in a fixed order, then one global atomic per non-zero sum.
+// Called by all threads between barriers.
+template <bool SOFT, bool LABELS>
+__device__ __forceinline__ void fold_table(float* hist, int CL, int K, int R, float* accum,
+                                           int64_t stat_stride, int64_t row0) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int e = warp; e < CL * K; e += kThreads / 32) {
+    float* base = hist + (int64_t)e * 3 * R;
+    const int64_t gi = row0 * K + e;
+#pragma unroll
+    for (int s = 0; s < 3; ++s) {
+      if (stat_is_count<SOFT, LABELS>(s)) {
+        unsigned v = 0;
+        for (int l = lane; l < R; l += 32) v += __float_as_uint(base[s * R + l]);
+        v = __reduce_add_sync(0xffffffffu, v);
+        if (lane == 0 && v) atomicAdd(reinterpret_cast<unsigned*>(accum) + s * stat_stride + gi, v);
       } else {
-        if (y != 0.0f) H.add_f(a + 2 * H.SS, y);
+        float v = 0.0f;
+        for (int l = lane; l < R; l += 32) v += base[s * R + l];
+        v = warp_sum(v);
+        if (lane == 0 && v != 0.0f) atomicAdd(accum + s * stat_stride + gi, v);
       }
     }
-  } else {
-    const SoftW w = ace_soft_weights(p, j, lohi, K);
-    const int al = H.at(row, w.l);
-    const int ar = H.at(row, w.r);
-    H.add_f(al, w.lw);
-    H.add_f(ar, w.rw);
-    H.add_f(al + H.SS, ACE_FMUL(w.lw, p));
-    H.add_f(ar + H.SS, ACE_FMUL(w.rw, p));
-    if constexpr (LABELS) {
-      if (y != 0.0f) {
-        H.add_f(al + 2 * H.SS, w.lw);
-        H.add_f(ar + 2 * H.SS, w.rw);
-      }
-    } else {
-      if (y != 0.0f) {
-        H.add_f(al + 2 * H.SS, ACE_FMUL(w.lw, y));
-        H.add_f(ar + 2 * H.SS, ACE_FMUL(w.rw, y));
-      }
-    }
+    for (int l = lane; l < 3 * R; l += 32) base[l] = 0.0f;
   }
+}
+
+// Channel count of a kernel instance: exact for softmax instances with CM <= 4
+// (the loops then have no per-channel guard), else the runtime value (CM is a
+// capacity, or 1 for the pointwise activations that loop over channels).
+template <int CM, bool SOFTMAX>
+__device__ __forceinline__ int channels(int runtime_c) {
+  return (SOFTMAX && CM <= 4) ? CM : runtime_c;
 }
 
 // ---------------------------------------------------------------------------
@@ -191,37 +223,89 @@ __device__ __forceinline__ void accumulate(const SmemHist& H, const float2* __re
 // a tile is kThreads * V voxels and thread t owns V consecutive voxels of it, read
 // with 16-byte (V * sizeof(T)) coalesced loads per channel (the channel stride is
 // N). The logits of all C channels of a voxel are in registers, so the softmax
-// needs no second read. At the end each CTA folds its table into the workspace
-// accumulators with global atomics (one per non-zero statistic), and the last CTA
-// to finish (counter in the workspace, no waiting) writes the statistics, resets
-// the workspace, and runs the epilogue.
+// needs no second read. Per voxel the bins of all loss channels are located first
+// (one shared-memory load each, straight-line), a rare fix-up pass corrects
+// guesses off by one, then the table updates are issued; the true class's target
+// updates are issued once per voxel. At the end the CTA folds its table into the
+// workspace, and the last CTA to finish (counter in the workspace, no waiting)
+// writes W, P, G, resets the workspace and runs the epilogue.
 // ---------------------------------------------------------------------------
 template <typename T, int V, int CM, bool SOFTMAX, bool SOFT, bool LABELS>
 __global__ void __launch_bounds__(kThreads) hist_kernel(const __grid_constant__ FwdParams P) {
   extern __shared__ __align__(16) float smem[];
   const int tid = threadIdx.x;
   const int b = blockIdx.y;
-  const int C = P.g.C, CL = P.g.CL, off = P.g.offset, K = P.tab.K;
+  const int C = channels<CM, SOFTMAX>(P.g.C), CL = P.g.CL, off = P.g.offset, K = P.tab.K;
   const int64_t N = P.g.N;
   const int R = P.R;
+  const float Kf = (float)K;
 
   float2* pairs = reinterpret_cast<float2*>(smem);
   float* hist = smem + 2 * (kMaxBins + 1);
-  const int entries = 3 * CL * K;
+  const int table_words = CL * K * 3 * R;
   for (int i = tid; i <= K; i += kThreads) pairs[i] = P.tab.pair[i];
-  for (int i = tid; i < entries * R; i += kThreads) hist[i] = 0.0f;
+  for (int i = tid; i < table_words; i += kThreads) hist[i] = 0.0f;
   __syncthreads();
 
-  SmemHist H;
-  H.h = hist;
-  H.shift = 31 - __clz(R);
-  H.RS = K * R;
-  H.SS = CL * H.RS;
-  H.col = tid & (R - 1);
+  const int col = tid & (R - 1);
+  const int bin_stride = 3 * R, row_stride = K * bin_stride;
+  const int R2 = 2 * R;
+  const int64_t stat_stride = (int64_t)P.B_total * CL * K;
+  const int64_t row0 = (int64_t)(P.b_offset + b) * CL;
 
   const T* xb = static_cast<const T*>(P.x) + (int64_t)b * C * N;
   const int64_t* lb = LABELS ? static_cast<const int64_t*>(P.target) + (int64_t)b * N : nullptr;
   const float* yb = LABELS ? nullptr : static_cast<const float*>(P.target) + (int64_t)b * C * N;
+
+  // One loss-channel value into the table. Returns what the true-class target
+  // update of this value needs: the table index of its (left) bin, and for soft
+  // binning the right bin's index offset and the two weights.
+  struct TrueUpd {
+    int a, ar;
+    float lw, rw;
+  };
+  auto update = [&](int row, float p, int j, float2 lohi, float y) -> TrueUpd {
+    TrueUpd t;
+    if constexpr (!SOFT) {
+      t.a = -1;
+      if (j < K) {  // p above the last edge (only for invalid p > 1 + eps) is dropped
+        const int a = row * row_stride + j * bin_stride + col;
+        sadd_u(hist, a, 1u);
+        sadd_f(hist, a + R, p);
+        if constexpr (!LABELS) {
+          if (y != 0.0f) sadd_f(hist, a + R2, y);
+        }
+        t.a = a;
+      }
+    } else {
+      const SoftW w = ace_soft_weights(p, j, lohi, K);
+      const int base = row * row_stride + col;
+      const int al = base + w.l * bin_stride, ar = base + w.r * bin_stride;
+      sadd_f(hist, al, w.lw);
+      sadd_f(hist, ar, w.rw);
+      sadd_f(hist, al + R, ACE_FMUL(w.lw, p));
+      sadd_f(hist, ar + R, ACE_FMUL(w.rw, p));
+      if constexpr (!LABELS) {
+        if (y != 0.0f) {
+          sadd_f(hist, al + R2, ACE_FMUL(w.lw, y));
+          sadd_f(hist, ar + R2, ACE_FMUL(w.rw, y));
+        }
+      }
+      t.a = al;
+      t.ar = ar;
+      t.lw = w.lw;
+      t.rw = w.rw;
+    }
+    return t;
+  };
+  auto true_update = [&](const TrueUpd& t) {
+    if constexpr (!SOFT) {
+      if (t.a >= 0) sadd_u(hist, t.a + R2, 1u);
+    } else {
+      sadd_f(hist, t.a + R2, t.lw);
+      sadd_f(hist, t.ar + R2, t.rw);
+    }
+  };
 
   const int64_t t0 = (int64_t)blockIdx.x * P.g.tiles_per_chunk;
   const int64_t t1 = min(t0 + P.g.tiles_per_chunk, P.g.tiles);
@@ -239,23 +323,51 @@ __global__ void __launch_bounds__(kThreads) hist_kernel(const __grid_constant__ 
       if constexpr (!LABELS) {
 #pragma unroll
         for (int c = 0; c < CM; ++c)
-          if (c >= off && c < C) VecIO<float, V>::load(yb + (int64_t)c * N + v0, yv[c]);
+          if ((c > 0 || off == 0) && c < C) VecIO<float, V>::load(yb + (int64_t)c * N + v0, yv[c]);
       }
 #pragma unroll
       for (int i = 0; i < V; ++i) {
-        float e[CM];
+        float p[CM];
 #pragma unroll
-        for (int c = 0; c < CM; ++c) e[c] = xv[c][i];
-        const float s = ace_softmax_exp<CM>(e, C);
+        for (int c = 0; c < CM; ++c) p[c] = xv[c][i];
+        ace_softmax<CM>(p, C);
+        int j[CM];
+        float2 lh[CM];
+        bool ok = true;
 #pragma unroll
         for (int c = 0; c < CM; ++c) {
-          if (c >= off && c < C) {
-            const float p = ACE_FDIV(e[c], s);
-            float y;
-            if constexpr (LABELS) y = (lab[i] == c) ? 1.0f : 0.0f;
-            else y = yv[c][i];
-            accumulate<SOFT, LABELS>(H, pairs, K, P.right, c - off, p, y);
+          if ((c > 0 || off == 0) && c < C) {
+            j[c] = ace_guess(p[c], Kf, K, SOFT);
+            lh[c] = pairs[j[c]];
+            ok &= ace_is_count(p[c], j[c], K, lh[c]);
           }
+        }
+        if (!ok) {
+#pragma unroll
+          for (int c = 0; c < CM; ++c)
+            if ((c > 0 || off == 0) && c < C && !ace_is_count(p[c], j[c], K, lh[c])) {
+              const Located r = ace_fix_count(p[c], j[c], K, pairs);
+              j[c] = r.i;
+              lh[c] = r.pr;
+            }
+        }
+        TrueUpd tu;
+        tu.a = -1;
+        tu.ar = 0;
+        tu.lw = tu.rw = 0.0f;
+#pragma unroll
+        for (int c = 0; c < CM; ++c) {
+          if ((c > 0 || off == 0) && c < C) {
+            float y = 0.0f;
+            if constexpr (!LABELS) y = yv[c][i];
+            const TrueUpd u = update(c - off, p[c], j[c], lh[c], y);
+            if constexpr (LABELS) {
+              if (lab[i] == c) tu = u;
+            }
+          }
+        }
+        if constexpr (LABELS) {
+          if (lab[i] >= off && lab[i] < C) true_update(tu);
         }
       }
     } else {
@@ -268,36 +380,20 @@ __global__ void __launch_bounds__(kThreads) hist_kernel(const __grid_constant__ 
 #pragma unroll
         for (int i = 0; i < V; ++i) {
           const float p = P.act == ACE_B200_ACT_SIGMOID ? ace_sigmoid(xv[i]) : xv[i];
-          float y;
-          if constexpr (LABELS) y = (lab[i] == c) ? 1.0f : 0.0f;
-          else y = yv[i];
-          accumulate<SOFT, LABELS>(H, pairs, K, P.right, c - off, p, y);
+          float2 lh;
+          const int j = ace_locate(p, pairs, K, Kf, SOFT, lh);
+          float y = 0.0f;
+          if constexpr (!LABELS) y = yv[i];
+          const TrueUpd u = update(c - off, p, j, lh, y);
+          if constexpr (LABELS) {
+            if (lab[i] == c) true_update(u);
+          }
         }
       }
     }
   }
   __syncthreads();
-
-  // Fold the lane columns (rotated start: conflict-free for R = 32) and add the
-  // CTA's statistics to the workspace accumulators.
-  const int64_t rowK = (int64_t)(P.b_offset + b) * CL * K;
-  const int64_t statS = (int64_t)P.B_total * CL * K;
-  for (int e = tid; e < entries; e += kThreads) {
-    const int stat = e / (CL * K);
-    const int rk = e - stat * CL * K;
-    const bool is_u = !SOFT && (stat == 0 || (stat == 2 && LABELS));
-    const float* src = hist + (int64_t)e * R;
-    const int64_t gi = stat * statS + rowK + rk;
-    if (is_u) {
-      unsigned s = 0;
-      for (int i = 0; i < R; ++i) s += __float_as_uint(src[(i + tid) & (R - 1)]);
-      if (s) atomicAdd(reinterpret_cast<unsigned*>(P.accum) + gi, s);
-    } else {
-      float s = 0.0f;
-      for (int i = 0; i < R; ++i) s += src[(i + tid) & (R - 1)];
-      if (s != 0.0f) atomicAdd(P.accum + gi, s);
-    }
-  }
+  fold_table<SOFT, LABELS>(hist, CL, K, R, P.accum, stat_stride, row0);
   __threadfence();
   __syncthreads();
   __shared__ bool s_last;
@@ -309,20 +405,25 @@ __global__ void __launch_bounds__(kThreads) hist_kernel(const __grid_constant__ 
   if (!s_last) return;
   __threadfence();
 
-  // Last CTA: statistics out, workspace back to zero, epilogue.
-  const int64_t total = 3 * statS;
+  // Last CTA: statistics out, workspace back to zero and, when all rows fit in
+  // the (now free) shared-memory table, the epilogue from shared memory.
+  const int rows = P.B_total * CL;
+  const int64_t total = 3 * stat_stride;
+  const bool stage = P.do_epilogue && total <= (int64_t)table_words;
   unsigned* acc_u = reinterpret_cast<unsigned*>(P.accum);
   for (int64_t i = tid; i < total; i += kThreads) {
-    const int stat = (int)(i / statS);
+    const int stat = (int)(i / stat_stride);
     const bool is_u = !SOFT && (stat == 0 || (stat == 2 && LABELS));
     const unsigned raw = __ldcg(acc_u + i);
-    P.hist_out[i] = is_u ? (float)raw : __uint_as_float(raw);
+    const float v = is_u ? (float)raw : __uint_as_float(raw);
+    P.hist_out[i] = v;
+    if (stage) hist[i] = v;
     __stcg(acc_u + i, 0u);
   }
   if (tid == 0) *P.counter = 0u;
-  if (P.do_epilogue) {
+  if (stage) {
     __syncthreads();
-    epilogue_block(P.epi, P.hist_out);
+    write_loss_if0(P.epi, epilogue_rows(P.epi, hist, rows, 0, 0, rows));
   }
 }
 
@@ -332,27 +433,25 @@ __global__ void __launch_bounds__(kThreads) hist_kernel(const __grid_constant__ 
 //   hard: gp_c = g_bc * coef[b, c, bin(p_c)]
 //   soft: gp_c = g_bc * (coef_l (lw - (p - y - d_l) / S) + coef_r (rw + (p - y - d_r) / S))
 //   softmax: dx_c = p_c (gp_c - sum_c' p_c' gp_c'); sigmoid: gp p (1 - p); none: gp
-// with gp = 0 on a dropped background channel. The activation is recomputed with
-// the forward's code (same bins); coef / d of this CTA's batch row sit in shared
-// memory as {coef, d} pairs. Hard binning reads no targets.
+// with gp = 0 on a dropped background channel. The activation and the bins are
+// recomputed with the forward's code (same bins). Per CTA, the rows of its batch
+// sit in shared memory with g folded in: hard, cg[row][k] = g coef (0 past the
+// last bin); soft, one record per interval j, {g coef_l, d_l, g coef_r, d_r} of
+// its two bins, read with one 16-byte load. Hard binning reads no targets.
 // ---------------------------------------------------------------------------
 template <bool SOFT>
-__device__ __forceinline__ float grad_p(const float2* __restrict__ pairs,
-                                        const float2* __restrict__ cd, int K, bool right,
-                                        int row, float g, float p, float y) {
-  float2 lohi;
-  const int j = ace_locate(p, pairs, K, SOFT, right, lohi);
-  const float2* cr = cd + row * K;
+__device__ __forceinline__ float grad_p(const float* __restrict__ tab, int row, int K, int j,
+                                        float2 lohi, float p, float y) {
   if constexpr (!SOFT) {
-    return j < K ? g * cr[j].x : 0.0f;
+    return tab[row * (K + 1) + j];
   } else {
-    const SoftW w = ace_soft_weights(p, j, lohi, K);
-    const float inv = ACE_FDIV(1.0f, w.span);
+    const float4 rec = reinterpret_cast<const float4*>(tab)[row * (K + 1) + j];
+    const float ld = ACE_FSUB(p, lohi.x);
+    const float rd = ACE_FSUB(lohi.y, p);
+    const float inv = ace_rcp_approx(ACE_FADD(ld, rd));
+    const float lw = rd * inv, rw = ld * inv;
     const float resid = p - y;
-    const float2 L = cr[w.l], Rr = cr[w.r];
-    const float left = L.x * (w.lw - inv * (resid - L.y));
-    const float right_ = Rr.x * (w.rw + inv * (resid - Rr.y));
-    return (left + right_) * g;
+    return rec.x * (lw - inv * (resid - rec.y)) + rec.z * (rw + inv * (resid - rec.w));
   }
 }
 
@@ -361,18 +460,27 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const __grid_constant__ 
   extern __shared__ __align__(16) float smem[];
   const int tid = threadIdx.x;
   const int b = blockIdx.y;
-  const int C = P.g.C, CL = P.g.CL, off = P.g.offset, K = P.tab.K;
+  const int C = channels<CM, SOFTMAX>(P.g.C), CL = P.g.CL, off = P.g.offset, K = P.tab.K;
   const int64_t N = P.g.N;
+  const float Kf = (float)K;
 
-  float2* pairs = reinterpret_cast<float2*>(smem);
-  float2* cd = pairs + (kMaxBins + 1);
-  float* gs = reinterpret_cast<float*>(cd + CL * K);
+  float* tab = smem;  // [CL][K+1] floats (hard) or float4 (soft)
+  float2* pairs = reinterpret_cast<float2*>(smem + (SOFT ? 4 : 1) * CL * (K + 1) +
+                                            ((SOFT ? 0 : (CL * (K + 1)) & 1)));
   const int64_t row0 = (int64_t)(P.b_offset + b) * CL;
   for (int i = tid; i <= K; i += kThreads) pairs[i] = P.tab.pair[i];
-  for (int i = tid; i < CL * K; i += kThreads)
-    cd[i] = make_float2(P.coef[row0 * K + i], P.d[row0 * K + i]);
-  for (int i = tid; i < CL; i += kThreads)
-    gs[i] = P.jac[row0 + i] * (P.grad_per_row ? P.grad_out[row0 + i] : P.grad_out[0]);
+  for (int e = tid; e < CL * (K + 1); e += kThreads) {
+    const int row = e / (K + 1), j = e - row * (K + 1);
+    const float g = P.jac[row0 + row] * (P.grad_per_row ? P.grad_out[row0 + row] : P.grad_out[0]);
+    const float* cf = P.coef + (row0 + row) * K;
+    const float* dd = P.d + (row0 + row) * K;
+    if constexpr (!SOFT) {
+      tab[e] = j < K ? g * cf[j] : 0.0f;
+    } else {
+      const int l = max(j - 1, 0), r = min(j, K - 1);
+      reinterpret_cast<float4*>(tab)[e] = make_float4(g * cf[l], dd[l], g * cf[r], dd[r]);
+    }
+  }
   __syncthreads();
 
   const T* xb = static_cast<const T*>(P.x) + (int64_t)b * C * N;
@@ -396,34 +504,52 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const __grid_constant__ 
       if constexpr (SOFT && !LABELS) {
 #pragma unroll
         for (int c = 0; c < CM; ++c)
-          if (c >= off && c < C) VecIO<float, V>::load(yb + (int64_t)c * N + v0, yv[c]);
+          if ((c > 0 || off == 0) && c < C) VecIO<float, V>::load(yb + (int64_t)c * N + v0, yv[c]);
       }
 #pragma unroll
       for (int i = 0; i < V; ++i) {
-        float e[CM];
+        float p[CM];
 #pragma unroll
-        for (int c = 0; c < CM; ++c) e[c] = xv[c][i];
-        const float s = ace_softmax_exp<CM>(e, C);
+        for (int c = 0; c < CM; ++c) p[c] = xv[c][i];
+        ace_softmax<CM>(p, C);
+        int j[CM];
+        float2 lh[CM];
+        bool ok = true;
+#pragma unroll
+        for (int c = 0; c < CM; ++c) {
+          if ((c > 0 || off == 0) && c < C) {
+            j[c] = ace_guess(p[c], Kf, K, SOFT);
+            lh[c] = pairs[j[c]];
+            ok &= ace_is_count(p[c], j[c], K, lh[c]);
+          }
+        }
+        if (!ok) {
+#pragma unroll
+          for (int c = 0; c < CM; ++c)
+            if ((c > 0 || off == 0) && c < C && !ace_is_count(p[c], j[c], K, lh[c])) {
+              const Located r = ace_fix_count(p[c], j[c], K, pairs);
+              j[c] = r.i;
+              lh[c] = r.pr;
+            }
+        }
         float gp[CM];
         float dot = 0.0f;
 #pragma unroll
         for (int c = 0; c < CM; ++c) {
           gp[c] = 0.0f;
           if (c < C) {
-            const float p = ACE_FDIV(e[c], s);
-            e[c] = p;
-            if (c >= off) {
+            if (c > 0 || off == 0) {
               float y = 0.0f;
               if constexpr (SOFT && LABELS) y = (lab[i] == c) ? 1.0f : 0.0f;
               if constexpr (SOFT && !LABELS) y = yv[c][i];
-              gp[c] = grad_p<SOFT>(pairs, cd, K, P.right, c - off, gs[c - off], p, y);
+              gp[c] = grad_p<SOFT>(tab, c - off, K, j[c], lh[c], p[c], y);
             }
-            dot += p * gp[c];
+            dot += p[c] * gp[c];
           }
         }
 #pragma unroll
         for (int c = 0; c < CM; ++c)
-          if (c < C) xv[c][i] = e[c] * (gp[c] - dot);
+          if (c < C) xv[c][i] = p[c] * (gp[c] - dot);
       }
 #pragma unroll
       for (int c = 0; c < CM; ++c)
@@ -440,7 +566,6 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const __grid_constant__ 
         VecIO<T, V>::load(xb + (int64_t)c * N + v0, xv);
         float yv[V];
         if constexpr (SOFT && !LABELS) VecIO<float, V>::load(yb + (int64_t)c * N + v0, yv);
-        const float g = gs[c - off];
 #pragma unroll
         for (int i = 0; i < V; ++i) {
           const bool sig = P.act == ACE_B200_ACT_SIGMOID;
@@ -448,7 +573,9 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const __grid_constant__ 
           float y = 0.0f;
           if constexpr (SOFT && LABELS) y = (lab[i] == c) ? 1.0f : 0.0f;
           if constexpr (SOFT && !LABELS) y = yv[i];
-          const float gp = grad_p<SOFT>(pairs, cd, K, P.right, c - off, g, p, y);
+          float2 lh;
+          const int j = ace_locate(p, pairs, K, Kf, SOFT, lh);
+          const float gp = grad_p<SOFT>(tab, c - off, K, j, lh, p, y);
           xv[i] = sig ? gp * p * (1.0f - p) : gp;
         }
         VecIO<T, V>::store(db + (int64_t)c * N + v0, xv);
@@ -475,10 +602,10 @@ __global__ void __launch_bounds__(kThreads) probs_kernel(const T* __restrict__ x
       float e[kMaxClasses];
 #pragma unroll
       for (int c = 0; c < kMaxClasses; ++c) e[c] = c < C ? ace_to_float<T>(xp[(int64_t)c * N]) : 0.0f;
-      const float s = ace_softmax_exp<kMaxClasses>(e, C);
+      ace_softmax<kMaxClasses>(e, C);
 #pragma unroll
       for (int c = 0; c < kMaxClasses; ++c)
-        if (c < C) op[(int64_t)c * N] = ACE_FDIV(e[c], s);
+        if (c < C) op[(int64_t)c * N] = e[c];
     } else {
       for (int c = 0; c < C; ++c) {
         const float v = ace_to_float<T>(xp[(int64_t)c * N]);
@@ -491,21 +618,38 @@ __global__ void __launch_bounds__(kThreads) probs_kernel(const T* __restrict__ x
 // ---------------------------------------------------------------------------
 // Host-side dispatch from a runtime Variant to a template instance.
 // ---------------------------------------------------------------------------
+// The launchers live in an unnamed namespace: their "already opted in" state is
+// then private to the translation unit that launches the kernels (a static local
+// of an exported template would be merged with any other loaded copy of the
+// library and could skip the opt-in).
+namespace {
+
+// Opt a kernel in to `smem` dynamic shared-memory bytes when static + dynamic
+// would exceed the default 48 KB (once per kernel and size).
+template <typename K>
+cudaError_t set_smem(K* kernel, int smem, int& configured) {
+  if (smem <= 40 * 1024 || smem <= configured) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e == cudaSuccess) configured = smem;
+  return e;
+}
+
 template <typename T, int V, int CM, bool SM, bool SOFT, bool LAB>
 struct HistLauncher {
+  static int& configured() {
+    static int bytes = 0;  // dynamic shared memory this instance is opted in to
+    return bytes;
+  }
   static cudaError_t run(const FwdParams& p, dim3 grid, int smem, cudaStream_t s) {
     auto k = hist_kernel<T, V, CM, SM, SOFT, LAB>;
-    if (smem > 48 * 1024) {
-      cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      if (e != cudaSuccess) return e;
-    }
+    cudaError_t e = set_smem(k, smem, configured());
+    if (e != cudaSuccess) return e;
     k<<<grid, kThreads, smem, s>>>(p);
     return cudaGetLastError();
   }
   static int occupancy(int smem) {
     auto k = hist_kernel<T, V, CM, SM, SOFT, LAB>;
-    if (smem > 48 * 1024)
-      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    set_smem(k, smem, configured());
     int n = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, kThreads, smem) != cudaSuccess) n = 1;
     return n > 0 ? n : 1;
@@ -514,24 +658,27 @@ struct HistLauncher {
 
 template <typename T, int V, int CM, bool SM, bool SOFT, bool LAB>
 struct GradLauncher {
+  static int& configured() {
+    static int bytes = 0;
+    return bytes;
+  }
   static cudaError_t run(const BwdParams& p, dim3 grid, int smem, cudaStream_t s) {
     auto k = grad_kernel<T, V, CM, SM, SOFT, LAB>;
-    if (smem > 48 * 1024) {
-      cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      if (e != cudaSuccess) return e;
-    }
+    cudaError_t e = set_smem(k, smem, configured());
+    if (e != cudaSuccess) return e;
     k<<<grid, kThreads, smem, s>>>(p);
     return cudaGetLastError();
   }
   static int occupancy(int smem) {
     auto k = grad_kernel<T, V, CM, SM, SOFT, LAB>;
-    if (smem > 48 * 1024)
-      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    set_smem(k, smem, configured());
     int n = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, kThreads, smem) != cudaSuccess) n = 1;
     return n > 0 ? n : 1;
   }
 };
+
+}  // namespace
 
 // Calls L<T, V, CM, softmax, soft, labels>::F(args...) for the runtime variant.
 // The (V, CM) pairs instantiated here are the ones the host chooses
@@ -541,6 +688,10 @@ struct GradLauncher {
     constexpr int VM = 16 / (int)sizeof(T);                                               \
     constexpr int V8 = (VM < 4 ? VM : 4);                                                 \
     if (v.softmax) {                                                                      \
+      if (v.CM == 2 && v.V == VM) return L<T, VM, 2, true, S_, L_>::F(__VA_ARGS__);      \
+      if (v.CM == 2 && v.V == 1) return L<T, 1, 2, true, S_, L_>::F(__VA_ARGS__);        \
+      if (v.CM == 3 && v.V == VM) return L<T, VM, 3, true, S_, L_>::F(__VA_ARGS__);      \
+      if (v.CM == 3 && v.V == 1) return L<T, 1, 3, true, S_, L_>::F(__VA_ARGS__);        \
       if (v.CM == 4 && v.V == VM) return L<T, VM, 4, true, S_, L_>::F(__VA_ARGS__);      \
       if (v.CM == 4 && v.V == 1) return L<T, 1, 4, true, S_, L_>::F(__VA_ARGS__);        \
       if (v.CM == 8 && v.V == V8) return L<T, V8, 8, true, S_, L_>::F(__VA_ARGS__);      \

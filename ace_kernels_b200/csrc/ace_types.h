@@ -6,7 +6,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include "../../include/ace_b200.h"
+#include "ace_b200.h"  // include/ (on the include path of the build)
 
 namespace ace {
 
@@ -17,11 +17,14 @@ constexpr int kThreads = 256;                      // threads per CTA, all kerne
 // Sorted search table with its neighbours paired (see ace_locate): hard binning
 // uses the K upper bin edges, soft binning the K bin centres; pair[i] =
 // {t[i-1], t[i]} with -10000 / +10000 at the two ends (the reference's soft
-// sentinels, ace_reference/softl1ace.py:99-105).
+// sentinels, ace_reference/softl1ace.py:99-105). With `right` (count t <= p) each
+// entry is replaced by the next float below it, so the kernels always test
+// t < p: for finite floats, t <= p exactly when prev(t) < p.
 struct BinTable {
   int K;
   float2 pair[kMaxBins + 1];
 };
+
 
 // Where one launch's voxels sit in the statistics: rows b_offset .. b_offset+B-1
 // of a [3, B_total, CL, K] buffer (batch sharding across ranks), and which slice
@@ -60,12 +63,11 @@ struct FwdParams {
   const void* target;  // [B, N] int64 labels or [B, C, N] fp32 dense targets
   Grid g;
   int act;             // ACE_B200_ACT_*
-  bool right;
   int soft;
   int R;               // lane replicas of the shared-memory histogram (power of 2)
   int b_offset;        // first statistics row of this launch
   int B_total;
-  float* accum;        // workspace: [3, B_total, CL, K] running sums (self-cleaning)
+  float* accum;        // workspace: [3, B_total, CL, K] sums (u32 for exact counts)
   unsigned* counter;   // workspace: finished-CTA counter (self-cleaning)
   float* hist_out;     // [3, B_total, CL, K] statistics (W, P, G)
   int do_epilogue;
@@ -79,7 +81,6 @@ struct BwdParams {
   void* dx;            // [B, C, N], dtype of x
   Grid g;
   int act;
-  bool right;
   int soft;
   int b_offset;        // first row of coef / d / jac used by this launch
   const float* coef;   // [B_total, CL, K]

@@ -56,9 +56,11 @@ def _cuda_hist(args: KernelArgs, out: ForwardOut) -> None:
 def _cuda_epilogue(args: KernelArgs, out: ForwardOut) -> None:
     lib = _lib.load()
     s = args.setup
+    b_total = int(args.inputs.b_total)
+    ws = workspace(args.x.device, lib.ace_b200_workspace_bytes(b_total, s.cl, s.num_bins))
     rc = lib.ace_b200_epilogue(
-        out.hist.data_ptr(), int(args.inputs.b_total), s.cl, float(args.inputs.rows_global),
-        ctypes.byref(s.options), epilogue_struct(out),
+        out.hist.data_ptr(), b_total, s.cl, float(args.inputs.rows_global),
+        ctypes.byref(s.options), epilogue_struct(out), ws.data_ptr(), ws.numel(),
         torch.cuda.current_stream(args.x.device).cuda_stream,
     )
     _lib.check(rc, "ace_b200_epilogue")

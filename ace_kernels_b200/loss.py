@@ -255,8 +255,18 @@ class ForwardOut:
     loss: torch.Tensor  # [] fp32
 
 
-def alloc_outputs(device: torch.device, b_total: int, cl: int, k: int) -> ForwardOut:
-    # one allocation for all outputs (fewer allocator calls per step)
+def alloc_outputs(device: torch.device, b_total: int, cl: int, k: int,
+                  separate: bool = False) -> ForwardOut:
+    """Output buffers of the forward: one allocation for all (fewer allocator
+    calls per step), or separate tensors when they are returned from a custom op
+    (whose outputs may not alias one another)."""
+    if separate:
+        f32 = {"dtype": torch.float32, "device": device}
+        return ForwardOut(
+            torch.empty(3, b_total, cl, k, **f32), torch.empty(b_total, cl, k, **f32),
+            torch.empty(b_total, cl, k, **f32), torch.empty(b_total, cl, **f32),
+            torch.empty(b_total, cl, **f32), torch.empty((), **f32),
+        )
     rk = b_total * cl * k
     r = b_total * cl
     buf = torch.empty(3 * rk + 2 * rk + 2 * r + 1, dtype=torch.float32, device=device)
@@ -285,13 +295,13 @@ def epilogue_struct(out: ForwardOut) -> _lib.EpilogueOut:
     )
 
 
-def run_forward(args: KernelArgs) -> ForwardOut:
+def run_forward(args: KernelArgs, separate: bool = False) -> ForwardOut:
     """Statistics + epilogue in one launch on the current stream."""
     lib = _lib.load()
     s = args.setup
     b_total = int(args.inputs.b_total)
     device = args.x.device
-    out = alloc_outputs(device, b_total, s.cl, s.num_bins)
+    out = alloc_outputs(device, b_total, s.cl, s.num_bins, separate)
     nbytes = lib.ace_b200_workspace_bytes(b_total, s.cl, s.num_bins)
     ws = workspace(device, nbytes)
     stream = torch.cuda.current_stream(device).cuda_stream
@@ -372,27 +382,65 @@ class B200ACELoss(torch.autograd.Function):
 # torch.library custom ops: the same two launches as opaque nodes, so that
 # torch.compile(fullgraph=True) of a training step keeps the loss in the graph
 # (the reference does the same for its v6 path: ace_kernels/impls/v6_triton.py:141-216).
-# The config travels as its JSON; it must be constant for a compiled function.
+# The config travels as its fields (plain scalars, which the compiler reads as
+# constants of the traced code); it must stay constant for a compiled function.
 # ---------------------------------------------------------------------------
 @functools.lru_cache(maxsize=64)
-def _config_from_json(config_json: str) -> ACEConfig:
-    return ACEConfig.model_validate_json(config_json)
+def _config_from_fields(binning: str, num_bins: int, activation: str, to_onehot_y: bool,
+                        include_background: bool, ignore_empty_classes: bool,
+                        reduction: str, weight: tuple[float, ...] | float | None, right: bool,
+                        empty_weight: float) -> ACEConfig:
+    return ACEConfig(binning=binning, num_bins=num_bins, activation=activation,
+                     to_onehot_y=to_onehot_y, include_background=include_background,
+                     ignore_empty_classes=ignore_empty_classes, reduction=reduction,
+                     weight=weight, right=right, empty_weight=empty_weight)
+
+
+def _op_config(fields: list[float], names: str) -> ACEConfig:
+    """Inverse of ``_op_fields``."""
+    binning, activation, reduction, weight_kind = names.split(",")
+    num_bins, to_onehot_y, include_bg, ignore_empty, right, empty_weight = fields[:6]
+    rest = tuple(float(v) for v in fields[6:])
+    weight: tuple[float, ...] | float | None
+    if weight_kind == "none":
+        weight = None
+    elif weight_kind == "scalar":
+        weight = rest[0]
+    else:
+        weight = rest
+    return _config_from_fields(binning, int(num_bins), activation, bool(to_onehot_y),
+                               bool(include_bg), bool(ignore_empty), reduction, weight,
+                               bool(right), float(empty_weight))
+
+
+def _op_fields(config: Any) -> tuple[list[float], str]:
+    """The config as (numbers, "binning,activation,reduction,weight_kind")."""
+    w = config.weight
+    if w is None:
+        kind, wl = "none", []
+    elif isinstance(w, (int, float)):
+        kind, wl = "scalar", [float(w)]
+    else:
+        kind, wl = "seq", [float(v) for v in w]
+    nums = [float(config.num_bins), float(config.to_onehot_y), float(config.include_background),
+            float(config.ignore_empty_classes), float(config.right), float(config.empty_weight), *wl]
+    return nums, f"{config.binning},{config.activation},{config.reduction},{kind}"
 
 
 @torch.library.custom_op("ace_b200::forward", mutates_args=())
 def op_forward(
-    input: torch.Tensor, target: torch.Tensor, config_json: str
+    input: torch.Tensor, target: torch.Tensor, fields: list[float], names: str
 ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
-    config = _config_from_json(config_json)
+    config = _op_config(fields, names)
     args = kernel_args(input, target, config)
-    out = run_forward(args)
+    out = run_forward(args, separate=True)
     loss = shape_loss(out, args.setup, input)
-    return loss.clone(), out.coef, out.d, out.jac
+    return loss.clone() if loss.dim() else loss, out.coef, out.d, out.jac
 
 
 @op_forward.register_fake
-def _(input: torch.Tensor, target: torch.Tensor, config_json: str) -> tuple[torch.Tensor, ...]:
-    config = _config_from_json(config_json)
+def _(input: torch.Tensor, target: torch.Tensor, fields: list[float], names: str) -> tuple[torch.Tensor, ...]:
+    config = _op_config(fields, names)
     b, c = input.shape[:2]
     cl = c - (1 if (not config.include_background and c > 1) else 0)
     per_bin = input.new_empty((b, cl, config.num_bins), dtype=torch.float32)
@@ -410,51 +458,42 @@ def op_backward(
     d: torch.Tensor,
     jac: torch.Tensor,
     grad_output: torch.Tensor,
-    config_json: str,
+    fields: list[float],
+    names: str,
 ) -> torch.Tensor:
-    config = _config_from_json(config_json)
+    config = _op_config(fields, names)
     args = kernel_args(input, target, config)
     return run_backward(args, coef, d, jac, grad_output).view(input.shape)
 
 
 @op_backward.register_fake
-def _(input, target, coef, d, jac, grad_output, config_json):  # type: ignore[no-untyped-def]
+def _(input, target, coef, d, jac, grad_output, fields, names):  # type: ignore[no-untyped-def]
     return torch.empty_like(input)
 
 
 def _setup_context(ctx: Any, inputs: tuple[Any, ...], output: Any) -> None:
-    input, target, config_json = inputs
+    input, target, fields, names = inputs
     _, coef, d, jac = output
-    ctx.config_json = config_json
+    ctx.fields, ctx.names = fields, names
     ctx.set_materialize_grads(False)
     ctx.save_for_backward(input, target, coef, d, jac)
 
 
 def _op_autograd(ctx: Any, grad_loss: torch.Tensor, *_unused: Any) -> tuple[Any, ...]:
     input, target, coef, d, jac = ctx.saved_tensors
-    dx = op_backward(input, target, coef, d, jac, grad_loss, ctx.config_json)
-    return dx, None, None
+    dx = op_backward(input, target, coef, d, jac, grad_loss, ctx.fields, ctx.names)
+    return dx, None, None, None
 
 
 op_forward.register_autograd(_op_autograd, setup_context=_setup_context)
 
 
-def _config_json(config: Any) -> str:
-    if isinstance(config, ACEConfig):
-        return config.model_dump_json()
-    return ACEConfig.model_validate(
-        {name: getattr(config, name) for name in ACEConfig.model_fields}
-    ).model_dump_json()
-
-
-config_arg = torch.compiler.assume_constant_result(_config_json)
-
-
 def b200_cuda(input: torch.Tensor, target: torch.Tensor, config: Any) -> torch.Tensor:
     """Registry function of ``impl="b200_cuda"``: mL1-ACE loss of ``input``
     against ``target`` under ``config`` (an ``ACEConfig``, ours or the
-    reference's)."""
+    reference's). Under ``torch.compile`` the loss is the custom-op pair."""
     if torch.compiler.is_compiling():
-        return op_forward(input, target, config_arg(config))[0]
+        fields, names = _op_fields(config)
+        return op_forward(input, target, fields, names)[0]
     loss: torch.Tensor = B200ACELoss.apply(input, target, config)
     return loss

@@ -151,14 +151,16 @@ int ace_b200_hist(const ace_b200_inputs* in, const ace_b200_options* opt, float*
                   void* workspace, size_t workspace_bytes, void* stream);
 
 /*
- * Epilogue on [3, b_total, cl, K] statistics. Replaces epilogue_triton
+ * Epilogue on [3, b_total, cl, K] statistics (workspace as for ace_b200_hist,
+ * with the same b_total, cl and num_bins). Replaces epilogue_triton
  * (ace_kernels/kernels/epilogue.py:23-129), i.e. v2_autograd.coefficients
  * (ace_kernels/impls/v2_autograd.py:66-76) + common.reduce_classes
  * (ace_kernels/common.py:184-207) + the reduction jacobian
  * (ace_kernels/impls/v2_autograd.py:138-151).
  */
 int ace_b200_epilogue(const float* hist, int64_t b_total, int64_t cl, double rows_global,
-                      const ace_b200_options* opt, ace_b200_epilogue_out out, void* stream);
+                      const ace_b200_options* opt, ace_b200_epilogue_out out, void* workspace,
+                      size_t workspace_bytes, void* stream);
 
 /*
  * Backward: d loss / d x for this launch's x (dx has x's dtype and shape).

@@ -136,8 +136,9 @@ def test_misaligned_and_odd_sizes_use_scalar_path() -> None:
     xo.copy_(x)
     a = run("b200_cuda", xo, y, cfg)
     b = run("b200_cuda", x.clone(), y, cfg)
-    torch.testing.assert_close(a.loss, b.loss, rtol=0, atol=0)
-    torch.testing.assert_close(a.grad, b.grad, rtol=0, atol=0)
+    # same bins; the sums add in another order (another vector width)
+    torch.testing.assert_close(a.loss, b.loss, rtol=1e-6, atol=1e-7)
+    torch.testing.assert_close(a.grad, b.grad, rtol=1e-4, atol=1e-9)
 
 
 @pytest.mark.parametrize("binning", ["hard", "soft"])

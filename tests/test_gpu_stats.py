@@ -74,7 +74,7 @@ def test_bins_vs_cpu_softmax_only_near_boundaries(binning: str, include_backgrou
                      "include_background": include_background})
     x, y = make(Spec(2, 5, (40, 40, 9), seed=5), 20, "cuda")
     hist = kernel_hist(x, y, cfg).cpu()
-    p_cpu = oracle.activate(x.cpu(), "softmax")
+    p_cpu = oracle.activate(x.cpu(), "softmax").flatten(2)
     W, P, G = oracle_stats_on(p_cpu, x, y, cfg)
     p_gpu = kernel_probs(x, act_code(cfg, 5)).cpu()
     ulps = ((p_gpu.view(torch.int32).long() - p_cpu.view(torch.int32).long()).abs()).max().item()

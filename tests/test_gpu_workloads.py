@@ -22,7 +22,10 @@ def test_workload_matches_reference(name: str) -> None:
     w = wl.WORKLOADS[rec["workload"]]
     cfg = to_config(rec["config"])
     x, y = wl.make(w, "cuda")
-    res = run("b200_cuda", x, y, cfg)
+    # half-precision gradients of this loss (~1e-8) underflow in fp16: scale the
+    # upstream gradient as mixed-precision training does (loss scaling 2^16)
+    scale = 65536.0 if x.dtype != torch.float32 else 1.0
+    res = run("b200_cuda", x, y, cfg, torch.tensor(scale))
     rel = abs(res.loss.item() - rec["loss"].item()) / abs(rec["loss"].item())
     print(f"\n{name}: loss {res.loss.item():.7f} reference {rec['loss'].item():.7f} rel {rel:.2e}")
     assert rel <= 1e-5
@@ -39,11 +42,12 @@ def test_workload_matches_reference(name: str) -> None:
     for i, key in enumerate("WPG"):
         torch.testing.assert_close(hist[i], rec[key], rtol=5e-4, atol=1e-2)
 
-    g = res.grad.float().flatten().cpu()
+    g = res.grad.float().flatten().cpu() / scale
     got, want = g[rec["grad_idx"]], rec["grad_vals"]
-    ok = torch.isclose(got, want, rtol=1e-3, atol=1e-10)
+    rtol = {torch.float32: 1e-3, torch.float16: 2e-3, torch.bfloat16: 1e-2}[x.dtype]
+    ok = torch.isclose(got, want, rtol=rtol, atol=1e-10)
     print(f"sampled gradients: {int((~ok).sum())} of {ok.numel()} differ; "
           f"L2 rel {(got - want).norm() / want.norm():.2e}")
     assert (~ok).float().mean().item() <= 1e-3
     sq = g.double().square().sum().item()
-    assert sq == pytest.approx(rec["grad_sq_sum"], rel=2e-3)
+    assert sq == pytest.approx(rec["grad_sq_sum"], rel=2e-3 if x.dtype == torch.float32 else 2e-2)
