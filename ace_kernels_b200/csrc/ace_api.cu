@@ -93,17 +93,18 @@ int sm_count(int dev) {
 
 size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-// Workspace layout: [accumulators: 3 * b_total * cl * K 32-bit words][histogram
-// counter][epilogue counter][epilogue partial sums: one per epilogue CTA], each
-// part 256-byte aligned. Counters and accumulators are zero between calls.
+// Workspace layout: [accumulators: up to 6 * b_total * cl * (K + 1) doubles]
+// [histogram counter][epilogue counter][epilogue partial sums: one per epilogue
+// CTA], each part 256-byte aligned. Counters and accumulators are zero between
+// calls.
 size_t accum_bytes(int64_t b_total, int64_t cl, int K) {
-  return round_up((size_t)3 * b_total * cl * K * sizeof(float), 256);
+  return round_up((size_t)6 * b_total * cl * (K + 1) * sizeof(double), 256);
 }
 
 int64_t epi_ctas(int64_t rows) { return (rows + kEpiRowsPerCta - 1) / kEpiRowsPerCta; }
 
 struct Workspace {
-  float* accum;
+  double* accum;
   unsigned* hist_counter;
   unsigned* epi_counter;
   float* epi_partial;
@@ -113,7 +114,7 @@ Workspace carve(void* ws, int64_t b_total, int64_t cl, int K) {
   char* base = static_cast<char*>(ws);
   const size_t a = accum_bytes(b_total, cl, K);
   Workspace w;
-  w.accum = reinterpret_cast<float*>(base);
+  w.accum = reinterpret_cast<double*>(base);
   w.hist_counter = reinterpret_cast<unsigned*>(base + a);
   w.epi_counter = reinterpret_cast<unsigned*>(base + a + 256);
   w.epi_partial = reinterpret_cast<float*>(base + a + 512);
@@ -238,14 +239,15 @@ Variant choose_variant(const ace_b200_inputs* in, const ace_b200_options* opt, c
 
 // One wave of CTAs, split over the batches; each CTA gets a contiguous run of
 // tiles of one batch.
-Grid make_grid(const ace_b200_inputs* in, int CL, int offset, int V, int ctas_per_sm, int dev) {
+Grid make_grid(const ace_b200_inputs* in, int CL, int offset, int V, int threads,
+               int ctas_per_sm, int dev) {
   Grid g;
   g.N = in->N;
   g.B = (int)in->B;
   g.C = (int)in->C;
   g.CL = CL;
   g.offset = offset;
-  const int64_t tile = (int64_t)kThreads * V;
+  const int64_t tile = (int64_t)threads * V;
   g.tiles = (in->N + tile - 1) / tile;
   const int64_t wave = (int64_t)sm_count(dev) * ctas_per_sm;
   int64_t chunks = (wave + g.B - 1) / g.B;
@@ -303,16 +305,29 @@ int hist_impl(const ace_b200_inputs* in, const ace_b200_options* opt, float* his
     rc = fill_epi(p.epi, in->b_total, CL, in->rows_global, opt, *out);
     if (rc) return rc;
   }
-  const Variant v = choose_variant(in, opt, nullptr);
-  // Lane replicas of the shared-memory table: as many as fit in ~56 KB (32 =
-  // conflict-free), so several CTAs stay resident per SM.
+  Variant v = choose_variant(in, opt, nullptr);
+  // Shared-memory table: `entries` words per lane replica. A 32-bit word of a
+  // replica takes at most (kHistThreads / R) * V additions per tile and must not
+  // take more than 511 between two folds (values up to 2^22 each), so R has a
+  // floor; above it, as many replicas as fit in ~100 KB (32 = conflict-free),
+  // two CTAs per SM.
   const bool soft = opt->soft != 0;
-  const int entries = CL * K * 3;
+  const bool labels = in->target_kind == ACE_B200_TARGET_LABELS;
+  const int nacc = soft ? (labels ? 10 : 11) : 3;
+  const int entries = CL * (soft ? K + 1 : K) * nacc;
   const size_t table_bytes = 2 * (kMaxBins + 1) * sizeof(float);
+  auto r_min = [&](int V) {
+    int r = 1;
+    while ((kHistThreads / r) * V > 511) r <<= 1;
+    return r;
+  };
+  if (table_bytes + (size_t)entries * r_min(v.V) * 4 > 200 * 1024) v.V = 1;
   int R = 32;
-  while (R > 1 && table_bytes + (size_t)entries * R * 4 > 44 * 1024) R >>= 1;
+  while (R > r_min(v.V) && table_bytes + (size_t)entries * R * 4 > 100 * 1024) R >>= 1;
   const int smem = (int)(table_bytes + (size_t)entries * R * 4);
-  if (smem > 227 * 1024) return fail(ACE_B200_EUNSUPPORTED, "statistics do not fit in shared memory");
+  if (smem > 200 * 1024)
+    return fail(ACE_B200_EUNSUPPORTED,
+                "statistics table of %d channels x %d bins does not fit in shared memory", CL, K);
 
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -320,10 +335,11 @@ int hist_impl(const ace_b200_inputs* in, const ace_b200_options* opt, float* his
   const int occ = occupancy(0, in->x_dtype, v, smem, dev);
   p.x = in->x;
   p.target = in->target;
-  p.g = make_grid(in, CL, opt->offset, v.V, occ, dev);
+  p.g = make_grid(in, CL, opt->offset, v.V, kHistThreads, occ, dev);
   p.act = opt->activation;
   p.soft = soft;
   p.R = R;
+  p.flush_tiles = 511 / ((kHistThreads / R) * v.V);
   p.b_offset = (int)in->b_offset;
   p.B_total = (int)in->b_total;
   const Workspace w = carve(workspace, in->b_total, CL, K);
@@ -468,7 +484,7 @@ int ace_b200_backward(const ace_b200_inputs* in, const ace_b200_options* opt,
   p.x = in->x;
   p.target = in->target;
   p.dx = dx;
-  p.g = make_grid(in, CL, opt->offset, v.V, occ, dev);
+  p.g = make_grid(in, CL, opt->offset, v.V, kThreads, occ, dev);
   p.act = opt->activation;
   p.soft = soft;
   p.b_offset = (int)in->b_offset;

@@ -75,14 +75,14 @@ __device__ __forceinline__ int warp_sum_i(int v) {
 // Returns (on every thread) this CTA's sum of f over its rows, in fixed order.
 __device__ __forceinline__ float epilogue_rows(const EpiParams& E, const float* st, int st_rows,
                                                int st_row0, int r0, int r1) {
-  __shared__ float wsum[kThreads / 32];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  __shared__ float wsum[32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
   const int K = E.K;
   const int64_t RK = (int64_t)st_rows * K;
   const float nan = __int_as_float(0x7fc00000);
   const float rows = (float)E.rows_global;
   float mine = 0.0f;
-  for (int r = r0 + warp; r < r1; r += kThreads / 32) {
+  for (int r = r0 + warp; r < r1; r += nwarps) {
     const int64_t base = (int64_t)(r - st_row0) * K;
     float dk[4], wk[4];
     bool ne[4];
@@ -141,8 +141,7 @@ __device__ __forceinline__ float epilogue_rows(const EpiParams& E, const float* 
   if (lane == 0) wsum[warp] = mine;
   __syncthreads();
   float total = 0.0f;
-#pragma unroll
-  for (int w = 0; w < kThreads / 32; ++w) total = ACE_FADD(total, wsum[w]);
+  for (int w = 0; w < nwarps; ++w) total = ACE_FADD(total, wsum[w]);
   __syncthreads();
   return total;
 }
@@ -157,54 +156,121 @@ __device__ __forceinline__ void write_loss_if0(const EpiParams& E, float total) 
 }
 
 // ---------------------------------------------------------------------------
-// Shared-memory statistics table, lane-replicated.
+// Shared-memory statistics table: integer fixed point, lane-replicated.
 //
-// Layout [row][bin][stat][R] 32-bit words, stat 0 W, 1 P, 2 G; lane l updates
-// replica l % R, so with R = 32 every warp-wide update is conflict-free whatever
-// the bins are (no serialisation on hot bins such as p < 0.05). Hard-binning
-// counts (W, and G with label targets) are exact u32 counts; every other
-// statistic is an fp32 sum (shared-memory atomic adds, fire-and-forget).
-// Soft binning adds, per value, its two interpolation weights lw, rw (and lw p,
-// rw p, lw y, rw y) to the two neighbouring bins, exactly as the reference's
-// scatters (ace_kernels/binning.py:74-116, ace_reference/softl1ace.py:112-140).
+// Values are accumulated with native 32-bit integer shared-memory atomics (a
+// float atomic add there is a compare-and-swap loop, measured 3x slower). A
+// value v in [0, 1] is added as the bit pattern of the float v * 2^22 +
+// 1.5 * 2^23, which equals 0x4B400000 + round(v * 2^22): one FMA-pipe
+// instruction and no conversion instruction. Each slot also counts its additions
+// (n), so its sum of patterns minus n * 0x4B400000 (mod 2^32) is the exact sum of
+// the rounded values. For soft binning, where sums of a few small weights
+// matter, every value is split in two words: hi = round(v * 2^22) and lo =
+// round((v * 2^22 - hi) * 2^22), an absolute precision of 2^-45 per value. The CTA
+// folds its table into the workspace before any 32-bit word could overflow
+// (every `flush_tiles` tiles) and at the end. The sums are integers, so they do
+// not depend on the order of the additions.
+//
+// Layout [row][slot][acc][R] 32-bit words; lane l updates replica l % R (R = 32
+// keeps every warp-wide update conflict-free whatever the bins are).
+//   hard, slot = bin k (K slots):        0 n, 1 p, 2 y (a count for labels)
+//   soft, slot = interval j (K+1 slots): 0 n, 1-2 t, 3-4 p, 5-6 t p,
+//        labels: 7 ny (true-class count), 8-9 t (true class);
+//        dense:  7-8 y, 9-10 t y
+// where interval j lies between bin centres j-1 and j (sentinels at the ends),
+// t = (p - lo) / S is the weight of the right bin and 1 - t the weight of the
+// left bin (ace_kernels/common.py:43-61). W, P, G of the bins follow exactly
+// from these moments (the last CTA's reconstruction below).
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void sadd_f(float* h, int a, float v) { atomicAdd(h + a, v); }
-__device__ __forceinline__ void sadd_u(float* h, int a, unsigned v) {
-  atomicAdd(reinterpret_cast<unsigned*>(h) + a, v);
+template <bool SOFT, bool LABELS>
+struct Acc {
+  static constexpr int NACC = SOFT ? (LABELS ? 10 : 11) : 3;  // words per slot
+  static constexpr int NOUT = SOFT ? 6 : 3;                   // global sums per slot
+};
+
+constexpr float kFixScale = 4194304.0f;          // 2^22
+constexpr float kFixMagic = 12582912.0f;         // 1.5 * 2^23
+constexpr unsigned kFixMagicBits = 0x4B400000u;  // bits of kFixMagic
+
+__device__ __forceinline__ void sadd(unsigned* h, int a, unsigned v) { atomicAdd(h + a, v); }
+
+// Bit patterns of the hi and lo words of v * 2^22 = vs (already scaled).
+__device__ __forceinline__ uint2 fix2_scaled(float vs) {
+  const float hb = __fadd_rn(vs, kFixMagic);
+  const float r = __fsub_rn(vs, __fsub_rn(hb, kFixMagic));  // exact residual, |r| <= 1/2
+  return make_uint2(__float_as_uint(hb), __float_as_uint(__fmaf_rn(r, kFixScale, kFixMagic)));
+}
+// Same for a product a * b (a scaled by 2^22): one rounding for hi, exact residual.
+__device__ __forceinline__ uint2 fix2_prod(float as, float b) {
+  const float hb = __fmaf_rn(as, b, kFixMagic);
+  const float r = __fmaf_rn(as, b, -__fsub_rn(hb, kFixMagic));
+  return make_uint2(__float_as_uint(hb), __float_as_uint(__fmaf_rn(r, kFixScale, kFixMagic)));
+}
+__device__ __forceinline__ unsigned fix1(float v) {
+  return __float_as_uint(__fmaf_rn(v, kFixScale, kFixMagic));
 }
 
-// Is statistic `stat` an exact count?
-template <bool SOFT, bool LABELS>
-__device__ __forceinline__ constexpr bool stat_is_count(int stat) {
-  return !SOFT && (stat == 0 || (stat == 2 && LABELS));
-}
-
-// Folds this CTA's table into the workspace and clears it: one warp per
-// (row, bin), lane l reading replica l of the three statistics (conflict-free),
-// a warp reduction in a fixed order, then one global atomic per non-zero sum.
-// Called by all threads between barriers.
-template <bool SOFT, bool LABELS>
-__device__ __forceinline__ void fold_table(float* hist, int CL, int K, int R, float* accum,
-                                           int64_t stat_stride, int64_t row0) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int e = warp; e < CL * K; e += kThreads / 32) {
-    float* base = hist + (int64_t)e * 3 * R;
-    const int64_t gi = row0 * K + e;
+__device__ __forceinline__ long long warp_sum_ll(long long v) {
 #pragma unroll
-    for (int s = 0; s < 3; ++s) {
-      if (stat_is_count<SOFT, LABELS>(s)) {
-        unsigned v = 0;
-        for (int l = lane; l < R; l += 32) v += __float_as_uint(base[s * R + l]);
-        v = __reduce_add_sync(0xffffffffu, v);
-        if (lane == 0 && v) atomicAdd(reinterpret_cast<unsigned*>(accum) + s * stat_stride + gi, v);
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Folds this CTA's table into the workspace (double sums, one global atomic per
+// non-zero sum) and clears it: one warp per slot, lane l reading replica l
+// (conflict-free), exact integer warp reductions. Called by all threads
+// between barriers.
+template <bool SOFT, bool LABELS>
+__device__ __forceinline__ void fold_table(unsigned* hist, int CL, int slots, int R,
+                                           double* accum, int64_t out_stride, int64_t row0) {
+  constexpr int NACC = Acc<SOFT, LABELS>::NACC;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const double unit = 1.0 / 4194304.0;           // 2^-22
+  const double unit2 = unit / 4194304.0;         // 2^-44
+  for (int e = warp; e < CL * slots; e += nwarps) {
+    unsigned* base = hist + (int64_t)e * NACC * R;
+    unsigned w[NACC];
+#pragma unroll
+    for (int a = 0; a < NACC; ++a) w[a] = lane < R ? base[a * R + lane] : 0u;
+#pragma unroll
+    for (int a = 0; a < NACC; ++a)
+      if (lane < R) base[a * R + lane] = 0u;
+    const unsigned n = w[0];
+    const unsigned ny = (SOFT && LABELS) ? w[7] : 0u;
+    // per-lane exact value of a magic-offset word with `cnt` additions
+    auto val = [&](unsigned raw, unsigned cnt) -> long long {
+      return (long long)(int)(raw - cnt * kFixMagicBits);
+    };
+    double out[Acc<SOFT, LABELS>::NOUT];
+    if constexpr (!SOFT) {
+      out[0] = (double)warp_sum_ll((long long)n);
+      out[1] = (double)warp_sum_ll(val(w[1], n)) * unit;
+      out[2] = LABELS ? (double)warp_sum_ll((long long)w[2])
+                      : (double)warp_sum_ll(val(w[2], n)) * unit;
+    } else {
+      auto pair = [&](int a, unsigned cnt) -> double {
+        const long long v = val(w[a], cnt) * 4194304ll + val(w[a + 1], cnt);
+        return (double)warp_sum_ll(v) * unit2;
+      };
+      out[0] = (double)warp_sum_ll((long long)n);
+      out[1] = pair(1, n);
+      out[2] = pair(3, n);
+      out[3] = pair(5, n);
+      if constexpr (LABELS) {
+        out[4] = (double)warp_sum_ll((long long)ny);
+        out[5] = pair(8, ny);
       } else {
-        float v = 0.0f;
-        for (int l = lane; l < R; l += 32) v += base[s * R + l];
-        v = warp_sum(v);
-        if (lane == 0 && v != 0.0f) atomicAdd(accum + s * stat_stride + gi, v);
+        out[4] = pair(7, n);
+        out[5] = pair(9, n);
       }
     }
-    for (int l = lane; l < 3 * R; l += 32) base[l] = 0.0f;
+    if (lane == 0) {
+      const int row = e / slots, slot = e - row * slots;
+      const int64_t gi = (row0 + row) * slots + slot;
+#pragma unroll
+      for (int a = 0; a < Acc<SOFT, LABELS>::NOUT; ++a)
+        if (out[a] != 0.0) atomicAdd(accum + a * out_stride + gi, out[a]);
+    }
   }
 }
 
@@ -219,181 +285,197 @@ __device__ __forceinline__ int channels(int runtime_c) {
 // ---------------------------------------------------------------------------
 // Forward: fused activation + W/P/G statistics (+ epilogue in the last CTA).
 //
-// Grid (chunks, B): CTA (x, b) streams tiles [x * tpc, (x + 1) * tpc) of batch b;
-// a tile is kThreads * V voxels and thread t owns V consecutive voxels of it, read
-// with 16-byte (V * sizeof(T)) coalesced loads per channel (the channel stride is
-// N). The logits of all C channels of a voxel are in registers, so the softmax
-// needs no second read. Per voxel the bins of all loss channels are located first
-// (one shared-memory load each, straight-line), a rare fix-up pass corrects
-// guesses off by one, then the table updates are issued; the true class's target
-// updates are issued once per voxel. At the end the CTA folds its table into the
-// workspace, and the last CTA to finish (counter in the workspace, no waiting)
-// writes W, P, G, resets the workspace and runs the epilogue.
+// Grid (chunks, B), kHistThreads threads: CTA (x, b) streams tiles
+// [x * tpc, (x + 1) * tpc) of batch b; a tile is kHistThreads * V voxels and
+// thread t owns V consecutive voxels of it, read with 16-byte (V * sizeof(T))
+// coalesced loads per channel (the channel stride is N). The logits of all C
+// channels of a voxel are in registers, so the softmax needs no second read. Per
+// voxel the bins of all loss channels are located first (one shared-memory load
+// each, straight-line), a rare fix-up pass corrects guesses off by one, then the
+// table updates are issued; the true class's target updates are issued once per
+// voxel. The last CTA to finish (counter in the workspace, no waiting) turns the
+// workspace sums into W, P, G, resets the workspace and runs the epilogue.
 // ---------------------------------------------------------------------------
 template <typename T, int V, int CM, bool SOFTMAX, bool SOFT, bool LABELS>
-__global__ void __launch_bounds__(kThreads) hist_kernel(const __grid_constant__ FwdParams P) {
+__global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constant__ FwdParams P) {
+  constexpr int NACC = Acc<SOFT, LABELS>::NACC;
+  constexpr int NOUT = Acc<SOFT, LABELS>::NOUT;
   extern __shared__ __align__(16) float smem[];
   const int tid = threadIdx.x;
   const int b = blockIdx.y;
   const int C = channels<CM, SOFTMAX>(P.g.C), CL = P.g.CL, off = P.g.offset, K = P.tab.K;
+  const int slots = SOFT ? K + 1 : K;
   const int64_t N = P.g.N;
   const int R = P.R;
   const float Kf = (float)K;
 
   float2* pairs = reinterpret_cast<float2*>(smem);
-  float* hist = smem + 2 * (kMaxBins + 1);
-  const int table_words = CL * K * 3 * R;
-  for (int i = tid; i <= K; i += kThreads) pairs[i] = P.tab.pair[i];
-  for (int i = tid; i < table_words; i += kThreads) hist[i] = 0.0f;
+  unsigned* hist = reinterpret_cast<unsigned*>(smem + 2 * (kMaxBins + 1));
+  const int table_words = CL * slots * NACC * R;
+  for (int i = tid; i <= K; i += kHistThreads) pairs[i] = P.tab.pair[i];
+  for (int i = tid; i < table_words; i += kHistThreads) hist[i] = 0u;
   __syncthreads();
 
   const int col = tid & (R - 1);
-  const int bin_stride = 3 * R, row_stride = K * bin_stride;
-  const int R2 = 2 * R;
-  const int64_t stat_stride = (int64_t)P.B_total * CL * K;
+  const int slot_stride = NACC * R, row_stride = slots * slot_stride;
+  const int64_t out_stride = (int64_t)P.B_total * CL * slots;
   const int64_t row0 = (int64_t)(P.b_offset + b) * CL;
 
   const T* xb = static_cast<const T*>(P.x) + (int64_t)b * C * N;
   const int64_t* lb = LABELS ? static_cast<const int64_t*>(P.target) + (int64_t)b * N : nullptr;
   const float* yb = LABELS ? nullptr : static_cast<const float*>(P.target) + (int64_t)b * C * N;
 
-  // One loss-channel value into the table. Returns what the true-class target
-  // update of this value needs: the table index of its (left) bin, and for soft
-  // binning the right bin's index offset and the two weights.
-  struct TrueUpd {
-    int a, ar;
-    float lw, rw;
+  // One loss-channel value into the table; returns the slot index (-1: none) and
+  // the scaled right weight for the true-class target update.
+  struct Upd {
+    int a;
+    float ts;
   };
-  auto update = [&](int row, float p, int j, float2 lohi, float y) -> TrueUpd {
-    TrueUpd t;
+  auto update = [&](int row, float p, int j, float2 lohi, float y) -> Upd {
+    Upd u;
+    u.a = -1;
+    u.ts = 0.0f;
     if constexpr (!SOFT) {
-      t.a = -1;
       if (j < K) {  // p above the last edge (only for invalid p > 1 + eps) is dropped
-        const int a = row * row_stride + j * bin_stride + col;
-        sadd_u(hist, a, 1u);
-        sadd_f(hist, a + R, p);
-        if constexpr (!LABELS) {
-          if (y != 0.0f) sadd_f(hist, a + R2, y);
-        }
-        t.a = a;
+        const int a = row * row_stride + j * slot_stride + col;
+        sadd(hist, a, 1u);
+        sadd(hist, a + R, fix1(p));
+        if constexpr (!LABELS) sadd(hist, a + 2 * R, fix1(y));
+        u.a = a;
       }
     } else {
-      const SoftW w = ace_soft_weights(p, j, lohi, K);
-      const int base = row * row_stride + col;
-      const int al = base + w.l * bin_stride, ar = base + w.r * bin_stride;
-      sadd_f(hist, al, w.lw);
-      sadd_f(hist, ar, w.rw);
-      sadd_f(hist, al + R, ACE_FMUL(w.lw, p));
-      sadd_f(hist, ar + R, ACE_FMUL(w.rw, p));
+      const float ld = ACE_FSUB(p, lohi.x);
+      const float rd = ACE_FSUB(lohi.y, p);
+      const float inv = ACE_FMUL(ace_rcp_approx(ACE_FADD(ld, rd)), kFixScale);
+      const float ts = fminf(ACE_FMUL(ld, inv), kFixScale);  // t * 2^22, t in [0, 1]
+      const int a = row * row_stride + j * slot_stride + col;
+      sadd(hist, a, 1u);
+      const uint2 tw = fix2_scaled(ts);
+      sadd(hist, a + R, tw.x);
+      sadd(hist, a + 2 * R, tw.y);
+      const uint2 pw = fix2_prod(kFixScale, p);
+      sadd(hist, a + 3 * R, pw.x);
+      sadd(hist, a + 4 * R, pw.y);
+      const uint2 tpw = fix2_prod(ts, p);
+      sadd(hist, a + 5 * R, tpw.x);
+      sadd(hist, a + 6 * R, tpw.y);
       if constexpr (!LABELS) {
-        if (y != 0.0f) {
-          sadd_f(hist, al + R2, ACE_FMUL(w.lw, y));
-          sadd_f(hist, ar + R2, ACE_FMUL(w.rw, y));
-        }
+        const uint2 yw = fix2_prod(kFixScale, y);
+        sadd(hist, a + 7 * R, yw.x);
+        sadd(hist, a + 8 * R, yw.y);
+        const uint2 tyw = fix2_prod(ts, y);
+        sadd(hist, a + 9 * R, tyw.x);
+        sadd(hist, a + 10 * R, tyw.y);
       }
-      t.a = al;
-      t.ar = ar;
-      t.lw = w.lw;
-      t.rw = w.rw;
+      u.a = a;
+      u.ts = ts;
     }
-    return t;
+    return u;
   };
-  auto true_update = [&](const TrueUpd& t) {
+  auto true_update = [&](const Upd& u) {
+    if (u.a < 0) return;
     if constexpr (!SOFT) {
-      if (t.a >= 0) sadd_u(hist, t.a + R2, 1u);
+      sadd(hist, u.a + 2 * R, 1u);
     } else {
-      sadd_f(hist, t.a + R2, t.lw);
-      sadd_f(hist, t.ar + R2, t.rw);
+      sadd(hist, u.a + 7 * R, 1u);
+      const uint2 tw = fix2_scaled(u.ts);
+      sadd(hist, u.a + 8 * R, tw.x);
+      sadd(hist, u.a + 9 * R, tw.y);
     }
   };
 
   const int64_t t0 = (int64_t)blockIdx.x * P.g.tiles_per_chunk;
   const int64_t t1 = min(t0 + P.g.tiles_per_chunk, P.g.tiles);
+  int since_fold = 0;
   for (int64_t t = t0; t < t1; ++t) {
-    const int64_t v0 = (t * kThreads + tid) * V;
-    if (v0 >= N) continue;  // V > 1 implies N % V == 0: groups are whole
-    int lab[V];
-    if constexpr (LABELS) ace_load_labels<V>(lb + v0, lab);
-    if constexpr (SOFTMAX) {
-      float xv[CM][V];
-#pragma unroll
-      for (int c = 0; c < CM; ++c)
-        if (c < C) VecIO<T, V>::load(xb + (int64_t)c * N + v0, xv[c]);
-      float yv[CM][V];
-      if constexpr (!LABELS) {
+    const int64_t v0 = (t * kHistThreads + tid) * V;
+    if (v0 < N) {  // V > 1 implies N % V == 0: groups are whole
+      int lab[V];
+      if constexpr (LABELS) ace_load_labels<V>(lb + v0, lab);
+      if constexpr (SOFTMAX) {
+        float xv[CM][V];
 #pragma unroll
         for (int c = 0; c < CM; ++c)
-          if ((c > 0 || off == 0) && c < C) VecIO<float, V>::load(yb + (int64_t)c * N + v0, yv[c]);
-      }
-#pragma unroll
-      for (int i = 0; i < V; ++i) {
-        float p[CM];
-#pragma unroll
-        for (int c = 0; c < CM; ++c) p[c] = xv[c][i];
-        ace_softmax<CM>(p, C);
-        int j[CM];
-        float2 lh[CM];
-        bool ok = true;
-#pragma unroll
-        for (int c = 0; c < CM; ++c) {
-          if ((c > 0 || off == 0) && c < C) {
-            j[c] = ace_guess(p[c], Kf, K, SOFT);
-            lh[c] = pairs[j[c]];
-            ok &= ace_is_count(p[c], j[c], K, lh[c]);
-          }
-        }
-        if (!ok) {
+          if (c < C) VecIO<T, V>::load(xb + (int64_t)c * N + v0, xv[c]);
+        float yv[CM][V];
+        if constexpr (!LABELS) {
 #pragma unroll
           for (int c = 0; c < CM; ++c)
-            if ((c > 0 || off == 0) && c < C && !ace_is_count(p[c], j[c], K, lh[c])) {
-              const Located r = ace_fix_count(p[c], j[c], K, pairs);
-              j[c] = r.i;
-              lh[c] = r.pr;
-            }
+            if ((c > 0 || off == 0) && c < C) VecIO<float, V>::load(yb + (int64_t)c * N + v0, yv[c]);
         }
-        TrueUpd tu;
-        tu.a = -1;
-        tu.ar = 0;
-        tu.lw = tu.rw = 0.0f;
-#pragma unroll
-        for (int c = 0; c < CM; ++c) {
-          if ((c > 0 || off == 0) && c < C) {
-            float y = 0.0f;
-            if constexpr (!LABELS) y = yv[c][i];
-            const TrueUpd u = update(c - off, p[c], j[c], lh[c], y);
-            if constexpr (LABELS) {
-              if (lab[i] == c) tu = u;
-            }
-          }
-        }
-        if constexpr (LABELS) {
-          if (lab[i] >= off && lab[i] < C) true_update(tu);
-        }
-      }
-    } else {
-      // none / sigmoid: channels are independent, one at a time
-      for (int c = off; c < C; ++c) {
-        float xv[V];
-        VecIO<T, V>::load(xb + (int64_t)c * N + v0, xv);
-        float yv[V];
-        if constexpr (!LABELS) VecIO<float, V>::load(yb + (int64_t)c * N + v0, yv);
 #pragma unroll
         for (int i = 0; i < V; ++i) {
-          const float p = P.act == ACE_B200_ACT_SIGMOID ? ace_sigmoid(xv[i]) : xv[i];
-          float2 lh;
-          const int j = ace_locate(p, pairs, K, Kf, SOFT, lh);
-          float y = 0.0f;
-          if constexpr (!LABELS) y = yv[i];
-          const TrueUpd u = update(c - off, p, j, lh, y);
-          if constexpr (LABELS) {
-            if (lab[i] == c) true_update(u);
+          float p[CM];
+#pragma unroll
+          for (int c = 0; c < CM; ++c) p[c] = xv[c][i];
+          ace_softmax<CM>(p, C);
+          int j[CM];
+          float2 lh[CM];
+          bool ok = true;
+#pragma unroll
+          for (int c = 0; c < CM; ++c) {
+            if ((c > 0 || off == 0) && c < C) {
+              j[c] = ace_guess(p[c], Kf, K, SOFT);
+              lh[c] = pairs[j[c]];
+              ok &= ace_is_count(p[c], j[c], K, lh[c]);
+            }
+          }
+          if (!ok) {
+#pragma unroll
+            for (int c = 0; c < CM; ++c)
+              if ((c > 0 || off == 0) && c < C && !ace_is_count(p[c], j[c], K, lh[c])) {
+                const Located r = ace_fix_count(p[c], j[c], K, pairs);
+                j[c] = r.i;
+                lh[c] = r.pr;
+              }
+          }
+          Upd tu;
+          tu.a = -1;
+          tu.ts = 0.0f;
+#pragma unroll
+          for (int c = 0; c < CM; ++c) {
+            if ((c > 0 || off == 0) && c < C) {
+              float y = 0.0f;
+              if constexpr (!LABELS) y = yv[c][i];
+              const Upd u = update(c - off, p[c], j[c], lh[c], y);
+              if constexpr (LABELS) {
+                if (lab[i] == c) tu = u;
+              }
+            }
+          }
+          if constexpr (LABELS) true_update(tu);
+        }
+      } else {
+        // none / sigmoid: channels are independent, one at a time
+        for (int c = off; c < C; ++c) {
+          float xv[V];
+          VecIO<T, V>::load(xb + (int64_t)c * N + v0, xv);
+          float yv[V];
+          if constexpr (!LABELS) VecIO<float, V>::load(yb + (int64_t)c * N + v0, yv);
+#pragma unroll
+          for (int i = 0; i < V; ++i) {
+            const float p = P.act == ACE_B200_ACT_SIGMOID ? ace_sigmoid(xv[i]) : xv[i];
+            float2 lh;
+            const int j = ace_locate(p, pairs, K, Kf, SOFT, lh);
+            float y = 0.0f;
+            if constexpr (!LABELS) y = yv[i];
+            const Upd u = update(c - off, p, j, lh, y);
+            if constexpr (LABELS) {
+              if (lab[i] == c) true_update(u);
+            }
           }
         }
       }
     }
+    if (++since_fold == P.flush_tiles && t + 1 < t1) {
+      since_fold = 0;
+      __syncthreads();
+      fold_table<SOFT, LABELS>(hist, CL, slots, R, P.accum, out_stride, row0);
+      __syncthreads();
+    }
   }
   __syncthreads();
-  fold_table<SOFT, LABELS>(hist, CL, K, R, P.accum, stat_stride, row0);
+  fold_table<SOFT, LABELS>(hist, CL, slots, R, P.accum, out_stride, row0);
   __threadfence();
   __syncthreads();
   __shared__ bool s_last;
@@ -405,25 +487,55 @@ __global__ void __launch_bounds__(kThreads) hist_kernel(const __grid_constant__ 
   if (!s_last) return;
   __threadfence();
 
-  // Last CTA: statistics out, workspace back to zero and, when all rows fit in
-  // the (now free) shared-memory table, the epilogue from shared memory.
+  // Last CTA: the workspace sums become W, P, G per bin. Hard: slot = bin. Soft:
+  // interval j in 1..K-1 gives its 1 - t share to bin j-1 and its t share to bin
+  // j; intervals 0 and K give everything to bins 0 and K-1 (both neighbours are
+  // the end bin there), exactly as the reference's two scatters.
   const int rows = P.B_total * CL;
-  const int64_t total = 3 * stat_stride;
-  const bool stage = P.do_epilogue && total <= (int64_t)table_words;
-  unsigned* acc_u = reinterpret_cast<unsigned*>(P.accum);
-  for (int64_t i = tid; i < total; i += kThreads) {
-    const int stat = (int)(i / stat_stride);
-    const bool is_u = !SOFT && (stat == 0 || (stat == 2 && LABELS));
-    const unsigned raw = __ldcg(acc_u + i);
-    const float v = is_u ? (float)raw : __uint_as_float(raw);
-    P.hist_out[i] = v;
-    if (stage) hist[i] = v;
-    __stcg(acc_u + i, 0u);
+  const int64_t stat_stride = (int64_t)rows * K;
+  const bool stage = P.do_epilogue && 3 * stat_stride <= (int64_t)table_words;
+  float* staged = reinterpret_cast<float*>(hist);
+  const double* acc = P.accum;
+  for (int64_t e = tid; e < stat_stride; e += kHistThreads) {
+    const int64_t r = e / K;
+    const int k = (int)(e - r * K);
+    double w, pp, g;
+    if constexpr (!SOFT) {
+      const int64_t gi = r * slots + k;
+      w = __ldcg(acc + gi);
+      pp = __ldcg(acc + out_stride + gi);
+      g = __ldcg(acc + 2 * out_stride + gi);
+    } else {
+      // bin k takes the t share of interval k and the 1 - t share of interval
+      // k + 1; an end interval (0 or K) gives it all of its moments
+      auto share = [&](int j, int a_all, int a_t) -> double {
+        const int64_t gi = r * slots + j;
+        const double all = __ldcg(acc + a_all * out_stride + gi);
+        if (j == 0 || j == K) return all;
+        const double tm = __ldcg(acc + a_t * out_stride + gi);
+        return j == k ? tm : all - tm;
+      };
+      w = share(k, 0, 1) + share(k + 1, 0, 1);
+      pp = share(k, 2, 3) + share(k + 1, 2, 3);
+      g = share(k, 4, 5) + share(k + 1, 4, 5);
+    }
+    const float wf = (float)w, pf = (float)pp, gf = (float)g;
+    P.hist_out[e] = wf;
+    P.hist_out[stat_stride + e] = pf;
+    P.hist_out[2 * stat_stride + e] = gf;
+    if (stage) {
+      staged[e] = wf;
+      staged[stat_stride + e] = pf;
+      staged[2 * stat_stride + e] = gf;
+    }
   }
+  __syncthreads();
+  double* accw = P.accum;
+  for (int64_t i = tid; i < NOUT * out_stride; i += kHistThreads) __stcg(accw + i, 0.0);
   if (tid == 0) *P.counter = 0u;
   if (stage) {
     __syncthreads();
-    write_loss_if0(P.epi, epilogue_rows(P.epi, hist, rows, 0, 0, rows));
+    write_loss_if0(P.epi, epilogue_rows(P.epi, staged, rows, 0, 0, rows));
   }
 }
 
@@ -644,14 +756,14 @@ struct HistLauncher {
     auto k = hist_kernel<T, V, CM, SM, SOFT, LAB>;
     cudaError_t e = set_smem(k, smem, configured());
     if (e != cudaSuccess) return e;
-    k<<<grid, kThreads, smem, s>>>(p);
+    k<<<grid, kHistThreads, smem, s>>>(p);
     return cudaGetLastError();
   }
   static int occupancy(int smem) {
     auto k = hist_kernel<T, V, CM, SM, SOFT, LAB>;
     set_smem(k, smem, configured());
     int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, kThreads, smem) != cudaSuccess) n = 1;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, kHistThreads, smem) != cudaSuccess) n = 1;
     return n > 0 ? n : 1;
   }
 };

@@ -12,7 +12,8 @@ namespace ace {
 
 constexpr int kMaxBins = ACE_B200_MAX_BINS;        // num_bins limit of the kernels
 constexpr int kMaxClasses = ACE_B200_MAX_CLASSES;  // channels limit of the kernels
-constexpr int kThreads = 256;                      // threads per CTA, all kernels
+constexpr int kThreads = 256;                      // threads per CTA (gradient, epilogue)
+constexpr int kHistThreads = 512;                  // threads per CTA of the histogram
 
 // Sorted search table with its neighbours paired (see ace_locate): hard binning
 // uses the K upper bin edges, soft binning the K bin centres; pair[i] =
@@ -65,9 +66,10 @@ struct FwdParams {
   int act;             // ACE_B200_ACT_*
   int soft;
   int R;               // lane replicas of the shared-memory histogram (power of 2)
+  int flush_tiles;     // tiles between folds of the shared table (32-bit range)
   int b_offset;        // first statistics row of this launch
   int B_total;
-  float* accum;        // workspace: [3, B_total, CL, K] sums (u32 for exact counts)
+  double* accum;       // workspace: [NOUT, B_total, CL, slots] sums (self-cleaning)
   unsigned* counter;   // workspace: finished-CTA counter (self-cleaning)
   float* hist_out;     // [3, B_total, CL, K] statistics (W, P, G)
   int do_epilogue;
