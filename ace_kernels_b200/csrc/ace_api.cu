@@ -312,9 +312,8 @@ int hist_impl(const ace_b200_inputs* in, const ace_b200_options* opt, float* his
   // floor; above it, as many replicas as fit in ~100 KB (32 = conflict-free),
   // two CTAs per SM.
   const bool soft = opt->soft != 0;
-  const bool labels = in->target_kind == ACE_B200_TARGET_LABELS;
-  const int nacc = soft ? (labels ? 10 : 11) : 3;
-  const int entries = CL * (soft ? K + 1 : K) * nacc;
+  const int words = soft ? 9 : 3;  // words per slot replica (odd: conflict-free)
+  const int entries = CL * (soft ? K + 1 : K) * words;
   const size_t table_bytes = 2 * (kMaxBins + 1) * sizeof(float);
   auto r_min = [&](int V) {
     int r = 1;

@@ -85,10 +85,12 @@ __host__ __device__ __forceinline__ int ace_guess(float p, float nf, int n, bool
   return i < 0 ? 0 : (i > n ? n : i);
 }
 
-// Is i the count for p, given pr = pair[i]? (The table is `right`-adjusted, so
-// "entry counted" is always t < p.)
-__host__ __device__ __forceinline__ bool ace_is_count(float p, int i, int n, float2 pr) {
-  return (i == 0 || pr.x < p) && (i == n || !(pr.y < p));
+// Is i the count for p, given pr = pair[i]? The table is `right`-adjusted, so
+// "entry counted" is always t < p, and its ends hold the -10000 / +10000
+// sentinels, which need no index test for -10000 < p < 10000 (a NaN or an
+// out-of-range value fails the test and takes the guarded slow path).
+__host__ __device__ __forceinline__ bool ace_is_count(float p, float2 pr) {
+  return pr.x < p && !(pr.y < p);
 }
 
 // Rare path: walk from a guess that failed ace_is_count to the count (one or two
@@ -123,7 +125,7 @@ __host__ __device__ __forceinline__ int ace_locate(float p, const float2* pair, 
                                                    bool soft, float2& lohi) {
   int i = ace_guess(p, nf, n, soft);
   float2 pr = pair[i];
-  if (!ace_is_count(p, i, n, pr)) {
+  if (!ace_is_count(p, pr)) {
     const Located r = ace_fix_count(p, i, n, pair);
     i = r.i;
     pr = r.pr;

@@ -161,31 +161,35 @@ __device__ __forceinline__ void write_loss_if0(const EpiParams& E, float total) 
 // Values are accumulated with native 32-bit integer shared-memory atomics (a
 // float atomic add there is a compare-and-swap loop, measured 3x slower). A
 // value v in [0, 1] is added as the bit pattern of the float v * 2^22 +
-// 1.5 * 2^23, which equals 0x4B400000 + round(v * 2^22): one FMA-pipe
-// instruction and no conversion instruction. Each slot also counts its additions
-// (n), so its sum of patterns minus n * 0x4B400000 (mod 2^32) is the exact sum of
-// the rounded values. For soft binning, where sums of a few small weights
-// matter, every value is split in two words: hi = round(v * 2^22) and lo =
-// round((v * 2^22 - hi) * 2^22), an absolute precision of 2^-45 per value. The CTA
-// folds its table into the workspace before any 32-bit word could overflow
-// (every `flush_tiles` tiles) and at the end. The sums are integers, so they do
-// not depend on the order of the additions.
+// 1.5 * 2^23, which equals 0x4B400000 + round(v * 2^22): FMA-pipe instructions
+// only, no conversion instruction. Each slot also counts its additions (n), so
+// its sum of patterns minus n * 0x4B400000 (mod 2^32) is the exact sum of the
+// rounded values. Where sums of a few small values matter (soft binning), every
+// value is split in two words, hi = round(v * 2^22) and lo = round((v * 2^22 -
+// hi) * 2^22): an absolute precision of 2^-45 per value. The CTA folds its table
+// into the workspace before any 32-bit word could overflow (every `flush_tiles`
+// tiles) and at the end; the sums are integers, so they do not depend on the
+// order of the additions.
 //
-// Layout [row][slot][acc][R] 32-bit words; lane l updates replica l % R (R = 32
-// keeps every warp-wide update conflict-free whatever the bins are).
-//   hard, slot = bin k (K slots):        0 n, 1 p, 2 y (a count for labels)
-//   soft, slot = interval j (K+1 slots): 0 n, 1-2 t, 3-4 p, 5-6 t p,
-//        labels: 7 ny (true-class count), 8-9 t (true class);
-//        dense:  7-8 y, 9-10 t y
-// where interval j lies between bin centres j-1 and j (sentinels at the ends),
-// t = (p - lo) / S is the weight of the right bin and 1 - t the weight of the
-// left bin (ace_kernels/common.py:43-61). W, P, G of the bins follow exactly
-// from these moments (the last CTA's reconstruction below).
+// Layout [row][slot][R][NW] 32-bit words, NW odd: lane l updates replica l % R,
+// whose NW words are contiguous, so the accumulator offsets are immediates and
+// the 32 lanes of a warp hit 32 different banks whatever their bins (R = 32).
+//   hard, slot = bin k (K slots), NW 3:  0 n, 1 p, 2 y (a count for labels)
+//   soft, slot = interval j (K+1 slots), NW 9:  0 n, 1-2 u, 3-4 u^2, then
+//        labels: 5 ny (true-class count), 6-7 u (true class), 8 unused;
+//        dense:  5-6 y, 7-8 u y
+// Interval j lies between bin centres lo = c_{j-1} and hi = c_j; there u = t =
+// (p - lo) / S with the interval's span S = hi - lo is the weight of the right
+// bin and 1 - t that of the left bin (ace_kernels/common.py:43-61), and p = lo +
+// S t, so the bins' W, P, G follow exactly from n, sum t, sum t^2 (the last CTA's
+// reconstruction below). In the two end intervals (sentinel at one side) all the
+// weight goes to one end bin: there u = p, and only n, sum p (and the target
+// moments) are used.
 // ---------------------------------------------------------------------------
 template <bool SOFT, bool LABELS>
 struct Acc {
-  static constexpr int NACC = SOFT ? (LABELS ? 10 : 11) : 3;  // words per slot
-  static constexpr int NOUT = SOFT ? 6 : 3;                   // global sums per slot
+  static constexpr int NW = SOFT ? 9 : 3;    // words per slot replica (odd)
+  static constexpr int NOUT = SOFT ? 6 : 3;  // global sums per slot
 };
 
 constexpr float kFixScale = 4194304.0f;          // 2^22
@@ -218,28 +222,34 @@ __device__ __forceinline__ long long warp_sum_ll(long long v) {
 
 // Folds this CTA's table into the workspace (double sums, one global atomic per
 // non-zero sum) and clears it: one warp per slot, lane l reading replica l
-// (conflict-free), exact integer warp reductions. Called by all threads
-// between barriers.
+// (conflict-free: NW is odd), exact integer warp reductions. Global sums per
+// slot: hard (n, sum p, sum y); soft (n, sum u, sum u^2, target count or sum y,
+// target sum u, [dense: sum u y]) as laid out in fold_out below. Called by all
+// threads between barriers.
 template <bool SOFT, bool LABELS>
 __device__ __forceinline__ void fold_table(unsigned* hist, int CL, int slots, int R,
                                            double* accum, int64_t out_stride, int64_t row0) {
-  constexpr int NACC = Acc<SOFT, LABELS>::NACC;
+  constexpr int NW = Acc<SOFT, LABELS>::NW;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-  const double unit = 1.0 / 4194304.0;           // 2^-22
-  const double unit2 = unit / 4194304.0;         // 2^-44
+  const double unit = 1.0 / 4194304.0;    // 2^-22
+  const double unit2 = unit / 4194304.0;  // 2^-44
   for (int e = warp; e < CL * slots; e += nwarps) {
-    unsigned* base = hist + (int64_t)e * NACC * R;
-    unsigned w[NACC];
+    unsigned* base = hist + ((int64_t)e * R + lane) * NW;
+    unsigned w[NW];
 #pragma unroll
-    for (int a = 0; a < NACC; ++a) w[a] = lane < R ? base[a * R + lane] : 0u;
+    for (int a = 0; a < NW; ++a) w[a] = lane < R ? base[a] : 0u;
+    if (lane < R) {
 #pragma unroll
-    for (int a = 0; a < NACC; ++a)
-      if (lane < R) base[a * R + lane] = 0u;
+      for (int a = 0; a < NW; ++a) base[a] = 0u;
+    }
     const unsigned n = w[0];
-    const unsigned ny = (SOFT && LABELS) ? w[7] : 0u;
     // per-lane exact value of a magic-offset word with `cnt` additions
     auto val = [&](unsigned raw, unsigned cnt) -> long long {
       return (long long)(int)(raw - cnt * kFixMagicBits);
+    };
+    auto pair = [&](int a, unsigned cnt) -> double {
+      const long long v = val(w[a], cnt) * 4194304ll + val(w[a + 1], cnt);
+      return (double)warp_sum_ll(v) * unit2;
     };
     double out[Acc<SOFT, LABELS>::NOUT];
     if constexpr (!SOFT) {
@@ -248,20 +258,17 @@ __device__ __forceinline__ void fold_table(unsigned* hist, int CL, int slots, in
       out[2] = LABELS ? (double)warp_sum_ll((long long)w[2])
                       : (double)warp_sum_ll(val(w[2], n)) * unit;
     } else {
-      auto pair = [&](int a, unsigned cnt) -> double {
-        const long long v = val(w[a], cnt) * 4194304ll + val(w[a + 1], cnt);
-        return (double)warp_sum_ll(v) * unit2;
-      };
       out[0] = (double)warp_sum_ll((long long)n);
       out[1] = pair(1, n);
       out[2] = pair(3, n);
-      out[3] = pair(5, n);
       if constexpr (LABELS) {
-        out[4] = (double)warp_sum_ll((long long)ny);
-        out[5] = pair(8, ny);
+        out[3] = (double)warp_sum_ll((long long)w[5]);
+        out[4] = pair(6, w[5]);
+        out[5] = 0.0;
       } else {
+        out[3] = pair(5, n);
         out[4] = pair(7, n);
-        out[5] = pair(9, n);
+        out[5] = 0.0;
       }
     }
     if (lane == 0) {
@@ -298,7 +305,7 @@ __device__ __forceinline__ int channels(int runtime_c) {
 // ---------------------------------------------------------------------------
 template <typename T, int V, int CM, bool SOFTMAX, bool SOFT, bool LABELS>
 __global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constant__ FwdParams P) {
-  constexpr int NACC = Acc<SOFT, LABELS>::NACC;
+  constexpr int NW = Acc<SOFT, LABELS>::NW;
   constexpr int NOUT = Acc<SOFT, LABELS>::NOUT;
   extern __shared__ __align__(16) float smem[];
   const int tid = threadIdx.x;
@@ -311,13 +318,13 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constan
 
   float2* pairs = reinterpret_cast<float2*>(smem);
   unsigned* hist = reinterpret_cast<unsigned*>(smem + 2 * (kMaxBins + 1));
-  const int table_words = CL * slots * NACC * R;
+  const int table_words = CL * slots * R * NW;
   for (int i = tid; i <= K; i += kHistThreads) pairs[i] = P.tab.pair[i];
   for (int i = tid; i < table_words; i += kHistThreads) hist[i] = 0u;
   __syncthreads();
 
-  const int col = tid & (R - 1);
-  const int slot_stride = NACC * R, row_stride = slots * slot_stride;
+  const int col = (tid & (R - 1)) * NW;
+  const int slot_stride = R * NW, row_stride = slots * slot_stride;
   const int64_t out_stride = (int64_t)P.B_total * CL * slots;
   const int64_t row0 = (int64_t)(P.b_offset + b) * CL;
 
@@ -325,62 +332,60 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constan
   const int64_t* lb = LABELS ? static_cast<const int64_t*>(P.target) + (int64_t)b * N : nullptr;
   const float* yb = LABELS ? nullptr : static_cast<const float*>(P.target) + (int64_t)b * C * N;
 
-  // One loss-channel value into the table; returns the slot index (-1: none) and
-  // the scaled right weight for the true-class target update.
+  // One loss-channel value into the table; returns the slot word index (-1:
+  // none) and the scaled u for the true-class target update.
   struct Upd {
     int a;
-    float ts;
+    float us;
   };
   auto update = [&](int row, float p, int j, float2 lohi, float y) -> Upd {
     Upd u;
     u.a = -1;
-    u.ts = 0.0f;
+    u.us = 0.0f;
     if constexpr (!SOFT) {
       if (j < K) {  // p above the last edge (only for invalid p > 1 + eps) is dropped
         const int a = row * row_stride + j * slot_stride + col;
         sadd(hist, a, 1u);
-        sadd(hist, a + R, fix1(p));
-        if constexpr (!LABELS) sadd(hist, a + 2 * R, fix1(y));
+        sadd(hist, a + 1, fix1(p));
+        if constexpr (!LABELS) sadd(hist, a + 2, fix1(y));
         u.a = a;
       }
     } else {
-      const float ld = ACE_FSUB(p, lohi.x);
-      const float rd = ACE_FSUB(lohi.y, p);
-      const float inv = ACE_FMUL(ace_rcp_approx(ACE_FADD(ld, rd)), kFixScale);
-      const float ts = fminf(ACE_FMUL(ld, inv), kFixScale);  // t * 2^22, t in [0, 1]
+      // u = (p - lo) / S in the interior, u = p in the two end intervals
+      const bool end = (j == 0) | (j == K);
+      const float base = end ? 0.0f : lohi.x;
+      const float scale = end ? kFixScale : ACE_FMUL(ace_rcp_approx(ACE_FSUB(lohi.y, lohi.x)), kFixScale);
+      const float us = fminf(ACE_FMUL(ACE_FSUB(p, base), scale), kFixScale);  // u * 2^22
       const int a = row * row_stride + j * slot_stride + col;
       sadd(hist, a, 1u);
-      const uint2 tw = fix2_scaled(ts);
-      sadd(hist, a + R, tw.x);
-      sadd(hist, a + 2 * R, tw.y);
-      const uint2 pw = fix2_prod(kFixScale, p);
-      sadd(hist, a + 3 * R, pw.x);
-      sadd(hist, a + 4 * R, pw.y);
-      const uint2 tpw = fix2_prod(ts, p);
-      sadd(hist, a + 5 * R, tpw.x);
-      sadd(hist, a + 6 * R, tpw.y);
+      const uint2 uw = fix2_scaled(us);
+      sadd(hist, a + 1, uw.x);
+      sadd(hist, a + 2, uw.y);
+      const uint2 qw = fix2_prod(us, ACE_FMUL(us, 1.0f / kFixScale));
+      sadd(hist, a + 3, qw.x);
+      sadd(hist, a + 4, qw.y);
       if constexpr (!LABELS) {
         const uint2 yw = fix2_prod(kFixScale, y);
-        sadd(hist, a + 7 * R, yw.x);
-        sadd(hist, a + 8 * R, yw.y);
-        const uint2 tyw = fix2_prod(ts, y);
-        sadd(hist, a + 9 * R, tyw.x);
-        sadd(hist, a + 10 * R, tyw.y);
+        sadd(hist, a + 5, yw.x);
+        sadd(hist, a + 6, yw.y);
+        const uint2 tyw = fix2_prod(us, y);
+        sadd(hist, a + 7, tyw.x);
+        sadd(hist, a + 8, tyw.y);
       }
       u.a = a;
-      u.ts = ts;
+      u.us = us;
     }
     return u;
   };
   auto true_update = [&](const Upd& u) {
     if (u.a < 0) return;
     if constexpr (!SOFT) {
-      sadd(hist, u.a + 2 * R, 1u);
+      sadd(hist, u.a + 2, 1u);
     } else {
-      sadd(hist, u.a + 7 * R, 1u);
-      const uint2 tw = fix2_scaled(u.ts);
-      sadd(hist, u.a + 8 * R, tw.x);
-      sadd(hist, u.a + 9 * R, tw.y);
+      sadd(hist, u.a + 5, 1u);
+      const uint2 tw = fix2_scaled(u.us);
+      sadd(hist, u.a + 6, tw.x);
+      sadd(hist, u.a + 7, tw.y);
     }
   };
 
@@ -417,13 +422,13 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constan
             if ((c > 0 || off == 0) && c < C) {
               j[c] = ace_guess(p[c], Kf, K, SOFT);
               lh[c] = pairs[j[c]];
-              ok &= ace_is_count(p[c], j[c], K, lh[c]);
+              ok &= ace_is_count(p[c], lh[c]);
             }
           }
           if (!ok) {
 #pragma unroll
             for (int c = 0; c < CM; ++c)
-              if ((c > 0 || off == 0) && c < C && !ace_is_count(p[c], j[c], K, lh[c])) {
+              if ((c > 0 || off == 0) && c < C && !ace_is_count(p[c], lh[c])) {
                 const Located r = ace_fix_count(p[c], j[c], K, pairs);
                 j[c] = r.i;
                 lh[c] = r.pr;
@@ -431,7 +436,7 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constan
           }
           Upd tu;
           tu.a = -1;
-          tu.ts = 0.0f;
+          tu.us = 0.0f;
 #pragma unroll
           for (int c = 0; c < CM; ++c) {
             if ((c > 0 || off == 0) && c < C) {
@@ -488,9 +493,12 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constan
   __threadfence();
 
   // Last CTA: the workspace sums become W, P, G per bin. Hard: slot = bin. Soft:
-  // interval j in 1..K-1 gives its 1 - t share to bin j-1 and its t share to bin
-  // j; intervals 0 and K give everything to bins 0 and K-1 (both neighbours are
-  // the end bin there), exactly as the reference's two scatters.
+  // interval j in 1..K-1 (between lo and hi = lo + S) gives bin j its t share,
+  //   W += sum t,  P += lo sum t + S sum t^2,  G += target sum t,
+  // and bin j-1 its 1 - t share,
+  //   W += n - sum t,  P += lo (n - sum t) + S (sum t - sum t^2),  G += ny - target sum t;
+  // intervals 0 and K give all of n, sum p, ny to bins 0 and K-1 (both
+  // neighbours are the end bin there), as the reference's two scatters.
   const int rows = P.B_total * CL;
   const int64_t stat_stride = (int64_t)rows * K;
   const bool stage = P.do_epilogue && 3 * stat_stride <= (int64_t)table_words;
@@ -506,18 +514,34 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constan
       pp = __ldcg(acc + out_stride + gi);
       g = __ldcg(acc + 2 * out_stride + gi);
     } else {
-      // bin k takes the t share of interval k and the 1 - t share of interval
-      // k + 1; an end interval (0 or K) gives it all of its moments
-      auto share = [&](int j, int a_all, int a_t) -> double {
+      w = pp = g = 0.0;
+      // j = k: the t share of interval k (all of it if k == 0)
+      // j = k + 1: the 1 - t share of interval k + 1 (all of it if k + 1 == K)
+      for (int side = 0; side < 2; ++side) {
+        const int j = k + side;
         const int64_t gi = r * slots + j;
-        const double all = __ldcg(acc + a_all * out_stride + gi);
-        if (j == 0 || j == K) return all;
-        const double tm = __ldcg(acc + a_t * out_stride + gi);
-        return j == k ? tm : all - tm;
-      };
-      w = share(k, 0, 1) + share(k + 1, 0, 1);
-      pp = share(k, 2, 3) + share(k + 1, 2, 3);
-      g = share(k, 4, 5) + share(k + 1, 4, 5);
+        const double n = __ldcg(acc + gi), su = __ldcg(acc + out_stride + gi);
+        const double ny = __ldcg(acc + 3 * out_stride + gi);
+        const double yu = __ldcg(acc + 4 * out_stride + gi);
+        if (j == 0 || j == K) {
+          w += n;
+          pp += su;
+          g += ny;
+          continue;
+        }
+        const double lo = P.tab.pair[j].x, span = (double)P.tab.pair[j].y - lo;
+        const double su2 = __ldcg(acc + 2 * out_stride + gi);
+        const double pt = lo * su + span * su2;  // sum t p
+        if (side == 0) {
+          w += su;
+          pp += pt;
+          g += yu;
+        } else {
+          w += n - su;
+          pp += lo * n + span * su - pt;
+          g += ny - yu;
+        }
+      }
     }
     const float wf = (float)w, pf = (float)pp, gf = (float)g;
     P.hist_out[e] = wf;
@@ -632,13 +656,13 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const __grid_constant__ 
           if ((c > 0 || off == 0) && c < C) {
             j[c] = ace_guess(p[c], Kf, K, SOFT);
             lh[c] = pairs[j[c]];
-            ok &= ace_is_count(p[c], j[c], K, lh[c]);
+            ok &= ace_is_count(p[c], lh[c]);
           }
         }
         if (!ok) {
 #pragma unroll
           for (int c = 0; c < CM; ++c)
-            if ((c > 0 || off == 0) && c < C && !ace_is_count(p[c], j[c], K, lh[c])) {
+            if ((c > 0 || off == 0) && c < C && !ace_is_count(p[c], lh[c])) {
               const Located r = ace_fix_count(p[c], j[c], K, pairs);
               j[c] = r.i;
               lh[c] = r.pr;
