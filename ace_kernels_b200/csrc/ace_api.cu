@@ -64,7 +64,9 @@ void table_values(int K, bool soft, float* out) {
 }
 
 // With `right`, every entry becomes the next float below it (nextafterf toward
-// -inf), so that the kernels' test t < p means t <= p for the true entry.
+// -inf), so that the kernels' test t < p means t <= p for the true entry. Soft
+// binning also gets each interval's base and scale (u = (p - base) * scale /
+// 2^22): interior intervals u = (p - lo) / (hi - lo), the end intervals u = p.
 void build_table(int K, bool soft, bool right, BinTable& t) {
   float v[kMaxBins];
   table_values(K, soft, v);
@@ -72,8 +74,12 @@ void build_table(int K, bool soft, bool right, BinTable& t) {
     for (int j = 0; j < K; ++j) v[j] = nextafterf(v[j], -INFINITY);
   t.K = K;
   for (int i = 0; i <= K; ++i) {
-    t.pair[i].x = i == 0 ? -10000.0f : v[i - 1];
-    t.pair[i].y = i == K ? 10000.0f : v[i];
+    float2& e = t.lohi[i];
+    e.x = i == 0 ? -10000.0f : v[i - 1];
+    e.y = i == K ? 10000.0f : v[i];
+    const bool end = i == 0 || i == K;
+    t.map[i].x = end ? 0.0f : e.x;
+    t.map[i].y = end ? 4194304.0f : (float)(4194304.0 / ((double)e.y - (double)e.x));
   }
 }
 
@@ -312,9 +318,9 @@ int hist_impl(const ace_b200_inputs* in, const ace_b200_options* opt, float* his
   // floor; above it, as many replicas as fit in ~100 KB (32 = conflict-free),
   // two CTAs per SM.
   const bool soft = opt->soft != 0;
-  const int words = soft ? 9 : 3;  // words per slot replica (odd: conflict-free)
+  const int words = soft ? (in->target_kind == ACE_B200_TARGET_LABELS ? 7 : 9) : 3;  // odd
   const int entries = CL * (soft ? K + 1 : K) * words;
-  const size_t table_bytes = 2 * (kMaxBins + 1) * sizeof(float);
+  const size_t table_bytes = (size_t)(K + 1) * kTabCopies * sizeof(float4);
   auto r_min = [&](int V) {
     int r = 1;
     while ((kHistThreads / r) * V > 511) r <<= 1;
@@ -474,8 +480,15 @@ int ace_b200_backward(const ace_b200_inputs* in, const ace_b200_options* opt,
   memset(&p, 0, sizeof(p));
   const Variant v = choose_variant(in, opt, dx);
   const bool soft = opt->soft != 0;
-  const int smem = (int)((size_t)(soft ? 16 : 4) * CL * (K + 1) + 8 + (size_t)(K + 1) * 8);
+  // Record copies: as many as fit in 96 KB (two CTAs per SM keep their tables).
+  int copies = soft ? 8 : 32;
+  auto grad_smem = [&](int c) {
+    return (size_t)(K + 1) * kTabCopies * sizeof(float4) + (size_t)(soft ? 16 : 4) * c * CL * (K + 1);
+  };
+  while (copies > 1 && grad_smem(copies) > 96 * 1024) copies /= 2;
+  const int smem = (int)grad_smem(copies);
   if (smem > 227 * 1024) return fail(ACE_B200_EUNSUPPORTED, "gradient tables do not fit");
+  p.rec_copies = copies;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
@@ -538,7 +551,7 @@ int ace_b200_bin_index_host(const float* p, int64_t n, int32_t num_bins, int32_t
   build_table(num_bins, soft != 0, right != 0, t);
   for (int64_t i = 0; i < n; ++i) {
     float2 lohi;
-    out[i] = ace_locate(p[i], t.pair, num_bins, (float)num_bins, soft != 0, lohi);
+    out[i] = ace_locate(p[i], t.lohi, 1, num_bins, (float)num_bins, soft != 0, lohi);
   }
   return ACE_B200_OK;
 }

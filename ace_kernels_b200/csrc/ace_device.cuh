@@ -63,55 +63,58 @@ static inline float ace_host_round(float v) {
 // within one of the answer because entry j is (j+1)/K (hard) or (j+0.5)/K (soft)
 // up to a few ulp, then a verified correction against the table itself. The
 // correction loop terminates after one or two passes; its bound only guards the
-// loop. The table is stored as pairs pair[i] = {t[i-1], t[i]} (sentinels at both
-// ends) so one 8-byte shared-memory load fetches both neighbours, which the soft
-// binning also needs as its interval ends.
+// loop. Entry i of the table holds {t[i-1], t[i]} (sentinels at both ends), so
+// one shared-memory load fetches both neighbours, which the soft binning also
+// needs as its interval ends.
 // ---------------------------------------------------------------------------
 // Guess of the count: round(p*n - 0.5) (hard) or round(p*n) (soft), via the
 // 1.5 * 2^23 bias (adding it leaves the nearest integer in the low mantissa
 // bits), so the guess costs FMA-pipe work only and no float<->int conversion.
-// Any guess within one of the answer is corrected by the search below; NaN and
-// out-of-range values are clamped to the table and corrected the same way.
+// Any guess within one of the answer is corrected by the search below. An
+// unsigned minimum clamps it to the table: negative guesses (NaN or negative p)
+// become n and are walked down by the slow path like any other wrong guess.
 __host__ __device__ __forceinline__ int ace_guess(float p, float nf, int n, bool soft) {
   const float g = soft ? ACE_FMUL(p, nf) : ACE_FSUB(ACE_FMUL(p, nf), 0.5f);
   const float b = ACE_FADD(g, 12582912.0f);
-  int i;
+  unsigned i;
 #ifdef __CUDA_ARCH__
-  i = __float_as_int(b) - 0x4B400000;
+  i = __float_as_uint(b) - 0x4B400000u;
 #else
   memcpy(&i, &b, sizeof(i));
-  i -= 0x4B400000;
+  i -= 0x4B400000u;
 #endif
-  return i < 0 ? 0 : (i > n ? n : i);
+  return (int)(i < (unsigned)n ? i : (unsigned)n);
 }
 
-// Is i the count for p, given pr = pair[i]? The table is `right`-adjusted, so
-// "entry counted" is always t < p, and its ends hold the -10000 / +10000
-// sentinels, which need no index test for -10000 < p < 10000 (a NaN or an
-// out-of-range value fails the test and takes the guarded slow path).
+// Is i the count for p, given its table neighbours pr = {t[i-1], t[i]}? The
+// table is `right`-adjusted, so "entry counted" is always t < p, and its ends
+// hold the -10000 / +10000 sentinels, which need no index test for
+// -10000 < p < 10000 (a NaN or an out-of-range value fails the test and takes
+// the guarded slow path).
 __host__ __device__ __forceinline__ bool ace_is_count(float p, float2 pr) {
   return pr.x < p && !(pr.y < p);
 }
 
+
 // Rare path: walk from a guess that failed ace_is_count to the count (one or two
 // steps for probabilities; the bound only guards against NaN / invalid input).
-// Returns the count and its pair by value, so the caller's registers never need
-// a memory address (a reference argument would force them to local memory).
+// Returns the count and its neighbours by value, so the caller's registers never
+// need a memory address (a reference argument would force them to local memory).
 struct Located {
   int i;
   float2 pr;
 };
 
 static __host__ __device__ __noinline__ Located ace_fix_count(float p, int i, int n,
-                                                              const float2* pair) {
-  float2 pr = pair[i];
+                                                              const float2* lohi, int stride) {
+  float2 pr = lohi[i * stride];
 #pragma unroll 1
   for (int it = 0; it <= n + 1; ++it) {
     const bool lo_ok = (i == 0) || pr.x < p;
     if (lo_ok && (i == n || !(pr.y < p))) break;
     i += lo_ok ? 1 : -1;
     i = i < 0 ? 0 : (i > n ? n : i);
-    pr = pair[i];
+    pr = lohi[i * stride];
   }
   Located r;
   r.i = i;
@@ -119,14 +122,14 @@ static __host__ __device__ __noinline__ Located ace_fix_count(float p, int i, in
   return r;
 }
 
-// The count j in [0, n] of table entries counted for p, and pair[j] =
-// {t[j-1], t[j]}. `pair` has n + 1 entries; nf = (float)n.
-__host__ __device__ __forceinline__ int ace_locate(float p, const float2* pair, int n, float nf,
-                                                   bool soft, float2& lohi) {
+// The count j in [0, n] of table entries counted for p, and its neighbours
+// {t[j-1], t[j]}. `lohi_tab` has n + 1 entries `stride` apart; nf = (float)n.
+__host__ __device__ __forceinline__ int ace_locate(float p, const float2* lohi_tab, int stride,
+                                                   int n, float nf, bool soft, float2& lohi) {
   int i = ace_guess(p, nf, n, soft);
-  float2 pr = pair[i];
+  float2 pr = lohi_tab[i * stride];
   if (!ace_is_count(p, pr)) {
-    const Located r = ace_fix_count(p, i, n, pair);
+    const Located r = ace_fix_count(p, i, n, lohi_tab, stride);
     i = r.i;
     pr = r.pr;
   }
@@ -223,21 +226,43 @@ struct VecIO {
   }
 };
 
-// V int64 class labels -> int32 (labels are class indices; values outside
-// [0, C) select no channel).
+// V int64 class labels -> int32. Labels are only compared with channel
+// indices (never used as addresses), so the low 32 bits suffice: a class index in
+// [0, C) selects its channel; the reference rejects other values, here they
+// select whatever channel their low bits name, or none.
 template <int V>
 __device__ __forceinline__ void ace_load_labels(const int64_t* __restrict__ p, int (&out)[V]) {
   if constexpr (V >= 2) {
 #pragma unroll
     for (int i = 0; i < V; i += 2) {
-      longlong2 a = __ldg(reinterpret_cast<const longlong2*>(p + i));
-      out[i] = (int)max(min(a.x, (long long)0x7fffffff), (long long)-1);
-      out[i + 1] = (int)max(min(a.y, (long long)0x7fffffff), (long long)-1);
+      const int4 a = __ldg(reinterpret_cast<const int4*>(p + i));
+      out[i] = a.x;  // little-endian: the low word first
+      out[i + 1] = a.z;
     }
   } else {
-    long long a = __ldg(reinterpret_cast<const long long*>(p));
-    out[0] = (int)max(min(a, (long long)0x7fffffff), (long long)-1);
+    out[0] = __ldg(reinterpret_cast<const int*>(p));
   }
+}
+
+// Asynchronous prefetch of [p, p + bytes) from HBM into L2 (no registers, no
+// completion to wait for). p and bytes must be multiples of 16; the range must lie
+// inside the allocation.
+__device__ __forceinline__ void ace_prefetch_l2(const void* p, unsigned bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Prefetches into L2 the part of a tile of `count` elements of `elem` bytes
+// starting at element `start` of a row of n elements at `row`: from the first
+// element if its address is 16-byte aligned (else nothing), up to the last
+// 16-byte boundary inside the row.
+__device__ __forceinline__ void ace_prefetch_tile(const void* row, int64_t start, int64_t count,
+                                                  int64_t n, int elem) {
+  if (start >= n) return;
+  const int64_t end = min(start + count, n);
+  const uintptr_t a0 = reinterpret_cast<uintptr_t>(row) + (uintptr_t)(start * elem);
+  const uintptr_t a1 = (reinterpret_cast<uintptr_t>(row) + (uintptr_t)(end * elem)) & ~(uintptr_t)15;
+  if ((a0 & 15) != 0 || a1 <= a0) return;
+  ace_prefetch_l2(reinterpret_cast<const void*>(a0), (unsigned)(a1 - a0));
 }
 
 // ---------------------------------------------------------------------------

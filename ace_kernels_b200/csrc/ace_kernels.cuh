@@ -175,9 +175,10 @@ __device__ __forceinline__ void write_loss_if0(const EpiParams& E, float total) 
 // whose NW words are contiguous, so the accumulator offsets are immediates and
 // the 32 lanes of a warp hit 32 different banks whatever their bins (R = 32).
 //   hard, slot = bin k (K slots), NW 3:  0 n, 1 p, 2 y (a count for labels)
-//   soft, slot = interval j (K+1 slots), NW 9:  0 n, 1-2 u, 3-4 u^2, then
-//        labels: 5 ny (true-class count), 6-7 u (true class), 8 unused;
-//        dense:  5-6 y, 7-8 u y
+//   soft, slot = interval j (K+1 slots):  0 n, 1-2 u, 3 u^2 (one word: it only
+//        enters P multiplied by the span, ~1/K), then
+//        labels (NW 7): 4 ny (true-class count), 5-6 u (true class);
+//        dense  (NW 9): 4-5 y, 6-7 u y, 8 unused
 // Interval j lies between bin centres lo = c_{j-1} and hi = c_j; there u = t =
 // (p - lo) / S with the interval's span S = hi - lo is the weight of the right
 // bin and 1 - t that of the left bin (ace_kernels/common.py:43-61), and p = lo +
@@ -188,8 +189,8 @@ __device__ __forceinline__ void write_loss_if0(const EpiParams& E, float total) 
 // ---------------------------------------------------------------------------
 template <bool SOFT, bool LABELS>
 struct Acc {
-  static constexpr int NW = SOFT ? 9 : 3;    // words per slot replica (odd)
-  static constexpr int NOUT = SOFT ? 6 : 3;  // global sums per slot
+  static constexpr int NW = SOFT ? (LABELS ? 7 : 9) : 3;  // words per slot replica (odd)
+  static constexpr int NOUT = SOFT ? 6 : 3;               // global sums per slot
 };
 
 constexpr float kFixScale = 4194304.0f;          // 2^22
@@ -260,16 +261,15 @@ __device__ __forceinline__ void fold_table(unsigned* hist, int CL, int slots, in
     } else {
       out[0] = (double)warp_sum_ll((long long)n);
       out[1] = pair(1, n);
-      out[2] = pair(3, n);
+      out[2] = (double)warp_sum_ll(val(w[3], n)) * unit;
       if constexpr (LABELS) {
-        out[3] = (double)warp_sum_ll((long long)w[5]);
-        out[4] = pair(6, w[5]);
-        out[5] = 0.0;
+        out[3] = (double)warp_sum_ll((long long)w[4]);
+        out[4] = pair(5, w[4]);
       } else {
-        out[3] = pair(5, n);
-        out[4] = pair(7, n);
-        out[5] = 0.0;
+        out[3] = pair(4, n);
+        out[4] = pair(6, n);
       }
+      out[5] = 0.0;
     }
     if (lane == 0) {
       const int row = e / slots, slot = e - row * slots;
@@ -316,10 +316,18 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constan
   const int R = P.R;
   const float Kf = (float)K;
 
-  float2* pairs = reinterpret_cast<float2*>(smem);
-  unsigned* hist = reinterpret_cast<unsigned*>(smem + 2 * (kMaxBins + 1));
+  // Bin tables in kTabCopies interleaved copies (lane l reads copy l % 16, so a
+  // warp's random-index gather is bank-conflict-free), then the statistics.
+  float2* lohi_t = reinterpret_cast<float2*>(smem);
+  float2* map_t = lohi_t + (K + 1) * kTabCopies;
+  unsigned* hist = reinterpret_cast<unsigned*>(map_t + (K + 1) * kTabCopies);
   const int table_words = CL * slots * R * NW;
-  for (int i = tid; i <= K; i += kHistThreads) pairs[i] = P.tab.pair[i];
+  for (int i = tid; i < (K + 1) * kTabCopies; i += kHistThreads) {
+    lohi_t[i] = P.tab.lohi[i / kTabCopies];
+    map_t[i] = P.tab.map[i / kTabCopies];
+  }
+  const float2* my_lohi = lohi_t + (tid & (kTabCopies - 1));
+  const float2* my_map = map_t + (tid & (kTabCopies - 1));
   for (int i = tid; i < table_words; i += kHistThreads) hist[i] = 0u;
   __syncthreads();
 
@@ -332,67 +340,70 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constan
   const int64_t* lb = LABELS ? static_cast<const int64_t*>(P.target) + (int64_t)b * N : nullptr;
   const float* yb = LABELS ? nullptr : static_cast<const float*>(P.target) + (int64_t)b * C * N;
 
-  // One loss-channel value into the table; returns the slot word index (-1:
-  // none) and the scaled u for the true-class target update.
-  struct Upd {
-    int a;
-    float us;
-  };
-  auto update = [&](int row, float p, int j, float2 lohi, float y) -> Upd {
-    Upd u;
-    u.a = -1;
-    u.us = 0.0f;
+  // One loss-channel value into the table, with its target: y (dense) or
+  // whether this channel is the voxel's class (labels).
+  auto update = [&](int row, float p, int j, float4 q, float y, bool is_true) {
     if constexpr (!SOFT) {
       if (j < K) {  // p above the last edge (only for invalid p > 1 + eps) is dropped
         const int a = row * row_stride + j * slot_stride + col;
         sadd(hist, a, 1u);
         sadd(hist, a + 1, fix1(p));
-        if constexpr (!LABELS) sadd(hist, a + 2, fix1(y));
-        u.a = a;
+        if constexpr (LABELS) {
+          if (is_true) sadd(hist, a + 2, 1u);
+        } else {
+          sadd(hist, a + 2, fix1(y));
+        }
       }
     } else {
-      // u = (p - lo) / S in the interior, u = p in the two end intervals
-      const bool end = (j == 0) | (j == K);
-      const float base = end ? 0.0f : lohi.x;
-      const float scale = end ? kFixScale : ACE_FMUL(ace_rcp_approx(ACE_FSUB(lohi.y, lohi.x)), kFixScale);
-      const float us = fminf(ACE_FMUL(ACE_FSUB(p, base), scale), kFixScale);  // u * 2^22
+      // u * 2^22, u = (p - lo) / S inside, u = p in the end intervals
+      const float us = fminf(ACE_FMUL(ACE_FSUB(p, q.z), q.w), kFixScale);
       const int a = row * row_stride + j * slot_stride + col;
       sadd(hist, a, 1u);
       const uint2 uw = fix2_scaled(us);
       sadd(hist, a + 1, uw.x);
       sadd(hist, a + 2, uw.y);
-      const uint2 qw = fix2_prod(us, ACE_FMUL(us, 1.0f / kFixScale));
-      sadd(hist, a + 3, qw.x);
-      sadd(hist, a + 4, qw.y);
-      if constexpr (!LABELS) {
+      sadd(hist, a + 3, __float_as_uint(__fmaf_rn(us, ACE_FMUL(us, 1.0f / kFixScale), kFixMagic)));
+      if constexpr (LABELS) {
+        if (is_true) {
+          sadd(hist, a + 4, 1u);
+          sadd(hist, a + 5, uw.x);
+          sadd(hist, a + 6, uw.y);
+        }
+      } else {
         const uint2 yw = fix2_prod(kFixScale, y);
-        sadd(hist, a + 5, yw.x);
-        sadd(hist, a + 6, yw.y);
-        const uint2 tyw = fix2_prod(us, y);
-        sadd(hist, a + 7, tyw.x);
-        sadd(hist, a + 8, tyw.y);
+        sadd(hist, a + 4, yw.x);
+        sadd(hist, a + 5, yw.y);
+        const uint2 uyw = fix2_prod(us, y);
+        sadd(hist, a + 6, uyw.x);
+        sadd(hist, a + 7, uyw.y);
       }
-      u.a = a;
-      u.us = us;
     }
-    return u;
   };
-  auto true_update = [&](const Upd& u) {
-    if (u.a < 0) return;
-    if constexpr (!SOFT) {
-      sadd(hist, u.a + 2, 1u);
+  // Table entry of count j: neighbours and, for soft binning, base / scale.
+  auto entry = [&](int j) -> float4 {
+    const float2 lh = my_lohi[j * kTabCopies];
+    if constexpr (SOFT) {
+      const float2 m = my_map[j * kTabCopies];
+      return make_float4(lh.x, lh.y, m.x, m.y);
     } else {
-      sadd(hist, u.a + 5, 1u);
-      const uint2 tw = fix2_scaled(u.us);
-      sadd(hist, u.a + 6, tw.x);
-      sadd(hist, u.a + 7, tw.y);
+      return make_float4(lh.x, lh.y, 0.0f, 0.0f);
     }
   };
 
   const int64_t t0 = (int64_t)blockIdx.x * P.g.tiles_per_chunk;
   const int64_t t1 = min(t0 + P.g.tiles_per_chunk, P.g.tiles);
   int since_fold = 0;
+  const int64_t tile = (int64_t)kHistThreads * V;
+  // L2 prefetch of the next tile (one thread per channel row and one for the
+  // labels), so the loads of the next iteration hit L2 instead of HBM
+  const bool pf_x = ((reinterpret_cast<uintptr_t>(xb) | (N * sizeof(T))) & 15) == 0;
   for (int64_t t = t0; t < t1; ++t) {
+    if (t + 1 < t1 && pf_x) {
+      if (tid < C) ace_prefetch_tile(xb + (int64_t)tid * N, (t + 1) * tile, tile, N, sizeof(T));
+      if constexpr (LABELS) {
+        if (tid == C) ace_prefetch_tile(lb, (t + 1) * tile, tile, N, 8);
+      }
+    }
     const int64_t v0 = (t * kHistThreads + tid) * V;
     if (v0 < N) {  // V > 1 implies N % V == 0: groups are whole
       int lab[V];
@@ -415,40 +426,33 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constan
           for (int c = 0; c < CM; ++c) p[c] = xv[c][i];
           ace_softmax<CM>(p, C);
           int j[CM];
-          float2 lh[CM];
+          float4 q[CM];
           bool ok = true;
 #pragma unroll
           for (int c = 0; c < CM; ++c) {
             if ((c > 0 || off == 0) && c < C) {
               j[c] = ace_guess(p[c], Kf, K, SOFT);
-              lh[c] = pairs[j[c]];
-              ok &= ace_is_count(p[c], lh[c]);
+              q[c] = entry(j[c]);
+              ok &= ace_is_count(p[c], make_float2(q[c].x, q[c].y));
             }
           }
           if (!ok) {
 #pragma unroll
             for (int c = 0; c < CM; ++c)
-              if ((c > 0 || off == 0) && c < C && !ace_is_count(p[c], lh[c])) {
-                const Located r = ace_fix_count(p[c], j[c], K, pairs);
-                j[c] = r.i;
-                lh[c] = r.pr;
+              if ((c > 0 || off == 0) && c < C &&
+                  !ace_is_count(p[c], make_float2(q[c].x, q[c].y))) {
+                j[c] = ace_fix_count(p[c], j[c], K, my_lohi, kTabCopies).i;
+                q[c] = entry(j[c]);
               }
           }
-          Upd tu;
-          tu.a = -1;
-          tu.us = 0.0f;
 #pragma unroll
           for (int c = 0; c < CM; ++c) {
             if ((c > 0 || off == 0) && c < C) {
               float y = 0.0f;
               if constexpr (!LABELS) y = yv[c][i];
-              const Upd u = update(c - off, p[c], j[c], lh[c], y);
-              if constexpr (LABELS) {
-                if (lab[i] == c) tu = u;
-              }
+              update(c - off, p[c], j[c], q[c], y, LABELS && lab[i] == c);
             }
           }
-          if constexpr (LABELS) true_update(tu);
         }
       } else {
         // none / sigmoid: channels are independent, one at a time
@@ -461,13 +465,10 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constan
           for (int i = 0; i < V; ++i) {
             const float p = P.act == ACE_B200_ACT_SIGMOID ? ace_sigmoid(xv[i]) : xv[i];
             float2 lh;
-            const int j = ace_locate(p, pairs, K, Kf, SOFT, lh);
+            const int j = ace_locate(p, my_lohi, kTabCopies, K, Kf, SOFT, lh);
             float y = 0.0f;
             if constexpr (!LABELS) y = yv[i];
-            const Upd u = update(c - off, p, j, lh, y);
-            if constexpr (LABELS) {
-              if (lab[i] == c) true_update(u);
-            }
+            update(c - off, p, j, entry(j), y, LABELS && lab[i] == c);
           }
         }
       }
@@ -529,7 +530,7 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constan
           g += ny;
           continue;
         }
-        const double lo = P.tab.pair[j].x, span = (double)P.tab.pair[j].y - lo;
+        const double lo = P.tab.lohi[j].x, span = (double)P.tab.lohi[j].y - lo;
         const double su2 = __ldcg(acc + 2 * out_stride + gi);
         const double pt = lo * su + span * su2;  // sum t p
         if (side == 0) {
@@ -575,17 +576,21 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constan
 // last bin); soft, one record per interval j, {g coef_l, d_l, g coef_r, d_r} of
 // its two bins, read with one 16-byte load. Hard binning reads no targets.
 // ---------------------------------------------------------------------------
+// q = table entry of the value's interval: {lo, hi, base, 2^22 / S} (soft).
+// Inside an interval the weights are rw = t = (p - lo) / S, lw = 1 - t and
+// d w / d p = -+ 1 / S; in an end interval both sides are the same bin, where the
+// formula reduces to g coef for any weights summing to 1 (there u = p, 1 / S = 1).
 template <bool SOFT>
-__device__ __forceinline__ float grad_p(const float* __restrict__ tab, int row, int K, int j,
-                                        float2 lohi, float p, float y) {
+__device__ __forceinline__ float grad_p(const float* __restrict__ tab, int copies, int row, int K,
+                                        int j, float4 q, float p, float y) {
+  // `tab` points at this lane's copy; entries are `copies` apart.
   if constexpr (!SOFT) {
-    return tab[row * (K + 1) + j];
+    return tab[(row * (K + 1) + j) * copies];
   } else {
-    const float4 rec = reinterpret_cast<const float4*>(tab)[row * (K + 1) + j];
-    const float ld = ACE_FSUB(p, lohi.x);
-    const float rd = ACE_FSUB(lohi.y, p);
-    const float inv = ace_rcp_approx(ACE_FADD(ld, rd));
-    const float lw = rd * inv, rw = ld * inv;
+    const float4 rec = reinterpret_cast<const float4*>(tab)[(row * (K + 1) + j) * copies];
+    const float inv = q.w * (1.0f / 4194304.0f);
+    const float rw = (p - q.z) * inv;
+    const float lw = 1.0f - rw;
     const float resid = p - y;
     return rec.x * (lw - inv * (resid - rec.y)) + rec.z * (rw + inv * (resid - rec.w));
   }
@@ -600,13 +605,23 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const __grid_constant__ 
   const int64_t N = P.g.N;
   const float Kf = (float)K;
 
-  float* tab = smem;  // [CL][K+1] floats (hard) or float4 (soft)
-  float2* pairs = reinterpret_cast<float2*>(smem + (SOFT ? 4 : 1) * CL * (K + 1) +
-                                            ((SOFT ? 0 : (CL * (K + 1)) & 1)));
+  // Tables in interleaved copies so that the lanes of one load phase rarely share
+  // banks (random-index gathers): the bin tables in kTabCopies copies, the
+  // per-row records in up to 8 copies (16-byte records, 8 lanes a phase) or the
+  // hard g coef table in up to 32 copies (4-byte values, 32 lanes a phase); the
+  // host lowers P.rec_copies (a power of two) when many rows would not fit.
+  float* tab = smem;  // [CL][K+1][copies] floats (hard) or float4 (soft)
+  const int rec_copies = P.rec_copies;
+  float2* lohi_t = reinterpret_cast<float2*>(tab + (SOFT ? 4 : 1) * CL * (K + 1) * rec_copies);
+  float2* map_t = lohi_t + (K + 1) * kTabCopies;
   const int64_t row0 = (int64_t)(P.b_offset + b) * CL;
-  for (int i = tid; i <= K; i += kThreads) pairs[i] = P.tab.pair[i];
-  for (int e = tid; e < CL * (K + 1); e += kThreads) {
-    const int row = e / (K + 1), j = e - row * (K + 1);
+  for (int i = tid; i < (K + 1) * kTabCopies; i += kThreads) {
+    lohi_t[i] = P.tab.lohi[i / kTabCopies];
+    map_t[i] = P.tab.map[i / kTabCopies];
+  }
+  for (int e = tid; e < CL * (K + 1) * rec_copies; e += kThreads) {
+    const int ej = e / rec_copies;
+    const int row = ej / (K + 1), j = ej - row * (K + 1);
     const float g = P.jac[row0 + row] * (P.grad_per_row ? P.grad_out[row0 + row] : P.grad_out[0]);
     const float* cf = P.coef + (row0 + row) * K;
     const float* dd = P.d + (row0 + row) * K;
@@ -618,6 +633,19 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const __grid_constant__ 
     }
   }
   __syncthreads();
+  const float* my_tab = tab + (SOFT ? 4 : 1) * (tid & (rec_copies - 1));
+  const float2* my_lohi = lohi_t + (tid & (kTabCopies - 1));
+  const float2* my_map = map_t + (tid & (kTabCopies - 1));
+
+  auto entry = [&](int j) -> float4 {
+    const float2 lh = my_lohi[j * kTabCopies];
+    if constexpr (SOFT) {
+      const float2 m = my_map[j * kTabCopies];
+      return make_float4(lh.x, lh.y, m.x, m.y);
+    } else {
+      return make_float4(lh.x, lh.y, 0.0f, 0.0f);
+    }
+  };
 
   const T* xb = static_cast<const T*>(P.x) + (int64_t)b * C * N;
   T* db = static_cast<T*>(P.dx) + (int64_t)b * C * N;
@@ -626,7 +654,15 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const __grid_constant__ 
 
   const int64_t t0 = (int64_t)blockIdx.x * P.g.tiles_per_chunk;
   const int64_t t1 = min(t0 + P.g.tiles_per_chunk, P.g.tiles);
+  const int64_t tile = (int64_t)kThreads * V;
+  const bool pf_x = ((reinterpret_cast<uintptr_t>(xb) | (N * sizeof(T))) & 15) == 0;
   for (int64_t t = t0; t < t1; ++t) {
+    if (t + 1 < t1 && pf_x) {  // L2 prefetch of the next tile
+      if (tid < C) ace_prefetch_tile(xb + (int64_t)tid * N, (t + 1) * tile, tile, N, sizeof(T));
+      if constexpr (SOFT && LABELS) {
+        if (tid == C) ace_prefetch_tile(lb, (t + 1) * tile, tile, N, 8);
+      }
+    }
     const int64_t v0 = (t * kThreads + tid) * V;
     if (v0 >= N) continue;
     int lab[V];
@@ -649,23 +685,22 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const __grid_constant__ 
         for (int c = 0; c < CM; ++c) p[c] = xv[c][i];
         ace_softmax<CM>(p, C);
         int j[CM];
-        float2 lh[CM];
+        float4 q[CM];
         bool ok = true;
 #pragma unroll
         for (int c = 0; c < CM; ++c) {
           if ((c > 0 || off == 0) && c < C) {
             j[c] = ace_guess(p[c], Kf, K, SOFT);
-            lh[c] = pairs[j[c]];
-            ok &= ace_is_count(p[c], lh[c]);
+            q[c] = entry(j[c]);
+            ok &= ace_is_count(p[c], make_float2(q[c].x, q[c].y));
           }
         }
         if (!ok) {
 #pragma unroll
           for (int c = 0; c < CM; ++c)
-            if ((c > 0 || off == 0) && c < C && !ace_is_count(p[c], lh[c])) {
-              const Located r = ace_fix_count(p[c], j[c], K, pairs);
-              j[c] = r.i;
-              lh[c] = r.pr;
+            if ((c > 0 || off == 0) && c < C && !ace_is_count(p[c], make_float2(q[c].x, q[c].y))) {
+              j[c] = ace_fix_count(p[c], j[c], K, my_lohi, kTabCopies).i;
+              q[c] = entry(j[c]);
             }
         }
         float gp[CM];
@@ -678,7 +713,7 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const __grid_constant__ 
               float y = 0.0f;
               if constexpr (SOFT && LABELS) y = (lab[i] == c) ? 1.0f : 0.0f;
               if constexpr (SOFT && !LABELS) y = yv[c][i];
-              gp[c] = grad_p<SOFT>(tab, c - off, K, j[c], lh[c], p[c], y);
+              gp[c] = grad_p<SOFT>(my_tab, rec_copies, c - off, K, j[c], q[c], p[c], y);
             }
             dot += p[c] * gp[c];
           }
@@ -710,8 +745,8 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const __grid_constant__ 
           if constexpr (SOFT && LABELS) y = (lab[i] == c) ? 1.0f : 0.0f;
           if constexpr (SOFT && !LABELS) y = yv[i];
           float2 lh;
-          const int j = ace_locate(p, pairs, K, Kf, SOFT, lh);
-          const float gp = grad_p<SOFT>(tab, c - off, K, j, lh, p, y);
+          const int j = ace_locate(p, my_lohi, kTabCopies, K, Kf, SOFT, lh);
+          const float gp = grad_p<SOFT>(my_tab, rec_copies, c - off, K, j, entry(j), p, y);
           xv[i] = sig ? gp * p * (1.0f - p) : gp;
         }
         VecIO<T, V>::store(db + (int64_t)c * N + v0, xv);

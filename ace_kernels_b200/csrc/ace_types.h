@@ -14,18 +14,24 @@ constexpr int kMaxBins = ACE_B200_MAX_BINS;        // num_bins limit of the kern
 constexpr int kMaxClasses = ACE_B200_MAX_CLASSES;  // channels limit of the kernels
 constexpr int kThreads = 256;                      // threads per CTA (gradient, epilogue)
 constexpr int kHistThreads = 512;                  // threads per CTA of the histogram
+constexpr int kTabCopies = 16;                     // interleaved copies of the bin tables
 
 // Sorted search table with its neighbours paired (see ace_locate): hard binning
-// uses the K upper bin edges, soft binning the K bin centres; pair[i] =
-// {t[i-1], t[i]} with -10000 / +10000 at the two ends (the reference's soft
-// sentinels, ace_reference/softl1ace.py:99-105). With `right` (count t <= p) each
-// entry is replaced by the next float below it, so the kernels always test
-// t < p: for finite floats, t <= p exactly when prev(t) < p.
+// uses the K upper bin edges, soft binning the K bin centres; entry i holds
+// {t[i-1], t[i]} and {base, scale}, with -10000 / +10000 at the two ends (the
+// reference's soft sentinels, ace_reference/softl1ace.py:99-105). With `right`
+// (count t <= p) each t is replaced by the next float below it, so the kernels
+// always test t < p: for finite floats, t <= p exactly when prev(t) < p. The two
+// halves are separate 8-byte tables (an 8-byte shared-memory gather by 32 lanes
+// with random indices conflicts far less than a 16-byte one).
+// Soft binning: interval i lies between t[i-1] and t[i]; base and scale map p to
+// the interval's coordinate u = (p - base) * scale / 2^22 (u = t, the right-bin
+// weight, inside; u = p in the two end intervals: base 0, scale 2^22).
 struct BinTable {
   int K;
-  float2 pair[kMaxBins + 1];
+  float2 lohi[kMaxBins + 1];  // {t[i-1], t[i]}
+  float2 map[kMaxBins + 1];   // {base, scale}
 };
-
 
 // Where one launch's voxels sit in the statistics: rows b_offset .. b_offset+B-1
 // of a [3, B_total, CL, K] buffer (batch sharding across ranks), and which slice
@@ -90,6 +96,7 @@ struct BwdParams {
   const float* jac;    // [B_total, CL]
   const float* grad_out;  // scalar, or [B_total, CL] when grad_per_row
   int grad_per_row;
+  int rec_copies;      // interleaved copies of the per-row records (power of two)
   BinTable tab;
 };
 
