@@ -28,6 +28,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libace_b200.so"
 # Values of the #defines in include/ace_b200.h.
 OK, EINVAL, EUNSUPPORTED, ECUDA = 0, -1, -2, -3
 MAX_BINS, MAX_CLASSES = 128, 64
+STATIC_SCRATCH_BYTES = 1 << 20
 F32, BF16, F16 = 0, 1, 2
 ACT_NONE, ACT_SOFTMAX, ACT_SIGMOID = 0, 1, 2
 TARGET_LABELS, TARGET_DENSE = 0, 1
@@ -80,6 +81,11 @@ SIGNATURES: list[tuple[str, object, list[object]]] = [
         "ace_b200_forward",
         c_int,
         [POINTER(Inputs), POINTER(Options), c_void_p, EpilogueOut, c_void_p, c_size_t, c_void_p],
+    ),
+    (
+        "ace_b200_forward_static",
+        c_int,
+        [POINTER(Inputs), POINTER(Options), c_void_p, EpilogueOut, c_void_p],
     ),
     (
         "ace_b200_hist",

@@ -418,6 +418,41 @@ cudaError_t launch_epilogue(const float* hist, const EpiParams& e, unsigned* cou
   return cudaGetLastError();
 }
 
+// Scratch of ace_b200_forward_static. A __device__ array has one instance per
+// device context, created when the module loads; the first call on each device
+// looks its address up (cudaGetSymbolAddress may load the module lazily, which a
+// capturing stream does not allow) and clears it (the accumulators and the two
+// counters must start at zero; every call leaves them zero again).
+__device__ __align__(256) unsigned char g_static_scratch[ACE_B200_STATIC_SCRATCH_BYTES];
+
+std::mutex g_static_mu;
+void* g_static_ptr[64];
+
+int static_scratch(cudaStream_t s, void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(ACE_B200_EUNSUPPORTED, "device %d >= 64", dev);
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  if (!g_static_ptr[dev]) {
+    cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+    e = cudaStreamIsCapturing(s, &st);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamIsCapturing");
+    if (st != cudaStreamCaptureStatusNone)
+      return fail(ACE_B200_EINVAL,
+                  "the first ace_b200_forward_static call on device %d is being captured: "
+                  "make one call outside stream capture first", dev);
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress((void**)&ptr, g_static_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress");
+    e = cudaMemsetAsync(ptr, 0, ACE_B200_STATIC_SCRATCH_BYTES, s);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync of the static scratch");
+    g_static_ptr[dev] = ptr;
+  }
+  *out = g_static_ptr[dev];
+  return ACE_B200_OK;
+}
+
 }  // namespace ace
 
 using namespace ace;
@@ -434,6 +469,24 @@ int ace_b200_forward(const ace_b200_inputs* in, const ace_b200_options* opt, flo
                      ace_b200_epilogue_out out, void* workspace, size_t workspace_bytes,
                      void* stream) {
   return hist_impl(in, opt, hist, &out, workspace, workspace_bytes, stream);
+}
+
+int ace_b200_forward_static(const ace_b200_inputs* in, const ace_b200_options* opt, float* hist,
+                            ace_b200_epilogue_out out, void* stream) {
+  int CL = 0;
+  int rc = check_common(in, opt, CL);
+  if (rc) return rc;
+  const size_t need = ace_b200_workspace_bytes(in->b_total, CL, opt->num_bins);
+  if (need > ACE_B200_STATIC_SCRATCH_BYTES)
+    return fail(ACE_B200_EUNSUPPORTED,
+                "b_total=%lld x %d classes x %d bins needs %zu bytes of scratch, more than the "
+                "%d of the static scratch: use ace_b200_forward with a workspace",
+                (long long)in->b_total, CL, opt->num_bins, need, ACE_B200_STATIC_SCRATCH_BYTES);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  void* scratch = nullptr;
+  rc = static_scratch(s, &scratch);
+  if (rc) return rc;
+  return hist_impl(in, opt, hist, &out, scratch, ACE_B200_STATIC_SCRATCH_BYTES, stream);
 }
 
 int ace_b200_hist(const ace_b200_inputs* in, const ace_b200_options* opt, float* hist,

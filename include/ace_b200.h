@@ -142,6 +142,28 @@ int ace_b200_forward(const ace_b200_inputs* in, const ace_b200_options* opt, flo
                      void* stream);
 
 /*
+ * ace_b200_forward without a workspace: the scratch (accumulators and counters)
+ * is a fixed device array inside the library, ACE_B200_STATIC_SCRATCH_BYTES per
+ * device. No counterpart in the reference, which allocates its scratch through
+ * torch on every call. It serves callers that cannot hand over device memory: a
+ * host binding the library through its C ABI alone, with no device allocator
+ * of its own, or one whose allocator may not run inside its step loop. This
+ * call allocates nothing and calls no allocating function.
+ *   - Limit: ace_b200_workspace_bytes(b_total, C - offset, num_bins) must not
+ *     exceed ACE_B200_STATIC_SCRATCH_BYTES (about b_total * (C - offset) <= 1000
+ *     rows at K = 20); larger calls fail with ACE_B200_EUNSUPPORTED.
+ *   - Setup: the first call on each device looks the array up and clears it on
+ *     `stream`; it must not run under stream capture (it then fails with
+ *     ACE_B200_EINVAL).
+ *   - The scratch is shared by every call on a device: two calls whose kernels
+ *     may overlap (different streams without ordering between them, or two
+ *     threads) race on it and give wrong results. Order them on one stream.
+ */
+#define ACE_B200_STATIC_SCRATCH_BYTES 1048576 /* 1 MiB */
+int ace_b200_forward_static(const ace_b200_inputs* in, const ace_b200_options* opt, float* hist,
+                            ace_b200_epilogue_out out, void* stream);
+
+/*
  * Statistics only (the first half of ace_b200_forward), for callers that reduce
  * the statistics across ranks (NCCL all-reduce of `hist`) before the epilogue.
  * Replaces hard_hist_fused / soft_hist_fused (ace_kernels/kernels/hard_hist.py:186-233,
