@@ -104,8 +104,6 @@ def run_reference(args: argparse.Namespace) -> None:
     from ace_kernels_b200 import workloads as wl
 
     w = wl.WORKLOADS[args.workload]
-    for _ in range(max(0, min(args.warmup, 3))):
-        pass
     res = cpu_reference(w, w.config, seconds=120.0, max_steps=max(1, args.steps))
     line = {
         "metric": METRIC, "value": res["value"], "unit": UNIT, "n_gpus": args.gpus,
