@@ -66,7 +66,7 @@ void table_values(int K, bool soft, float* out) {
 // With `right`, every entry becomes the next float below it (nextafterf toward
 // -inf), so that the kernels' test t < p means t <= p for the true entry. Soft
 // binning also gets each interval's base and scale (u = (p - base) * scale /
-// 2^22): interior intervals u = (p - lo) / (hi - lo), the end intervals u = p.
+// 2^21): interior intervals u = (p - lo) / (hi - lo), the end intervals u = p.
 void build_table(int K, bool soft, bool right, BinTable& t) {
   float v[kMaxBins];
   table_values(K, soft, v);
@@ -79,7 +79,7 @@ void build_table(int K, bool soft, bool right, BinTable& t) {
     e.y = i == K ? 10000.0f : v[i];
     const bool end = i == 0 || i == K;
     t.map[i].x = end ? 0.0f : e.x;
-    t.map[i].y = end ? 4194304.0f : (float)(4194304.0 / ((double)e.y - (double)e.x));
+    t.map[i].y = end ? kFixScale : (float)((double)kFixScale / ((double)e.y - (double)e.x));
   }
 }
 
@@ -243,10 +243,14 @@ Variant choose_variant(const ace_b200_inputs* in, const ace_b200_options* opt, c
   return v;
 }
 
-// One wave of CTAs, split over the batches; each CTA gets a contiguous run of
-// tiles of one batch.
+// One wave of CTAs over the tiles of all batches. Per-batch chunks (each CTA a
+// contiguous run of one batch's tiles): always when `flat` is false (the
+// gradient: grid (chunks_per_batch, B)), and for the histogram (1-D grid) when a
+// wave of them is as short as the flat split; else flat: the tiles of all
+// batches in one sequence, each CTA a contiguous run that may cross a batch
+// boundary, so that no SM runs a second CTA when B does not divide the wave.
 Grid make_grid(const ace_b200_inputs* in, int CL, int offset, int V, int threads,
-               int ctas_per_sm, int dev) {
+               int ctas_per_sm, int dev, bool flat) {
   Grid g;
   g.N = in->N;
   g.B = (int)in->B;
@@ -255,13 +259,32 @@ Grid make_grid(const ace_b200_inputs* in, int CL, int offset, int V, int threads
   g.offset = offset;
   const int64_t tile = (int64_t)threads * V;
   g.tiles = (in->N + tile - 1) / tile;
-  const int64_t wave = (int64_t)sm_count(dev) * ctas_per_sm;
-  int64_t chunks = (wave + g.B - 1) / g.B;
-  if (chunks > g.tiles) chunks = g.tiles;
+  const int64_t wave = (int64_t)sm_count(dev) * (ctas_per_sm > 0 ? ctas_per_sm : 1);
+  g.chunks_per_batch = 0;
+  const int64_t total = g.B * g.tiles;
+  const int64_t cb = wave / g.B > 0 ? wave / g.B : 1;
+  if (!flat && g.tiles == 0) {  // nothing to do: one CTA per batch
+    g.tiles_per_chunk = 1;
+    g.chunks_per_batch = 1;
+    g.chunks = g.B;
+    return g;
+  }
+  if (g.tiles > 0 && (!flat || wave / g.B >= 1)) {
+    const int64_t c = cb < g.tiles ? cb : g.tiles;
+    const int64_t tpc = (g.tiles + c - 1) / c;
+    if (!flat || tpc <= (total + wave - 1) / wave) {
+      g.tiles_per_chunk = tpc;
+      g.chunks_per_batch = (int)((g.tiles + tpc - 1) / tpc);
+      g.chunks = g.chunks_per_batch * g.B;
+      return g;
+    }
+  }
+  int64_t chunks = wave;
+  if (chunks > total) chunks = total;
   if (chunks < 1) chunks = 1;
-  g.tiles_per_chunk = (g.tiles + chunks - 1) / chunks;
+  g.tiles_per_chunk = (total + chunks - 1) / chunks;
   if (g.tiles_per_chunk < 1) g.tiles_per_chunk = 1;
-  chunks = (g.tiles + g.tiles_per_chunk - 1) / g.tiles_per_chunk;
+  chunks = (total + g.tiles_per_chunk - 1) / g.tiles_per_chunk;
   if (chunks < 1) chunks = 1;
   g.chunks = (int)chunks;
   return g;
@@ -314,7 +337,7 @@ int hist_impl(const ace_b200_inputs* in, const ace_b200_options* opt, float* his
   Variant v = choose_variant(in, opt, nullptr);
   // Shared-memory table: `entries` words per lane replica. A 32-bit word of a
   // replica takes at most (kHistThreads / R) * V additions per tile and must not
-  // take more than 511 between two folds (values up to 2^22 each), so R has a
+  // take more than 1023 between two folds (values up to 2^21 each), so R has a
   // floor; above it, as many replicas as fit in ~100 KB (32 = conflict-free),
   // two CTAs per SM.
   const bool soft = opt->soft != 0;
@@ -323,7 +346,7 @@ int hist_impl(const ace_b200_inputs* in, const ace_b200_options* opt, float* his
   const size_t table_bytes = (size_t)(K + 1) * kTabCopies * sizeof(float4);
   auto r_min = [&](int V) {
     int r = 1;
-    while ((kHistThreads / r) * V > 511) r <<= 1;
+    while ((kHistThreads / r) * V > 1023) r <<= 1;
     return r;
   };
   if (table_bytes + (size_t)entries * r_min(v.V) * 4 > 200 * 1024) v.V = 1;
@@ -340,11 +363,11 @@ int hist_impl(const ace_b200_inputs* in, const ace_b200_options* opt, float* his
   const int occ = occupancy(0, in->x_dtype, v, smem, dev);
   p.x = in->x;
   p.target = in->target;
-  p.g = make_grid(in, CL, opt->offset, v.V, kHistThreads, occ, dev);
+  p.g = make_grid(in, CL, opt->offset, v.V, kHistThreads, occ, dev, true);
   p.act = opt->activation;
   p.soft = soft;
   p.R = R;
-  p.flush_tiles = 511 / ((kHistThreads / R) * v.V);
+  p.flush_tiles = 1023 / ((kHistThreads / R) * v.V);
   p.b_offset = (int)in->b_offset;
   p.B_total = (int)in->b_total;
   const Workspace w = carve(workspace, in->b_total, CL, K);
@@ -360,7 +383,7 @@ int hist_impl(const ace_b200_inputs* in, const ace_b200_options* opt, float* his
   const bool fused = out && stats <= (int64_t)entries * R && rows <= 8 * kEpiRowsPerCta;
   p.do_epilogue = fused ? 1 : 0;
 
-  const dim3 grid((unsigned)p.g.chunks, (unsigned)p.g.B);
+  const dim3 grid((unsigned)p.g.chunks, 1u);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (in->x_dtype == ACE_B200_F32) e = launch_hist<float>(p, v, grid, smem, s);
   else if (in->x_dtype == ACE_B200_BF16) e = launch_hist<__nv_bfloat16>(p, v, grid, smem, s);
@@ -549,7 +572,7 @@ int ace_b200_backward(const ace_b200_inputs* in, const ace_b200_options* opt,
   p.x = in->x;
   p.target = in->target;
   p.dx = dx;
-  p.g = make_grid(in, CL, opt->offset, v.V, kThreads, occ, dev);
+  p.g = make_grid(in, CL, opt->offset, v.V, kThreads, occ, dev, false);
   p.act = opt->activation;
   p.soft = soft;
   p.b_offset = (int)in->b_offset;
@@ -559,7 +582,7 @@ int ace_b200_backward(const ace_b200_inputs* in, const ace_b200_options* opt,
   p.grad_out = grad_output;
   p.grad_per_row = grad_per_row != 0;
   build_table(K, soft, opt->right != 0, p.tab);
-  const dim3 grid((unsigned)p.g.chunks, (unsigned)p.g.B);
+  const dim3 grid((unsigned)p.g.chunks_per_batch, (unsigned)p.g.B);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (in->x_dtype == ACE_B200_F32) e = launch_grad<float>(p, v, grid, smem, s);
   else if (in->x_dtype == ACE_B200_BF16) e = launch_grad<__nv_bfloat16>(p, v, grid, smem, s);

@@ -160,16 +160,16 @@ __device__ __forceinline__ void write_loss_if0(const EpiParams& E, float total) 
 //
 // Values are accumulated with native 32-bit integer shared-memory atomics (a
 // float atomic add there is a compare-and-swap loop, measured 3x slower). A
-// value v in [0, 1] is added as the bit pattern of the float v * 2^22 +
-// 1.5 * 2^23, which equals 0x4B400000 + round(v * 2^22): FMA-pipe instructions
+// value v in [0, 1] is added as the bit pattern of the float v * 2^21 +
+// 1.5 * 2^23, which equals 0x4B400000 + round(v * 2^21): FMA-pipe instructions
 // only, no conversion instruction. Each slot also counts its additions (n), so
 // its sum of patterns minus n * 0x4B400000 (mod 2^32) is the exact sum of the
 // rounded values. Where sums of a few small values matter (soft binning), every
-// value is split in two words, hi = round(v * 2^22) and lo = round((v * 2^22 -
-// hi) * 2^22): an absolute precision of 2^-45 per value. The CTA folds its table
-// into the workspace before any 32-bit word could overflow (every `flush_tiles`
-// tiles) and at the end; the sums are integers, so they do not depend on the
-// order of the additions.
+// value is split in two words, hi = round(v * 2^21) and lo = round((v * 2^21 -
+// hi) * 2^21): an absolute precision of 2^-43 per value. A word takes at most
+// 1023 additions between two folds (1023 * 2^21 < 2^31); the CTA folds its table
+// into the workspace every `flush_tiles` tiles and at the end. The sums are
+// integers, so they do not depend on the order of the additions.
 //
 // Layout [row][slot][R][NW] 32-bit words, NW odd: lane l updates replica l % R,
 // whose NW words are contiguous, so the accumulator offsets are immediates and
@@ -190,22 +190,22 @@ __device__ __forceinline__ void write_loss_if0(const EpiParams& E, float total) 
 template <bool SOFT, bool LABELS>
 struct Acc {
   static constexpr int NW = SOFT ? (LABELS ? 7 : 9) : 3;  // words per slot replica (odd)
-  static constexpr int NOUT = SOFT ? 6 : 3;               // global sums per slot
+  static constexpr int NOUT = SOFT ? 6 : 3;               // global sums per slot (stride)
+  static constexpr int NFOLD = SOFT ? 5 : 3;              // global sums per slot (used)
 };
 
-constexpr float kFixScale = 4194304.0f;          // 2^22
 constexpr float kFixMagic = 12582912.0f;         // 1.5 * 2^23
 constexpr unsigned kFixMagicBits = 0x4B400000u;  // bits of kFixMagic
 
 __device__ __forceinline__ void sadd(unsigned* h, int a, unsigned v) { atomicAdd(h + a, v); }
 
-// Bit patterns of the hi and lo words of v * 2^22 = vs (already scaled).
+// Bit patterns of the hi and lo words of v * 2^21 = vs (already scaled).
 __device__ __forceinline__ uint2 fix2_scaled(float vs) {
   const float hb = __fadd_rn(vs, kFixMagic);
   const float r = __fsub_rn(vs, __fsub_rn(hb, kFixMagic));  // exact residual, |r| <= 1/2
   return make_uint2(__float_as_uint(hb), __float_as_uint(__fmaf_rn(r, kFixScale, kFixMagic)));
 }
-// Same for a product a * b (a scaled by 2^22): one rounding for hi, exact residual.
+// Same for a product a * b (a scaled by 2^21): one rounding for hi, exact residual.
 __device__ __forceinline__ uint2 fix2_prod(float as, float b) {
   const float hb = __fmaf_rn(as, b, kFixMagic);
   const float r = __fmaf_rn(as, b, -__fsub_rn(hb, kFixMagic));
@@ -215,70 +215,75 @@ __device__ __forceinline__ unsigned fix1(float v) {
   return __float_as_uint(__fmaf_rn(v, kFixScale, kFixMagic));
 }
 
-__device__ __forceinline__ long long warp_sum_ll(long long v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
-
-// Folds this CTA's table into the workspace (double sums, one global atomic per
-// non-zero sum) and clears it: one warp per slot, lane l reading replica l
-// (conflict-free: NW is odd), exact integer warp reductions. Global sums per
-// slot: hard (n, sum p, sum y); soft (n, sum u, sum u^2, target count or sum y,
-// target sum u, [dense: sum u y]) as laid out in fold_out below. Called by all
-// threads between barriers.
+// Folds this CTA's table into the workspace and clears it. Each global sum of a
+// slot (hard: n, sum p, target count or sum y; soft: n, sum u, sum u^2, target
+// count or sum y, target sum u or sum u y) is taken by a group of G = 4
+// consecutive lanes (1 if R < 4): each adds R / G of the replicas exactly in
+// 64-bit integers, in an order rotated by the slot (spreading a warp's reads over
+// the banks), the group adds its parts with shuffles and its first lane issues
+// one fp64 atomic add; then the table is zeroed. A fixed-point word w with cnt
+// additions holds the exact value (int)(w - cnt * 0x4B400000); count words hold
+// their value. The word selection is branch-free, so the lanes of a warp, which
+// take different sums, do not diverge. Called by all threads between barriers.
 template <bool SOFT, bool LABELS>
 __device__ __forceinline__ void fold_table(unsigned* hist, int CL, int slots, int R,
                                            double* accum, int64_t out_stride, int64_t row0) {
   constexpr int NW = Acc<SOFT, LABELS>::NW;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-  const double unit = 1.0 / 4194304.0;    // 2^-22
-  const double unit2 = unit / 4194304.0;  // 2^-44
-  for (int e = warp; e < CL * slots; e += nwarps) {
-    unsigned* base = hist + ((int64_t)e * R + lane) * NW;
-    unsigned w[NW];
-#pragma unroll
-    for (int a = 0; a < NW; ++a) w[a] = lane < R ? base[a] : 0u;
-    if (lane < R) {
-#pragma unroll
-      for (int a = 0; a < NW; ++a) base[a] = 0u;
-    }
-    const unsigned n = w[0];
-    // per-lane exact value of a magic-offset word with `cnt` additions
-    auto val = [&](unsigned raw, unsigned cnt) -> long long {
-      return (long long)(int)(raw - cnt * kFixMagicBits);
-    };
-    auto pair = [&](int a, unsigned cnt) -> double {
-      const long long v = val(w[a], cnt) * 4194304ll + val(w[a + 1], cnt);
-      return (double)warp_sum_ll(v) * unit2;
-    };
-    double out[Acc<SOFT, LABELS>::NOUT];
+  constexpr int NF = Acc<SOFT, LABELS>::NFOLD;
+  const int G = R >= 4 ? 4 : 1;
+  const int per = R / G;
+  const double unit = 1.0 / (double)kFixScale;
+  const int total = CL * slots * NF * G;
+  for (int i0 = 0; i0 < total; i0 += blockDim.x) {  // uniform trip count: full-warp shuffles
+    const int i = i0 + threadIdx.x;
+    const bool valid = i < total;
+    const int out = valid ? i / G : 0, part = i - (i / G) * G;
+    const int e = out / NF, o = out - e * NF;
+    // cw: word counting the value's additions (-1: the value is a count); a, b:
+    // its words (b < 0: one word)
+    int cw, a, b;
     if constexpr (!SOFT) {
-      out[0] = (double)warp_sum_ll((long long)n);
-      out[1] = (double)warp_sum_ll(val(w[1], n)) * unit;
-      out[2] = LABELS ? (double)warp_sum_ll((long long)w[2])
-                      : (double)warp_sum_ll(val(w[2], n)) * unit;
-    } else {
-      out[0] = (double)warp_sum_ll((long long)n);
-      out[1] = pair(1, n);
-      out[2] = (double)warp_sum_ll(val(w[3], n)) * unit;
-      if constexpr (LABELS) {
-        out[3] = (double)warp_sum_ll((long long)w[4]);
-        out[4] = pair(5, w[4]);
-      } else {
-        out[3] = pair(4, n);
-        out[4] = pair(6, n);
-      }
-      out[5] = 0.0;
+      cw = o == 0 || (o == 2 && LABELS) ? -1 : 0;
+      a = o;
+      b = -1;
+    } else if constexpr (LABELS) {  // words: 0 n, 1-2 u, 3 u^2, 4 ny, 5-6 u (true class)
+      cw = (o == 0 || o == 3) ? -1 : (o == 4 ? 4 : 0);
+      a = o == 0 ? 0 : o == 1 ? 1 : o == 2 ? 3 : o == 3 ? 4 : 5;
+      b = o == 1 ? 2 : o == 4 ? 6 : -1;
+    } else {  // words: 0 n, 1-2 u, 3 u^2, 4-5 y, 6-7 u y
+      cw = o == 0 ? -1 : 0;
+      a = o == 0 ? 0 : o == 1 ? 1 : o == 2 ? 3 : o == 3 ? 4 : 6;
+      b = o == 1 ? 2 : o == 3 ? 5 : o == 4 ? 7 : -1;
     }
-    if (lane == 0) {
+    const unsigned mul = cw < 0 ? 0u : kFixMagicBits;
+    const int cwi = cw < 0 ? a : cw, bi = b < 0 ? a : b;
+    const long long hs = b < 0 ? 1ll : (long long)kFixScale;
+    const unsigned* base = hist + (int64_t)e * R * NW;
+    long long acc = 0;
+    if (valid) {
+      for (int k = 0; k < per; ++k) {
+        const unsigned* w = base + ((part * per + k + e) & (R - 1)) * NW;
+        const unsigned offv = w[cwi] * mul;
+        const long long hi = cw < 0 ? (long long)w[a] : (long long)(int)(w[a] - offv);
+        const long long lo = b < 0 ? 0ll : (long long)(int)(w[bi] - offv);
+        acc += hi * hs + lo;
+      }
+    }
+    if (G == 4) {
+      acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+      acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+    }
+    if (valid && part == 0 && acc != 0) {
+      const double scale = cw < 0 ? 1.0 : (b >= 0 ? unit * unit : unit);
       const int row = e / slots, slot = e - row * slots;
-      const int64_t gi = (row0 + row) * slots + slot;
-#pragma unroll
-      for (int a = 0; a < Acc<SOFT, LABELS>::NOUT; ++a)
-        if (out[a] != 0.0) atomicAdd(accum + a * out_stride + gi, out[a]);
+      atomicAdd(accum + o * out_stride + (row0 + row) * slots + slot, (double)acc * scale);
     }
   }
+  __syncthreads();
+  const int words = CL * slots * R * NW;
+  uint4* h4 = reinterpret_cast<uint4*>(hist);
+  for (int i = threadIdx.x; i < words / 4; i += blockDim.x) h4[i] = make_uint4(0u, 0u, 0u, 0u);
+  for (int i = (words & ~3) + threadIdx.x; i < words; i += blockDim.x) hist[i] = 0u;
 }
 
 // Channel count of a kernel instance: exact for softmax instances with CM <= 4
@@ -289,19 +294,36 @@ __device__ __forceinline__ int channels(int runtime_c) {
   return (SOFTMAX && CM <= 4) ? CM : runtime_c;
 }
 
+// Tiles [g0, g1) of CTA blockIdx.x (see the forward's comment).
+__device__ __forceinline__ void chunk_range(const Grid& G, int64_t& g0, int64_t& g1) {
+  const int64_t tpc = G.tiles_per_chunk;
+  if (G.chunks_per_batch > 0) {
+    const int cb = G.chunks_per_batch;
+    const int bx = (int)blockIdx.x / cb;
+    g0 = bx * G.tiles + (int64_t)((int)blockIdx.x - bx * cb) * tpc;
+    g1 = min(g0 + tpc, (bx + 1) * G.tiles);
+  } else {
+    g0 = (int64_t)blockIdx.x * tpc;
+    g1 = min(g0 + tpc, (int64_t)G.B * G.tiles);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Forward: fused activation + W/P/G statistics (+ epilogue in the last CTA).
 //
-// Grid (chunks, B), kHistThreads threads: CTA (x, b) streams tiles
-// [x * tpc, (x + 1) * tpc) of batch b; a tile is kHistThreads * V voxels and
-// thread t owns V consecutive voxels of it, read with 16-byte (V * sizeof(T))
+// Tiles of kHistThreads * V voxels are numbered over all batches (tile g is tile
+// g % tpb of batch g / tpb); a 1-D grid of one wave, CTA x streams tiles
+// [g0, g1): chunk x % cb of batch x / cb when the host chose chunks_per_batch =
+// cb > 0, else run x of the whole sequence, which may cross into the next batch
+// (the CTA then folds its table before it takes the next batch's rows). Thread t
+// owns V consecutive voxels of a tile, read with 16-byte (V * sizeof(T))
 // coalesced loads per channel (the channel stride is N). The logits of all C
 // channels of a voxel are in registers, so the softmax needs no second read. Per
 // voxel the bins of all loss channels are located first (one shared-memory load
-// each, straight-line), a rare fix-up pass corrects guesses off by one, then the
-// table updates are issued; the true class's target updates are issued once per
-// voxel. The last CTA to finish (counter in the workspace, no waiting) turns the
-// workspace sums into W, P, G, resets the workspace and runs the epilogue.
+// each, straight-line), then the table updates are issued; the true class's
+// target updates are issued once per voxel. The last CTA to finish (a ticket in
+// the workspace, no waiting) turns the workspace sums into W, P, G, resets the
+// workspace and runs the epilogue.
 // ---------------------------------------------------------------------------
 template <typename T, int V, int CM, bool SOFTMAX, bool SOFT, bool LABELS>
 __global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constant__ FwdParams P) {
@@ -309,7 +331,6 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constan
   constexpr int NOUT = Acc<SOFT, LABELS>::NOUT;
   extern __shared__ __align__(16) float smem[];
   const int tid = threadIdx.x;
-  const int b = blockIdx.y;
   const int C = channels<CM, SOFTMAX>(P.g.C), CL = P.g.CL, off = P.g.offset, K = P.tab.K;
   const int slots = SOFT ? K + 1 : K;
   const int64_t N = P.g.N;
@@ -328,21 +349,33 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constan
   }
   const float2* my_lohi = lohi_t + (tid & (kTabCopies - 1));
   const float2* my_map = map_t + (tid & (kTabCopies - 1));
-  for (int i = tid; i < table_words; i += kHistThreads) hist[i] = 0u;
+  {
+    uint4* h4 = reinterpret_cast<uint4*>(hist);  // 16-byte aligned: (K + 1) * 256 bytes in
+    for (int i = tid; i < table_words / 4; i += kHistThreads) h4[i] = make_uint4(0u, 0u, 0u, 0u);
+    for (int i = (table_words & ~3) + tid; i < table_words; i += kHistThreads) hist[i] = 0u;
+  }
   __syncthreads();
 
   const int col = (tid & (R - 1)) * NW;
   const int slot_stride = R * NW, row_stride = slots * slot_stride;
   const int64_t out_stride = (int64_t)P.B_total * CL * slots;
-  const int64_t row0 = (int64_t)(P.b_offset + b) * CL;
 
-  const T* xb = static_cast<const T*>(P.x) + (int64_t)b * C * N;
-  const int64_t* lb = LABELS ? static_cast<const int64_t*>(P.target) + (int64_t)b * N : nullptr;
-  const float* yb = LABELS ? nullptr : static_cast<const float*>(P.target) + (int64_t)b * C * N;
+  const int64_t tpb = P.g.tiles > 0 ? P.g.tiles : 1;  // (no tiles at all when N = 0)
+  int64_t g0, g1;
+  chunk_range(P.g, g0, g1);
+  auto x_of = [&](int bb) { return static_cast<const T*>(P.x) + (int64_t)bb * C * N; };
+  auto lab_of = [&](int bb) {
+    return LABELS ? static_cast<const int64_t*>(P.target) + (int64_t)bb * N : nullptr;
+  };
+  auto y_of = [&](int bb) {
+    return LABELS ? nullptr : static_cast<const float*>(P.target) + (int64_t)bb * C * N;
+  };
 
   // One loss-channel value into the table, with its target: y (dense) or
-  // whether this channel is the voxel's class (labels).
-  auto update = [&](int row, float p, int j, float4 q, float y, bool is_true) {
+  // whether this channel is the voxel's class (labels; the soft softmax path
+  // passes false and adds the true class once per voxel with true_update).
+  // Returns the soft fixed-point words of u.
+  auto update = [&](int row, float p, int j, float4 q, float y, bool is_true) -> uint2 {
     if constexpr (!SOFT) {
       if (j < K) {  // p above the last edge (only for invalid p > 1 + eps) is dropped
         const int a = row * row_stride + j * slot_stride + col;
@@ -354,8 +387,9 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constan
           sadd(hist, a + 2, fix1(y));
         }
       }
+      return make_uint2(0u, 0u);
     } else {
-      // u * 2^22, u = (p - lo) / S inside, u = p in the end intervals
+      // u * 2^21, u = (p - lo) / S inside, u = p in the end intervals
       const float us = fminf(ACE_FMUL(ACE_FSUB(p, q.z), q.w), kFixScale);
       const int a = row * row_stride + j * slot_stride + col;
       sadd(hist, a, 1u);
@@ -377,6 +411,18 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constan
         sadd(hist, a + 6, uyw.x);
         sadd(hist, a + 7, uyw.y);
       }
+      return uw;
+    }
+  };
+  // The voxel's class (labels): its count (and soft: its u words) in its row.
+  auto true_update = [&](int row, int j, uint2 uw) {
+    const int a = row * row_stride + j * slot_stride + col;
+    if constexpr (!SOFT) {
+      if (j < K) sadd(hist, a + 2, 1u);
+    } else {
+      sadd(hist, a + 4, 1u);
+      sadd(hist, a + 5, uw.x);
+      sadd(hist, a + 6, uw.y);
     }
   };
   // Table entry of count j: neighbours and, for soft binning, base / scale.
@@ -390,15 +436,46 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constan
     }
   };
 
-  const int64_t t0 = (int64_t)blockIdx.x * P.g.tiles_per_chunk;
-  const int64_t t1 = min(t0 + P.g.tiles_per_chunk, P.g.tiles);
+  // Soft binning, softmax path: the count is the rounded p * K clamped to
+  // [0, K], without the exact test. It can be one off only for p within a few
+  // ulps of a bin centre, where both candidate intervals give the centre's bin a
+  // weight of ~1 (t ~ 1 in the lower interval, t ~ 0 in the upper one), so the
+  // sums differ by ulps; t may then be a few ulps below 0, or is clamped at 1.
+  // (The gradient kernel keeps the exact interval: the derivative of the weights
+  // jumps at a centre.) Only base / scale are read.
+  auto soft_entry = [&](float p, int& j) -> float4 {
+    int i = (int)(__float_as_uint(__fadd_rn(__fmul_rn(p, Kf), kFixMagic)) - kFixMagicBits);
+    i = max(0, min(i, K));
+    j = i;
+    const float2 m = my_map[i * kTabCopies];
+    return make_float4(0.0f, 0.0f, m.x, m.y);
+  };
+
   int since_fold = 0;
   const int64_t tile = (int64_t)kHistThreads * V;
   // L2 prefetch of the next tile (one thread per channel row and one for the
   // labels), so the loads of the next iteration hit L2 instead of HBM
-  const bool pf_x = ((reinterpret_cast<uintptr_t>(xb) | (N * sizeof(T))) & 15) == 0;
-  for (int64_t t = t0; t < t1; ++t) {
-    if (t + 1 < t1 && pf_x) {
+  const bool pf_x = ((reinterpret_cast<uintptr_t>(P.x) | (N * sizeof(T))) & 15) == 0;
+  int b = (int)(g0 / tpb);   // batch of tile g
+  int64_t t = g0 - b * tpb;  // its tile within the batch
+  const T* xb = x_of(b);
+  const int64_t* lb = lab_of(b);
+  const float* yb = y_of(b);
+  int64_t row0 = (int64_t)(P.b_offset + b) * CL;
+  for (int64_t g = g0; g < g1; ++g, ++t) {
+    if (t == tpb) {  // next batch: fold this batch's rows first
+      __syncthreads();
+      fold_table<SOFT, LABELS>(hist, CL, slots, R, P.accum, out_stride, row0);
+      __syncthreads();
+      since_fold = 0;
+      ++b;
+      t = 0;
+      xb = x_of(b);
+      lb = lab_of(b);
+      yb = y_of(b);
+      row0 = (int64_t)(P.b_offset + b) * CL;
+    }
+    if (t + 1 < tpb && g + 1 < g1 && pf_x) {
       if (tid < C) ace_prefetch_tile(xb + (int64_t)tid * N, (t + 1) * tile, tile, N, sizeof(T));
       if constexpr (LABELS) {
         if (tid == C) ace_prefetch_tile(lb, (t + 1) * tile, tile, N, 8);
@@ -427,31 +504,53 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constan
           ace_softmax<CM>(p, C);
           int j[CM];
           float4 q[CM];
-          bool ok = true;
-#pragma unroll
-          for (int c = 0; c < CM; ++c) {
-            if ((c > 0 || off == 0) && c < C) {
-              j[c] = ace_guess(p[c], Kf, K, SOFT);
-              q[c] = entry(j[c]);
-              ok &= ace_is_count(p[c], make_float2(q[c].x, q[c].y));
-            }
-          }
-          if (!ok) {
+          if constexpr (SOFT) {
 #pragma unroll
             for (int c = 0; c < CM; ++c)
-              if ((c > 0 || off == 0) && c < C &&
-                  !ace_is_count(p[c], make_float2(q[c].x, q[c].y))) {
-                j[c] = ace_fix_count(p[c], j[c], K, my_lohi, kTabCopies).i;
+              if ((c > 0 || off == 0) && c < C) q[c] = soft_entry(p[c], j[c]);
+          } else {
+            bool ok = true;
+#pragma unroll
+            for (int c = 0; c < CM; ++c) {
+              if ((c > 0 || off == 0) && c < C) {
+                j[c] = ace_guess(p[c], Kf, K, SOFT);
                 q[c] = entry(j[c]);
+                ok &= ace_is_count(p[c], make_float2(q[c].x, q[c].y));
               }
+            }
+            if (!ok) {
+#pragma unroll
+              for (int c = 0; c < CM; ++c)
+                if ((c > 0 || off == 0) && c < C &&
+                    !ace_is_count(p[c], make_float2(q[c].x, q[c].y))) {
+                  j[c] = ace_fix_count(p[c], j[c], K, my_lohi, kTabCopies).i;
+                  q[c] = entry(j[c]);
+                }
+            }
           }
+          uint2 uw[CM];
 #pragma unroll
           for (int c = 0; c < CM; ++c) {
             if ((c > 0 || off == 0) && c < C) {
               float y = 0.0f;
               if constexpr (!LABELS) y = yv[c][i];
-              update(c - off, p[c], j[c], q[c], y, LABELS && lab[i] == c);
+              // hard: the class's count as one predicated add per channel
+              uw[c] = update(c - off, p[c], j[c], q[c], y, !SOFT && LABELS && lab[i] == c);
             }
+          }
+          if constexpr (SOFT && LABELS) {
+            // the voxel's class, if it is a loss channel: its bin and u words
+            const int lt = lab[i];
+            int jt = 0;
+            uint2 wt = make_uint2(0u, 0u);
+#pragma unroll
+            for (int c = 0; c < CM; ++c) {
+              if ((c > 0 || off == 0) && c < C && lt == c) {
+                jt = j[c];
+                wt = uw[c];
+              }
+            }
+            if (lt >= off && lt < C) true_update(lt - off, jt, wt);
           }
         }
       } else {
@@ -473,7 +572,7 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constan
         }
       }
     }
-    if (++since_fold == P.flush_tiles && t + 1 < t1) {
+    if (++since_fold == P.flush_tiles && g + 1 < g1) {
       since_fold = 0;
       __syncthreads();
       fold_table<SOFT, LABELS>(hist, CL, slots, R, P.accum, out_stride, row0);
@@ -482,16 +581,20 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constan
   }
   __syncthreads();
   fold_table<SOFT, LABELS>(hist, CL, slots, R, P.accum, out_stride, row0);
-  __threadfence();
   __syncthreads();
   __shared__ bool s_last;
   if (tid == 0) {
-    const unsigned done = atomicAdd(P.counter, 1u);
+    // The ticket is a release (this CTA's sums, ordered before it by the
+    // barrier) and an acquire (the other CTAs' sums, for the last CTA).
+    unsigned done;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
+                 : "=r"(done)
+                 : "l"(P.counter)
+                 : "memory");
     s_last = (done == gridDim.x * gridDim.y - 1);
   }
   __syncthreads();
   if (!s_last) return;
-  __threadfence();
 
   // Last CTA: the workspace sums become W, P, G per bin. Hard: slot = bin. Soft:
   // interval j in 1..K-1 (between lo and hi = lo + S) gives bin j its t share,
@@ -576,7 +679,7 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constan
 // last bin); soft, one record per interval j, {g coef_l, d_l, g coef_r, d_r} of
 // its two bins, read with one 16-byte load. Hard binning reads no targets.
 // ---------------------------------------------------------------------------
-// q = table entry of the value's interval: {lo, hi, base, 2^22 / S} (soft).
+// q = table entry of the value's interval: {lo, hi, base, 2^21 / S} (soft).
 // Inside an interval the weights are rw = t = (p - lo) / S, lw = 1 - t and
 // d w / d p = -+ 1 / S; in an end interval both sides are the same bin, where the
 // formula reduces to g coef for any weights summing to 1 (there u = p, 1 / S = 1).
@@ -588,7 +691,7 @@ __device__ __forceinline__ float grad_p(const float* __restrict__ tab, int copie
     return tab[(row * (K + 1) + j) * copies];
   } else {
     const float4 rec = reinterpret_cast<const float4*>(tab)[(row * (K + 1) + j) * copies];
-    const float inv = q.w * (1.0f / 4194304.0f);
+    const float inv = q.w * (1.0f / kFixScale);
     const float rw = (p - q.z) * inv;
     const float lw = 1.0f - rw;
     const float resid = p - y;
@@ -614,11 +717,11 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const __grid_constant__ 
   const int rec_copies = P.rec_copies;
   float2* lohi_t = reinterpret_cast<float2*>(tab + (SOFT ? 4 : 1) * CL * (K + 1) * rec_copies);
   float2* map_t = lohi_t + (K + 1) * kTabCopies;
-  const int64_t row0 = (int64_t)(P.b_offset + b) * CL;
   for (int i = tid; i < (K + 1) * kTabCopies; i += kThreads) {
     lohi_t[i] = P.tab.lohi[i / kTabCopies];
     map_t[i] = P.tab.map[i / kTabCopies];
   }
+  const int64_t row0 = (int64_t)(P.b_offset + b) * CL;
   for (int e = tid; e < CL * (K + 1) * rec_copies; e += kThreads) {
     const int ej = e / rec_copies;
     const int row = ej / (K + 1), j = ej - row * (K + 1);

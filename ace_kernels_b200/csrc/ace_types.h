@@ -15,6 +15,7 @@ constexpr int kMaxClasses = ACE_B200_MAX_CLASSES;  // channels limit of the kern
 constexpr int kThreads = 256;                      // threads per CTA (gradient, epilogue)
 constexpr int kHistThreads = 512;                  // threads per CTA of the histogram
 constexpr int kTabCopies = 16;                     // interleaved copies of the bin tables
+constexpr float kFixScale = 2097152.0f;            // 2^21: fixed-point unit of the statistics
 
 // Sorted search table with its neighbours paired (see ace_locate): hard binning
 // uses the K upper bin edges, soft binning the K bin centres; entry i holds
@@ -25,8 +26,8 @@ constexpr int kTabCopies = 16;                     // interleaved copies of the 
 // halves are separate 8-byte tables (an 8-byte shared-memory gather by 32 lanes
 // with random indices conflicts far less than a 16-byte one).
 // Soft binning: interval i lies between t[i-1] and t[i]; base and scale map p to
-// the interval's coordinate u = (p - base) * scale / 2^22 (u = t, the right-bin
-// weight, inside; u = p in the two end intervals: base 0, scale 2^22).
+// the interval's coordinate u = (p - base) * scale / 2^21 (u = t, the right-bin
+// weight, inside; u = p in the two end intervals: base 0, scale 2^21).
 struct BinTable {
   int K;
   float2 lohi[kMaxBins + 1];  // {t[i-1], t[i]}
@@ -43,8 +44,9 @@ struct Grid {
   int CL;              // loss channels: C - offset
   int offset;          // 1 when the background channel is dropped
   int chunks;          // CTAs per batch
-  int64_t tiles;       // tiles of kThreads * V voxels per batch
+  int64_t tiles;       // tiles of threads * V voxels per batch
   int64_t tiles_per_chunk;
+  int chunks_per_batch;  // > 0: chunks never cross batches; 0: flat over all tiles
 };
 
 struct EpiParams {

@@ -12,7 +12,10 @@ epilogue and the local backward.
 
 One step = forward + backward of ``ace_loss(..., impl="b200_cuda")`` through
 ``torch.autograd.grad``, inputs resident in HBM, replayed from a CUDA graph; L2 is
-flushed (512 MiB write) before every step, outside the step's events. ``value`` =
+flushed before every step, outside the step's events: a 512 MiB buffer is written
+and then read back, so the step starts with neither its inputs nor dirty lines in
+L2 (a write alone would leave the L2 full of dirty lines, whose write-back would
+then be charged to the step). ``value`` =
 voxels of all ranks / (max over ranks of the summed device time of K steps).
 ``e2e`` = the same call per step with the inputs copied from pinned host memory
 and the loss read back, inside the timed region. ``roofline`` = the dominant
@@ -209,12 +212,19 @@ def profiled_traffic(kernel: str, workload: str) -> float | None:
         return None
 
 
+def flush_l2(flush: torch.Tensor) -> None:
+    """Evicts the L2: writes a buffer larger than it, then reads the buffer back
+    (the write-backs of the written lines happen here, not in the timed step)."""
+    flush.fill_(1)
+    flush.view(torch.int64).sum()
+
+
 def time_events(fn, flush: torch.Tensor, reps: int) -> float:  # type: ignore[no-untyped-def]
     """Summed device milliseconds of ``reps`` calls, L2 flushed before each."""
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
     for i in range(reps):
-        flush.zero_()
+        flush_l2(flush)
         starts[i].record()
         fn()
         ends[i].record()
@@ -380,7 +390,7 @@ def run_ours(args: argparse.Namespace) -> None:
             "num_bins": cfg.num_bins,
             "parallelism": f"batch-sharded dp{world}" if world > 1 else "single GPU",
             "mode": "eager" if graph is None else "cuda_graph",
-            "l2": "flushed before every step (512 MiB write, outside the events)",
+            "l2": "flushed before every step: 512 MiB written, then read back, outside the events",
         },
         "hbm_frac_of_ideal_bytes": (step_bytes * world / (ms_per_step * 1e-3) / 1e9) / (peak * world),
         "eager_ms_per_step": eager_ms,
