@@ -502,6 +502,40 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constan
 #pragma unroll
           for (int c = 0; c < CM; ++c) p[c] = xv[c][i];
           ace_softmax<CM>(p, C);
+          if constexpr (CM > 4) {
+            // Many channels: locate and add one channel at a time, so that only
+            // the probabilities stay in registers (no per-channel bin arrays).
+            const int lt = LABELS ? lab[i] : -1;
+            int jt = 0;
+            uint2 wt = make_uint2(0u, 0u);
+#pragma unroll
+            for (int c = 0; c < CM; ++c) {
+              if ((c > 0 || off == 0) && c < C) {
+                int jc;
+                float4 qc;
+                if constexpr (SOFT) {
+                  qc = soft_entry(p[c], jc);
+                } else {
+                  float2 lh;
+                  jc = ace_locate(p[c], my_lohi, kTabCopies, K, Kf, false, lh);
+                  qc = make_float4(lh.x, lh.y, 0.0f, 0.0f);
+                }
+                float y = 0.0f;
+                if constexpr (!LABELS) y = yv[c][i];
+                const uint2 w = update(c - off, p[c], jc, qc, y, !SOFT && LABELS && lt == c);
+                if constexpr (SOFT && LABELS) {
+                  if (lt == c) {
+                    jt = jc;
+                    wt = w;
+                  }
+                }
+              }
+            }
+            if constexpr (SOFT && LABELS) {
+              if (lt >= off && lt < C) true_update(lt - off, jt, wt);
+            }
+            continue;
+          }
           int j[CM];
           float4 q[CM];
           if constexpr (SOFT) {
@@ -787,38 +821,58 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const __grid_constant__ 
 #pragma unroll
         for (int c = 0; c < CM; ++c) p[c] = xv[c][i];
         ace_softmax<CM>(p, C);
-        int j[CM];
-        float4 q[CM];
-        bool ok = true;
-#pragma unroll
-        for (int c = 0; c < CM; ++c) {
-          if ((c > 0 || off == 0) && c < C) {
-            j[c] = ace_guess(p[c], Kf, K, SOFT);
-            q[c] = entry(j[c]);
-            ok &= ace_is_count(p[c], make_float2(q[c].x, q[c].y));
-          }
-        }
-        if (!ok) {
-#pragma unroll
-          for (int c = 0; c < CM; ++c)
-            if ((c > 0 || off == 0) && c < C && !ace_is_count(p[c], make_float2(q[c].x, q[c].y))) {
-              j[c] = ace_fix_count(p[c], j[c], K, my_lohi, kTabCopies).i;
-              q[c] = entry(j[c]);
-            }
-        }
         float gp[CM];
         float dot = 0.0f;
+        if constexpr (CM > 4) {
+          // Many channels: one channel at a time (exact interval), so that only
+          // p and gp stay in registers.
 #pragma unroll
-        for (int c = 0; c < CM; ++c) {
-          gp[c] = 0.0f;
-          if (c < C) {
-            if (c > 0 || off == 0) {
-              float y = 0.0f;
-              if constexpr (SOFT && LABELS) y = (lab[i] == c) ? 1.0f : 0.0f;
-              if constexpr (SOFT && !LABELS) y = yv[c][i];
-              gp[c] = grad_p<SOFT>(my_tab, rec_copies, c - off, K, j[c], q[c], p[c], y);
+          for (int c = 0; c < CM; ++c) {
+            gp[c] = 0.0f;
+            if (c < C) {
+              if (c > 0 || off == 0) {
+                float2 lh;
+                const int jc = ace_locate(p[c], my_lohi, kTabCopies, K, Kf, SOFT, lh);
+                float y = 0.0f;
+                if constexpr (SOFT && LABELS) y = (lab[i] == c) ? 1.0f : 0.0f;
+                if constexpr (SOFT && !LABELS) y = yv[c][i];
+                gp[c] = grad_p<SOFT>(my_tab, rec_copies, c - off, K, jc, entry(jc), p[c], y);
+              }
+              dot += p[c] * gp[c];
             }
-            dot += p[c] * gp[c];
+          }
+        } else {
+          int j[CM];
+          float4 q[CM];
+          bool ok = true;
+#pragma unroll
+          for (int c = 0; c < CM; ++c) {
+            if ((c > 0 || off == 0) && c < C) {
+              j[c] = ace_guess(p[c], Kf, K, SOFT);
+              q[c] = entry(j[c]);
+              ok &= ace_is_count(p[c], make_float2(q[c].x, q[c].y));
+            }
+          }
+          if (!ok) {
+#pragma unroll
+            for (int c = 0; c < CM; ++c)
+              if ((c > 0 || off == 0) && c < C && !ace_is_count(p[c], make_float2(q[c].x, q[c].y))) {
+                j[c] = ace_fix_count(p[c], j[c], K, my_lohi, kTabCopies).i;
+                q[c] = entry(j[c]);
+              }
+          }
+#pragma unroll
+          for (int c = 0; c < CM; ++c) {
+            gp[c] = 0.0f;
+            if (c < C) {
+              if (c > 0 || off == 0) {
+                float y = 0.0f;
+                if constexpr (SOFT && LABELS) y = (lab[i] == c) ? 1.0f : 0.0f;
+                if constexpr (SOFT && !LABELS) y = yv[c][i];
+                gp[c] = grad_p<SOFT>(my_tab, rec_copies, c - off, K, j[c], q[c], p[c], y);
+              }
+              dot += p[c] * gp[c];
+            }
           }
         }
 #pragma unroll
