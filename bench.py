@@ -287,7 +287,8 @@ def run_ours(args: argparse.Namespace) -> None:
     for _ in range(max(3, args.warmup)):
         step()
     torch.cuda.synchronize()
-    # NCCL inside a captured graph is left for later: N > 1 runs eagerly
+    # One CUDA graph per step at N = 1; N > 1 runs eagerly (a captured step with
+    # the NCCL all-reduce inside hung in this bench, so it is not captured)
     graph = None if (args.eager or world > 1) else capture(step)
     run = step if graph is None else graph.replay
 

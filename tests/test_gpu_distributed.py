@@ -1,0 +1,95 @@
+"""Sharded mL1-ACE on two GPUs over NCCL (skipped with fewer than two GPUs): each
+rank runs the CUDA histogram on its shard, the statistics are all-reduced, and
+the loss and each rank's gradient equal the single-GPU call on the whole batch
+(batch sharding) or volume (spatial sharding), computed on the same device."""
+
+import os
+import socket
+import traceback
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from ace_kernels_b200 import ace_loss
+from ace_kernels_b200.distributed import batch_shard, sharded_ace_loss, spatial_shard
+from tests.cases import Spec, make
+from tests.helpers import to_config
+
+pytestmark = pytest.mark.gpu
+
+CONFIGS = {
+    "soft-mean": {"binning": "soft", "to_onehot_y": True},
+    "hard-sum-nobg": {"binning": "hard", "to_onehot_y": True, "include_background": False,
+                      "reduction": "sum"},
+    "soft-none": {"binning": "soft", "to_onehot_y": True, "reduction": "none"},
+}
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return int(s.getsockname()[1])
+
+
+def _worker(rank: int, world: int, port: int, name: str, mode: str, q) -> None:  # type: ignore[no-untyped-def]
+    import datetime
+
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                                timeout=datetime.timedelta(seconds=60))
+        cfg = to_config(CONFIGS[name])
+        x, y = make(Spec(4, 4, (24, 20, 16), seed=11), cfg.num_bins)
+        x, y = x.to(dev), y.to(dev)
+        # the unsharded call on this device
+        xf = x.clone().requires_grad_(True)
+        lf = ace_loss(xf, y, cfg, impl="b200_cuda")
+        gup = torch.linspace(0.5, 2.0, lf.numel(), device=dev).view_as(lf)
+        torch.autograd.backward(lf, gup)
+        if mode == "batch":
+            off, cnt = batch_shard(4, rank, world)
+            xs, ys = x[off:off + cnt], y[off:off + cnt]
+            kwargs = {"b_offset": off, "b_total": 4}
+            ref_grad = xf.grad[off:off + cnt]
+        else:
+            n = 24 * 20 * 16
+            start, cnt = spatial_shard(n, rank, world)
+            xs = x.flatten(2)[..., start:start + cnt].contiguous()
+            ys = y.flatten(2)[..., start:start + cnt].contiguous()
+            kwargs = {}
+            ref_grad = xf.grad.flatten(2)[..., start:start + cnt]
+        xs = xs.clone().requires_grad_(True)
+        loss = sharded_ace_loss(xs, ys, cfg, **kwargs)
+        torch.autograd.backward(loss, gup.view_as(loss))
+        torch.cuda.synchronize()
+        # the sharded sums are added in another order: loss to float rounding
+        # (reduction "none": the per-row losses, viewed by the shard's rank of dims)
+        torch.testing.assert_close(loss.detach().reshape(-1), lf.detach().reshape(-1),
+                                   rtol=1e-5, atol=1e-6)
+        torch.testing.assert_close(xs.grad, ref_grad, rtol=1e-3, atol=1e-6)
+        q.put((rank, "ok"))
+    except Exception:  # reported to the parent, which fails the test
+        q.put((rank, traceback.format_exc()))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("mode", ["batch", "spatial"])
+@pytest.mark.parametrize("name", sorted(CONFIGS))
+def test_two_gpus_match_single_gpu(name: str, mode: str) -> None:
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, name, mode, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+    assert results == {0: "ok", 1: "ok"}, results
