@@ -244,6 +244,16 @@ __device__ __forceinline__ void ace_load_labels(const int64_t* __restrict__ p, i
   }
 }
 
+// Programmatic dependent launch: wait until the grid this one depends on has
+// completed and its memory is visible (a no-op without the launch attribute);
+// and allow the dependent grid to be scheduled.
+__device__ __forceinline__ void ace_grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void ace_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Asynchronous prefetch of [p, p + bytes) from HBM into L2 (no registers, no
 // completion to wait for). p and bytes must be multiples of 16; the range must lie
 // inside the allocation.

@@ -354,6 +354,10 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constan
     for (int i = tid; i < table_words / 4; i += kHistThreads) h4[i] = make_uint4(0u, 0u, 0u, 0u);
     for (int i = (table_words & ~3) + tid; i < table_words; i += kHistThreads) hist[i] = 0u;
   }
+  // Launched with programmatic dependent launch: the setup above (parameters
+  // and shared memory only) overlaps the previous kernel's tail; no global
+  // memory is touched before the previous grid has completed.
+  ace_grid_dependency_wait();
   __syncthreads();
 
   const int col = (tid & (R - 1)) * NW;
@@ -613,6 +617,7 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constan
       __syncthreads();
     }
   }
+  ace_launch_dependents();  // a dependent launch may begin its own setup now
   __syncthreads();
   fold_table<SOFT, LABELS>(hist, CL, slots, R, P.accum, out_stride, row0);
   __syncthreads();
@@ -755,6 +760,8 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const __grid_constant__ 
     lohi_t[i] = P.tab.lohi[i / kTabCopies];
     map_t[i] = P.tab.map[i / kTabCopies];
   }
+  // programmatic dependent launch: global memory only after the previous grid
+  ace_grid_dependency_wait();
   const int64_t row0 = (int64_t)(P.b_offset + b) * CL;
   for (int e = tid; e < CL * (K + 1) * rec_copies; e += kThreads) {
     const int ej = e / rec_copies;
@@ -952,6 +959,25 @@ __global__ void __launch_bounds__(kThreads) probs_kernel(const T* __restrict__ x
 // library and could skip the opt-in).
 namespace {
 
+// Launch with programmatic stream serialization (programmatic dependent launch):
+// the kernel may start while the previous kernel on the stream finishes; it waits
+// for it (ace_grid_dependency_wait) before touching global memory.
+template <typename K, typename Params>
+cudaError_t launch_dependent(K* kernel, dim3 grid, int threads, int smem, cudaStream_t s,
+                             const Params& p) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3((unsigned)threads);
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, p);
+}
+
 // Opt a kernel in to `smem` dynamic shared-memory bytes when static + dynamic
 // would exceed the default 48 KB (once per kernel and size).
 template <typename K>
@@ -972,8 +998,7 @@ struct HistLauncher {
     auto k = hist_kernel<T, V, CM, SM, SOFT, LAB>;
     cudaError_t e = set_smem(k, smem, configured());
     if (e != cudaSuccess) return e;
-    k<<<grid, kHistThreads, smem, s>>>(p);
-    return cudaGetLastError();
+    return launch_dependent(k, grid, kHistThreads, smem, s, p);
   }
   static int occupancy(int smem) {
     auto k = hist_kernel<T, V, CM, SM, SOFT, LAB>;
@@ -994,8 +1019,7 @@ struct GradLauncher {
     auto k = grad_kernel<T, V, CM, SM, SOFT, LAB>;
     cudaError_t e = set_smem(k, smem, configured());
     if (e != cudaSuccess) return e;
-    k<<<grid, kThreads, smem, s>>>(p);
-    return cudaGetLastError();
+    return launch_dependent(k, grid, kThreads, smem, s, p);
   }
   static int occupancy(int smem) {
     auto k = grad_kernel<T, V, CM, SM, SOFT, LAB>;
