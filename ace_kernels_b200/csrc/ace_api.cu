@@ -218,7 +218,11 @@ int check_common(const ace_b200_inputs* in, const ace_b200_options* opt, int& CL
 }
 
 // Kernel variant and vector width for this launch (see ACE_VARIANT_CASES).
-Variant choose_variant(const ace_b200_inputs* in, const ace_b200_options* opt, const void* out) {
+// `hist`: the forward's many-channel instances (CM > 4) keep only per-voxel
+// scalars in registers, so they take two voxels per thread (CM >= 16) where the
+// gradient's register-tile instances take one.
+Variant choose_variant(const ace_b200_inputs* in, const ace_b200_options* opt, const void* out,
+                       bool hist) {
   Variant v;
   v.softmax = opt->activation == ACE_B200_ACT_SOFTMAX && in->C > 1;
   v.soft = opt->soft != 0;
@@ -230,7 +234,7 @@ Variant choose_variant(const ace_b200_inputs* in, const ace_b200_options* opt, c
     // exact channel count up to 4 (no per-channel guards), capacity buckets above
     const int C = (int)in->C;
     v.CM = C <= 4 ? C : C <= 8 ? 8 : C <= 16 ? 16 : C <= 32 ? 32 : 64;
-    V = v.CM <= 4 ? vmax : v.CM == 8 ? (vmax < 4 ? vmax : 4) : v.CM == 16 ? 2 : 1;
+    V = v.CM <= 4 ? vmax : v.CM == 8 ? (vmax < 4 ? vmax : 4) : (v.CM == 16 || hist) ? 2 : 1;
   } else {
     v.CM = 1;
     V = vmax;
@@ -334,7 +338,7 @@ int hist_impl(const ace_b200_inputs* in, const ace_b200_options* opt, float* his
     rc = fill_epi(p.epi, in->b_total, CL, in->rows_global, opt, *out);
     if (rc) return rc;
   }
-  Variant v = choose_variant(in, opt, nullptr);
+  Variant v = choose_variant(in, opt, nullptr, true);
   // Shared-memory table: `entries` words per lane replica. A 32-bit word of a
   // replica takes at most (kHistThreads / R) * V additions per tile and must not
   // take more than 1023 between two folds (values up to 2^21 each), so R has a
@@ -554,7 +558,7 @@ int ace_b200_backward(const ace_b200_inputs* in, const ace_b200_options* opt,
   const int K = opt->num_bins;
   BwdParams p;
   memset(&p, 0, sizeof(p));
-  const Variant v = choose_variant(in, opt, dx);
+  const Variant v = choose_variant(in, opt, dx, false);
   const bool soft = opt->soft != 0;
   // Record copies: as many as fit in 96 KB (two CTAs per SM keep their tables).
   int copies = soft ? 8 : 32;
@@ -562,7 +566,10 @@ int ace_b200_backward(const ace_b200_inputs* in, const ace_b200_options* opt,
     return (size_t)(K + 1) * kTabCopies * sizeof(float4) + (size_t)(soft ? 16 : 4) * c * CL * (K + 1);
   };
   while (copies > 1 && grad_smem(copies) > 96 * 1024) copies /= 2;
-  const int smem = (int)grad_smem(copies);
+  // the many-channel kernel keeps every channel's gp per thread: C x threads x V floats
+  const size_t scratch =
+      (v.softmax && v.CM > 4) ? (size_t)in->C * kThreads * v.V * sizeof(float) : 0;
+  const int smem = (int)(grad_smem(copies) + scratch);
   if (smem > 227 * 1024) return fail(ACE_B200_EUNSUPPORTED, "gradient tables do not fit");
   p.rec_copies = copies;
   int dev = 0;

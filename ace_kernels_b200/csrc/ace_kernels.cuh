@@ -489,7 +489,60 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constan
     if (v0 < N) {  // V > 1 implies N % V == 0: groups are whole
       int lab[V];
       if constexpr (LABELS) ace_load_labels<V>(lb + v0, lab);
-      if constexpr (SOFTMAX) {
+      if constexpr (SOFTMAX && CM > 4) {
+        // Many channels: three passes over the channels, so that only per-voxel
+        // scalars live in registers (the reloads hit L1 / L2): the maximum, the
+        // sum of exponentials (ascending channels), then each probability,
+        // computed as in ace_softmax (same operations, same result), is binned
+        // and added.
+        const T* xr = xb + v0;
+        float m[V], sm[V], rc[V];
+        VecIO<T, V>::load(xr, m);
+#pragma unroll 4
+        for (int c = 1; c < C; ++c) {
+          float x[V];
+          VecIO<T, V>::load(xr + (int64_t)c * N, x);
+#pragma unroll
+          for (int i = 0; i < V; ++i) m[i] = fmaxf(m[i], x[i]);
+        }
+#pragma unroll
+        for (int i = 0; i < V; ++i) sm[i] = 0.0f;
+#pragma unroll 4
+        for (int c = 0; c < C; ++c) {
+          float x[V];
+          VecIO<T, V>::load(xr + (int64_t)c * N, x);
+#pragma unroll
+          for (int i = 0; i < V; ++i) sm[i] = ACE_FADD(sm[i], expf(ACE_FSUB(x[i], m[i])));
+        }
+#pragma unroll
+        for (int i = 0; i < V; ++i) rc[i] = ace_rcp_refined(sm[i]);
+#pragma unroll 2
+        for (int c = off; c < C; ++c) {
+          float x[V], yv[V];
+          VecIO<T, V>::load(xr + (int64_t)c * N, x);
+          if constexpr (!LABELS) VecIO<float, V>::load(yb + (int64_t)c * N + v0, yv);
+#pragma unroll
+          for (int i = 0; i < V; ++i) {
+            const float p = ace_div_corrected(expf(ACE_FSUB(x[i], m[i])), sm[i], rc[i]);
+            int j;
+            float4 q;
+            if constexpr (SOFT) {
+              q = soft_entry(p, j);
+            } else {
+              float2 lh;
+              j = ace_locate(p, my_lohi, kTabCopies, K, Kf, false, lh);
+              q = make_float4(lh.x, lh.y, 0.0f, 0.0f);
+            }
+            float y = 0.0f;
+            if constexpr (!LABELS) y = yv[i];
+            const bool is_true = LABELS && lab[i] == c;
+            const uint2 w = update(c - off, p, j, q, y, !SOFT && is_true);
+            if constexpr (SOFT && LABELS) {
+              if (is_true) true_update(c - off, j, w);
+            }
+          }
+        }
+      } else if constexpr (SOFTMAX) {
         float xv[CM][V];
 #pragma unroll
         for (int c = 0; c < CM; ++c)
@@ -506,40 +559,6 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constan
 #pragma unroll
           for (int c = 0; c < CM; ++c) p[c] = xv[c][i];
           ace_softmax<CM>(p, C);
-          if constexpr (CM > 4) {
-            // Many channels: locate and add one channel at a time, so that only
-            // the probabilities stay in registers (no per-channel bin arrays).
-            const int lt = LABELS ? lab[i] : -1;
-            int jt = 0;
-            uint2 wt = make_uint2(0u, 0u);
-#pragma unroll
-            for (int c = 0; c < CM; ++c) {
-              if ((c > 0 || off == 0) && c < C) {
-                int jc;
-                float4 qc;
-                if constexpr (SOFT) {
-                  qc = soft_entry(p[c], jc);
-                } else {
-                  float2 lh;
-                  jc = ace_locate(p[c], my_lohi, kTabCopies, K, Kf, false, lh);
-                  qc = make_float4(lh.x, lh.y, 0.0f, 0.0f);
-                }
-                float y = 0.0f;
-                if constexpr (!LABELS) y = yv[c][i];
-                const uint2 w = update(c - off, p[c], jc, qc, y, !SOFT && LABELS && lt == c);
-                if constexpr (SOFT && LABELS) {
-                  if (lt == c) {
-                    jt = jc;
-                    wt = w;
-                  }
-                }
-              }
-            }
-            if constexpr (SOFT && LABELS) {
-              if (lt >= off && lt < C) true_update(lt - off, jt, wt);
-            }
-            continue;
-          }
           int j[CM];
           float4 q[CM];
           if constexpr (SOFT) {
@@ -756,6 +775,8 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const __grid_constant__ 
   const int rec_copies = P.rec_copies;
   float2* lohi_t = reinterpret_cast<float2*>(tab + (SOFT ? 4 : 1) * CL * (K + 1) * rec_copies);
   float2* map_t = lohi_t + (K + 1) * kTabCopies;
+  // many channels: per-thread gp of every channel, [c][thread][V] (fp32)
+  float* gscratch = reinterpret_cast<float*>(map_t + (K + 1) * kTabCopies);
   for (int i = tid; i < (K + 1) * kTabCopies; i += kThreads) {
     lohi_t[i] = P.tab.lohi[i / kTabCopies];
     map_t[i] = P.tab.map[i / kTabCopies];
@@ -811,7 +832,71 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const __grid_constant__ 
     if (v0 >= N) continue;
     int lab[V];
     if constexpr (SOFT && LABELS) ace_load_labels<V>(lb + v0, lab);
-    if constexpr (SOFTMAX) {
+    if constexpr (SOFTMAX && CM > 4) {
+      // Many channels, in passes as the forward: maximum, sum of exponentials,
+      // then p and gp per channel (gp kept in shared memory, the dot product in
+      // registers), then dx = p (gp - dot); only per-voxel scalars in registers.
+      const T* xr = xb + v0;
+      float m[V], sm[V], rc[V], dot[V];
+      VecIO<T, V>::load(xr, m);
+#pragma unroll 4
+      for (int c = 1; c < C; ++c) {
+        float x[V];
+        VecIO<T, V>::load(xr + (int64_t)c * N, x);
+#pragma unroll
+        for (int i = 0; i < V; ++i) m[i] = fmaxf(m[i], x[i]);
+      }
+#pragma unroll
+      for (int i = 0; i < V; ++i) sm[i] = 0.0f;
+#pragma unroll 4
+      for (int c = 0; c < C; ++c) {
+        float x[V];
+        VecIO<T, V>::load(xr + (int64_t)c * N, x);
+#pragma unroll
+        for (int i = 0; i < V; ++i) sm[i] = ACE_FADD(sm[i], expf(ACE_FSUB(x[i], m[i])));
+      }
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        rc[i] = ace_rcp_refined(sm[i]);
+        dot[i] = 0.0f;
+      }
+      float* gs = gscratch + tid * V;
+      const int gstride = kThreads * V;
+#pragma unroll 2
+      for (int c = 0; c < C; ++c) {
+        float x[V], yv[V];
+        VecIO<T, V>::load(xr + (int64_t)c * N, x);
+        if constexpr (SOFT && !LABELS) {
+          if (c >= off) VecIO<float, V>::load(yb + (int64_t)c * N + v0, yv);
+        }
+#pragma unroll
+        for (int i = 0; i < V; ++i) {
+          const float p = ace_div_corrected(expf(ACE_FSUB(x[i], m[i])), sm[i], rc[i]);
+          float gp = 0.0f;
+          if (c >= off) {
+            float2 lh;
+            const int jc = ace_locate(p, my_lohi, kTabCopies, K, Kf, SOFT, lh);
+            float y = 0.0f;
+            if constexpr (SOFT && LABELS) y = (lab[i] == c) ? 1.0f : 0.0f;
+            if constexpr (SOFT && !LABELS) y = yv[i];
+            gp = grad_p<SOFT>(my_tab, rec_copies, c - off, K, jc, entry(jc), p, y);
+          }
+          dot[i] += p * gp;
+          gs[c * gstride + i] = gp;
+        }
+      }
+#pragma unroll 2
+      for (int c = 0; c < C; ++c) {
+        float x[V], o[V];
+        VecIO<T, V>::load(xr + (int64_t)c * N, x);
+#pragma unroll
+        for (int i = 0; i < V; ++i) {
+          const float p = ace_div_corrected(expf(ACE_FSUB(x[i], m[i])), sm[i], rc[i]);
+          o[i] = p * (gs[c * gstride + i] - dot[i]);
+        }
+        VecIO<T, V>::store(db + (int64_t)c * N + v0, o);
+      }
+    } else if constexpr (SOFTMAX) {
       float xv[CM][V];
 #pragma unroll
       for (int c = 0; c < CM; ++c)
@@ -830,56 +915,36 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const __grid_constant__ 
         ace_softmax<CM>(p, C);
         float gp[CM];
         float dot = 0.0f;
-        if constexpr (CM > 4) {
-          // Many channels: one channel at a time (exact interval), so that only
-          // p and gp stay in registers.
+        int j[CM];
+        float4 q[CM];
+        bool ok = true;
 #pragma unroll
-          for (int c = 0; c < CM; ++c) {
-            gp[c] = 0.0f;
-            if (c < C) {
-              if (c > 0 || off == 0) {
-                float2 lh;
-                const int jc = ace_locate(p[c], my_lohi, kTabCopies, K, Kf, SOFT, lh);
-                float y = 0.0f;
-                if constexpr (SOFT && LABELS) y = (lab[i] == c) ? 1.0f : 0.0f;
-                if constexpr (SOFT && !LABELS) y = yv[c][i];
-                gp[c] = grad_p<SOFT>(my_tab, rec_copies, c - off, K, jc, entry(jc), p[c], y);
-              }
-              dot += p[c] * gp[c];
-            }
+        for (int c = 0; c < CM; ++c) {
+          if ((c > 0 || off == 0) && c < C) {
+            j[c] = ace_guess(p[c], Kf, K, SOFT);
+            q[c] = entry(j[c]);
+            ok &= ace_is_count(p[c], make_float2(q[c].x, q[c].y));
           }
-        } else {
-          int j[CM];
-          float4 q[CM];
-          bool ok = true;
+        }
+        if (!ok) {
 #pragma unroll
-          for (int c = 0; c < CM; ++c) {
-            if ((c > 0 || off == 0) && c < C) {
-              j[c] = ace_guess(p[c], Kf, K, SOFT);
+          for (int c = 0; c < CM; ++c)
+            if ((c > 0 || off == 0) && c < C && !ace_is_count(p[c], make_float2(q[c].x, q[c].y))) {
+              j[c] = ace_fix_count(p[c], j[c], K, my_lohi, kTabCopies).i;
               q[c] = entry(j[c]);
-              ok &= ace_is_count(p[c], make_float2(q[c].x, q[c].y));
             }
-          }
-          if (!ok) {
+        }
 #pragma unroll
-            for (int c = 0; c < CM; ++c)
-              if ((c > 0 || off == 0) && c < C && !ace_is_count(p[c], make_float2(q[c].x, q[c].y))) {
-                j[c] = ace_fix_count(p[c], j[c], K, my_lohi, kTabCopies).i;
-                q[c] = entry(j[c]);
-              }
-          }
-#pragma unroll
-          for (int c = 0; c < CM; ++c) {
-            gp[c] = 0.0f;
-            if (c < C) {
-              if (c > 0 || off == 0) {
-                float y = 0.0f;
-                if constexpr (SOFT && LABELS) y = (lab[i] == c) ? 1.0f : 0.0f;
-                if constexpr (SOFT && !LABELS) y = yv[c][i];
-                gp[c] = grad_p<SOFT>(my_tab, rec_copies, c - off, K, j[c], q[c], p[c], y);
-              }
-              dot += p[c] * gp[c];
+        for (int c = 0; c < CM; ++c) {
+          gp[c] = 0.0f;
+          if (c < C) {
+            if (c > 0 || off == 0) {
+              float y = 0.0f;
+              if constexpr (SOFT && LABELS) y = (lab[i] == c) ? 1.0f : 0.0f;
+              if constexpr (SOFT && !LABELS) y = yv[c][i];
+              gp[c] = grad_p<SOFT>(my_tab, rec_copies, c - off, K, j[c], q[c], p[c], y);
             }
+            dot += p[c] * gp[c];
           }
         }
 #pragma unroll
@@ -1050,7 +1115,9 @@ struct GradLauncher {
       if (v.CM == 8 && v.V == 1) return L<T, 1, 8, true, S_, L_>::F(__VA_ARGS__);        \
       if (v.CM == 16 && v.V == 2) return L<T, 2, 16, true, S_, L_>::F(__VA_ARGS__);      \
       if (v.CM == 16 && v.V == 1) return L<T, 1, 16, true, S_, L_>::F(__VA_ARGS__);      \
+      if (v.CM == 32 && v.V == 2) return L<T, 2, 32, true, S_, L_>::F(__VA_ARGS__);      \
       if (v.CM == 32 && v.V == 1) return L<T, 1, 32, true, S_, L_>::F(__VA_ARGS__);      \
+      if (v.CM == 64 && v.V == 2) return L<T, 2, 64, true, S_, L_>::F(__VA_ARGS__);      \
       if (v.CM == 64 && v.V == 1) return L<T, 1, 64, true, S_, L_>::F(__VA_ARGS__);      \
     } else {                                                                              \
       if (v.V == VM) return L<T, VM, 1, false, S_, L_>::F(__VA_ARGS__);                  \
