@@ -129,7 +129,7 @@ Workspace carve(void* ws, int64_t b_total, int64_t cl, int K) {
 
 // Per-variant occupancy, cached (the query costs a few microseconds).
 struct OccKey {
-  int kind, dtype, V, CM, sm, soft, labels, smem, dev;
+  int kind, dtype, V, CM, sm, soft, labels, split, smem, dev;
   bool operator==(const OccKey& o) const { return memcmp(this, &o, sizeof(*this)) == 0; }
 };
 struct OccHash {
@@ -153,6 +153,7 @@ int occupancy(int kind, int dtype, const Variant& v, int smem, int dev) {
   key.sm = v.softmax;
   key.soft = v.soft;
   key.labels = v.labels;
+  key.split = v.split;
   key.smem = smem;
   key.dev = dev;
   {
@@ -227,6 +228,7 @@ Variant choose_variant(const ace_b200_inputs* in, const ace_b200_options* opt, c
   v.softmax = opt->activation == ACE_B200_ACT_SOFTMAX && in->C > 1;
   v.soft = opt->soft != 0;
   v.labels = in->target_kind == ACE_B200_TARGET_LABELS;
+  v.split = false;
   const int es = elem_size(in->x_dtype);
   const int vmax = 16 / es;
   int V;
@@ -343,11 +345,16 @@ int hist_impl(const ace_b200_inputs* in, const ace_b200_options* opt, float* his
   // replica takes at most (kHistThreads / R) * V additions per tile and must not
   // take more than 1023 between two folds (values up to 2^21 each), so R has a
   // floor; above it, as many replicas as fit in ~100 KB (32 = conflict-free),
-  // two CTAs per SM.
+  // two CTAs per SM. Soft binning with labels and a softmax over <= 4 channels
+  // takes the class-split kernel: slots (interval, class flag), 5 words each,
+  // and only the {base, scale} half of the bin table.
   const bool soft = opt->soft != 0;
-  const int words = soft ? (in->target_kind == ACE_B200_TARGET_LABELS ? 7 : 9) : 3;  // odd
-  const int entries = CL * (soft ? K + 1 : K) * words;
-  const size_t table_bytes = (size_t)(K + 1) * kTabCopies * sizeof(float4);
+  v.split = soft && v.softmax && v.labels && v.CM <= 4;
+  const int words =
+      v.split ? 5 : soft ? (in->target_kind == ACE_B200_TARGET_LABELS ? 7 : 9) : 3;  // odd
+  const int entries = CL * (v.split ? 2 * (K + 1) : soft ? K + 1 : K) * words;
+  const size_t table_bytes =
+      (size_t)(K + 1) * kTabCopies * (v.split ? sizeof(float2) : sizeof(float4));
   auto r_min = [&](int V) {
     int r = 1;
     while ((kHistThreads / r) * V > 1023) r <<= 1;
@@ -561,9 +568,9 @@ int ace_b200_backward(const ace_b200_inputs* in, const ace_b200_options* opt,
   const Variant v = choose_variant(in, opt, dx, false);
   const bool soft = opt->soft != 0;
   // Record copies: as many as fit in 96 KB (two CTAs per SM keep their tables).
-  int copies = soft ? 8 : 32;
+  int copies = soft ? 16 : 32;
   auto grad_smem = [&](int c) {
-    return (size_t)(K + 1) * kTabCopies * sizeof(float4) + (size_t)(soft ? 16 : 4) * c * CL * (K + 1);
+    return (size_t)(K + 1) * kTabCopies * sizeof(float2) + (size_t)(soft ? 8 : 4) * c * CL * (K + 1);
   };
   while (copies > 1 && grad_smem(copies) > 96 * 1024) copies /= 2;
   // the many-channel kernel keeps every channel's gp per thread: C x threads x V floats

@@ -3,9 +3,10 @@
 //
 // Everything that decides which bin a voxel lands in lives here, so the forward
 // and the backward kernels run the same instruction sequence on the same logits
-// and a voxel always falls in the same bin in both passes (the reference states
-// the same contract for its Triton kernels: ace_kernels/kernels/act.py:1-7,
-// ace_kernels/kernels/hard_bwd.py:9-11).
+// and, for hard binning, a voxel always falls in the same bin in both passes (the
+// reference states the same contract for its Triton kernels:
+// ace_kernels/kernels/act.py:1-7, ace_kernels/kernels/hard_bwd.py:9-11). Soft
+// binning needs no such contract: its weights are continuous in p.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -346,28 +347,40 @@ __device__ __forceinline__ void ace_softmax(float (&x)[CM], int C) {
     if (c < C) x[c] = ace_div_corrected(x[c], s, y);
 }
 
-// ---------------------------------------------------------------------------
-// Soft-binning weights (ace_kernels/common.py:43-61): distances to the interval
-// ends, span S = ld + rd, weights lw = rd / S (left bin), rw = ld / S (right
-// bin). The weights only feed floating-point sums compared with a tolerance, so
-// they take one approximate reciprocal of the span (shared with the backward's
-// 1/S) instead of the reference's two IEEE divisions: lw, rw within 2 ulp.
-// ---------------------------------------------------------------------------
-struct SoftW {
-  int l, r;
-  float lw, rw, inv_span;
-};
+// Softmax for soft binning, where no bin has to match the reference's bit for
+// bit: the soft weights are continuous in p, and the loss and gradient are
+// compared with a tolerance. exp is the hardware approximation (__expf: relative
+// error about 2^-22 + |x - m| 2^-23), the normalisation one approximate
+// reciprocal per voxel (1 ulp), so p is within a few ulp of the correctly rounded
+// softmax for the probabilities that carry weight. About a third of the
+// instructions of ace_softmax, and the same p in every kernel that calls it.
+__device__ __forceinline__ float ace_exp_fast(float v) { return __expf(v); }
 
-__device__ __forceinline__ SoftW ace_soft_weights(float p, int j, float2 lohi, int K) {
-  SoftW w;
-  const float ld = ACE_FSUB(p, lohi.x);
-  const float rd = ACE_FSUB(lohi.y, p);
-  w.inv_span = ace_rcp_approx(ACE_FADD(ld, rd));
-  w.lw = ACE_FMUL(rd, w.inv_span);
-  w.rw = ACE_FMUL(ld, w.inv_span);
-  w.l = max(j - 1, 0);
-  w.r = min(j, K - 1);
-  return w;
+template <int CM>
+__device__ __forceinline__ void ace_softmax_fast(float (&x)[CM], int C) {
+  float m = x[0];
+#pragma unroll
+  for (int c = 1; c < CM; ++c)
+    if (c < C) m = fmaxf(m, x[c]);
+  float s = 0.0f;
+#pragma unroll
+  for (int c = 0; c < CM; ++c) {
+    if (c < C) {
+      x[c] = ace_exp_fast(ACE_FSUB(x[c], m));
+      s = ACE_FADD(s, x[c]);
+    }
+  }
+  const float y = ace_rcp_approx(s);
+#pragma unroll
+  for (int c = 0; c < CM; ++c)
+    if (c < C) x[c] = ACE_FMUL(x[c], y);
+}
+
+// The softmax a kernel instance uses: fast for soft binning, exact otherwise.
+template <bool FAST, int CM>
+__device__ __forceinline__ void ace_softmax_sel(float (&x)[CM], int C) {
+  if constexpr (FAST) ace_softmax_fast<CM>(x, C);
+  else ace_softmax<CM>(x, C);
 }
 
 #endif  // __CUDACC__

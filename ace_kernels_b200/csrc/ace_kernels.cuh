@@ -18,6 +18,7 @@ struct Variant {
   bool softmax; // activation softmax over C > 1 channels (else none / sigmoid)
   bool soft;    // soft binning
   bool labels;  // int64 labels (else dense fp32 targets)
+  bool split;   // forward only: soft_hist_kernel (softmax, CM <= 4, soft, labels)
 };
 
 template <typename T>
@@ -192,6 +193,39 @@ struct Acc {
   static constexpr int NW = SOFT ? (LABELS ? 7 : 9) : 3;  // words per slot replica (odd)
   static constexpr int NOUT = SOFT ? 6 : 3;               // global sums per slot (stride)
   static constexpr int NFOLD = SOFT ? 5 : 3;              // global sums per slot (used)
+  // Global sum o of a slot: its word a (and low word b, or -1), and the word that
+  // counts its additions (cw; -1: the value is itself a count).
+  __device__ __forceinline__ static void words(int o, int& cw, int& a, int& b) {
+    if constexpr (!SOFT) {
+      cw = o == 0 || (o == 2 && LABELS) ? -1 : 0;
+      a = o;
+      b = -1;
+    } else if constexpr (LABELS) {  // words: 0 n, 1-2 u, 3 u^2, 4 ny, 5-6 u (true class)
+      cw = (o == 0 || o == 3) ? -1 : (o == 4 ? 4 : 0);
+      a = o == 0 ? 0 : o == 1 ? 1 : o == 2 ? 3 : o == 3 ? 4 : 5;
+      b = o == 1 ? 2 : o == 4 ? 6 : -1;
+    } else {  // words: 0 n, 1-2 u, 3 u^2, 4-5 y, 6-7 u y
+      cw = o == 0 ? -1 : 0;
+      a = o == 0 ? 0 : o == 1 ? 1 : o == 2 ? 3 : o == 3 ? 4 : 6;
+      b = o == 1 ? 2 : o == 3 ? 5 : o == 4 ? 7 : -1;
+    }
+  }
+};
+
+// Soft binning with class labels and a register-tile softmax (soft_hist_kernel):
+// the slots are (interval j, class flag t), slot 2 j + t, where t = 1 when the row
+// is the voxel's class. Every value then makes exactly one update of four words,
+// 0 n, 1-2 u, 3 u^2 (word 4 pads the stride to an odd count), and the target
+// moments are the t = 1 slot's n and u: no second update for the true class.
+struct AccSplit {
+  static constexpr int NW = 5;
+  static constexpr int NOUT = 3;  // n, sum u, sum u^2 per slot
+  static constexpr int NFOLD = 3;
+  __device__ __forceinline__ static void words(int o, int& cw, int& a, int& b) {
+    cw = o == 0 ? -1 : 0;
+    a = o == 0 ? 0 : o == 1 ? 1 : 3;
+    b = o == 1 ? 2 : -1;
+  }
 };
 
 constexpr float kFixMagic = 12582912.0f;         // 1.5 * 2^23
@@ -225,11 +259,11 @@ __device__ __forceinline__ unsigned fix1(float v) {
 // additions holds the exact value (int)(w - cnt * 0x4B400000); count words hold
 // their value. The word selection is branch-free, so the lanes of a warp, which
 // take different sums, do not diverge. Called by all threads between barriers.
-template <bool SOFT, bool LABELS>
+template <class L>
 __device__ __forceinline__ void fold_table(unsigned* hist, int CL, int slots, int R,
                                            double* accum, int64_t out_stride, int64_t row0) {
-  constexpr int NW = Acc<SOFT, LABELS>::NW;
-  constexpr int NF = Acc<SOFT, LABELS>::NFOLD;
+  constexpr int NW = L::NW;
+  constexpr int NF = L::NFOLD;
   const int G = R >= 4 ? 4 : 1;
   const int per = R / G;
   const double unit = 1.0 / (double)kFixScale;
@@ -242,19 +276,7 @@ __device__ __forceinline__ void fold_table(unsigned* hist, int CL, int slots, in
     // cw: word counting the value's additions (-1: the value is a count); a, b:
     // its words (b < 0: one word)
     int cw, a, b;
-    if constexpr (!SOFT) {
-      cw = o == 0 || (o == 2 && LABELS) ? -1 : 0;
-      a = o;
-      b = -1;
-    } else if constexpr (LABELS) {  // words: 0 n, 1-2 u, 3 u^2, 4 ny, 5-6 u (true class)
-      cw = (o == 0 || o == 3) ? -1 : (o == 4 ? 4 : 0);
-      a = o == 0 ? 0 : o == 1 ? 1 : o == 2 ? 3 : o == 3 ? 4 : 5;
-      b = o == 1 ? 2 : o == 4 ? 6 : -1;
-    } else {  // words: 0 n, 1-2 u, 3 u^2, 4-5 y, 6-7 u y
-      cw = o == 0 ? -1 : 0;
-      a = o == 0 ? 0 : o == 1 ? 1 : o == 2 ? 3 : o == 3 ? 4 : 6;
-      b = o == 1 ? 2 : o == 3 ? 5 : o == 4 ? 7 : -1;
-    }
+    L::words(o, cw, a, b);
     const unsigned mul = cw < 0 ? 0u : kFixMagicBits;
     const int cwi = cw < 0 ? a : cw, bi = b < 0 ? a : b;
     const long long hs = b < 0 ? 1ll : (long long)kFixScale;
@@ -469,7 +491,7 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constan
   for (int64_t g = g0; g < g1; ++g, ++t) {
     if (t == tpb) {  // next batch: fold this batch's rows first
       __syncthreads();
-      fold_table<SOFT, LABELS>(hist, CL, slots, R, P.accum, out_stride, row0);
+      fold_table<Acc<SOFT, LABELS>>(hist, CL, slots, R, P.accum, out_stride, row0);
       __syncthreads();
       since_fold = 0;
       ++b;
@@ -632,13 +654,13 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constan
     if (++since_fold == P.flush_tiles && g + 1 < g1) {
       since_fold = 0;
       __syncthreads();
-      fold_table<SOFT, LABELS>(hist, CL, slots, R, P.accum, out_stride, row0);
+      fold_table<Acc<SOFT, LABELS>>(hist, CL, slots, R, P.accum, out_stride, row0);
       __syncthreads();
     }
   }
   ace_launch_dependents();  // a dependent launch may begin its own setup now
   __syncthreads();
-  fold_table<SOFT, LABELS>(hist, CL, slots, R, P.accum, out_stride, row0);
+  fold_table<Acc<SOFT, LABELS>>(hist, CL, slots, R, P.accum, out_stride, row0);
   __syncthreads();
   __shared__ bool s_last;
   if (tid == 0) {
@@ -726,34 +748,211 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constan
 }
 
 // ---------------------------------------------------------------------------
+// Forward for soft binning with class labels and a softmax over C <= 4 channels
+// (the register-tile case): the same tiling, table replicas, folds and last-CTA
+// handoff as hist_kernel, with fewer instructions per value:
+// - the fast softmax (ace_softmax_fast);
+// - the interval is the rounded p K of the saturated p (NaN -> 0), so it lies in
+//   [0, K] without a clamp and without the exact test (see soft_entry above);
+// - slots split by class flag (AccSplit): one update of four words per value,
+//   and no per-voxel update for the true class.
+// The last CTA merges the two slots of each interval into the n, sum t, sum t^2,
+// ny, sum t y moments of hist_kernel's reconstruction.
+// ---------------------------------------------------------------------------
+template <typename T, int V, int C>
+__global__ void __launch_bounds__(kHistThreads) soft_hist_kernel(const __grid_constant__ FwdParams P) {
+  using L = AccSplit;
+  constexpr int NW = L::NW;
+  extern __shared__ __align__(16) float smem[];
+  const int tid = threadIdx.x;
+  const int CL = P.g.CL, off = P.g.offset, K = P.tab.K;
+  const int slots = 2 * (K + 1);
+  const int64_t N = P.g.N;
+  const int R = P.R;
+  const float Kf = (float)K;
+
+  float2* map_t = reinterpret_cast<float2*>(smem);
+  unsigned* hist = reinterpret_cast<unsigned*>(map_t + (K + 1) * kTabCopies);
+  const int table_words = CL * slots * R * NW;
+  for (int i = tid; i < (K + 1) * kTabCopies; i += kHistThreads) map_t[i] = P.tab.map[i / kTabCopies];
+  const float2* my_map = map_t + (tid & (kTabCopies - 1));
+  {
+    uint4* h4 = reinterpret_cast<uint4*>(hist);  // 16-byte aligned: (K + 1) * 128 bytes in
+    for (int i = tid; i < table_words / 4; i += kHistThreads) h4[i] = make_uint4(0u, 0u, 0u, 0u);
+    for (int i = (table_words & ~3) + tid; i < table_words; i += kHistThreads) hist[i] = 0u;
+  }
+  ace_grid_dependency_wait();  // programmatic dependent launch (see hist_kernel)
+  __syncthreads();
+
+  const int slot_stride = R * NW, row_stride = slots * slot_stride;
+  // word offset of row (c - off), interval 0, flag 0, this lane's replica
+  const int col = (tid & (R - 1)) * NW - off * row_stride;
+  const int64_t out_stride = (int64_t)P.B_total * CL * slots;
+
+  const int64_t tpb = P.g.tiles > 0 ? P.g.tiles : 1;
+  int64_t g0, g1;
+  chunk_range(P.g, g0, g1);
+  int since_fold = 0;
+  const int64_t tile = (int64_t)kHistThreads * V;
+  const bool pf_x = ((reinterpret_cast<uintptr_t>(P.x) | (N * sizeof(T))) & 15) == 0;
+  int b = (int)(g0 / tpb);
+  int64_t t = g0 - b * tpb;
+  const T* xb = static_cast<const T*>(P.x) + (int64_t)b * C * N;
+  const int64_t* lb = static_cast<const int64_t*>(P.target) + (int64_t)b * N;
+  int64_t row0 = (int64_t)(P.b_offset + b) * CL;
+  for (int64_t g = g0; g < g1; ++g, ++t) {
+    if (t == tpb) {  // next batch: fold this batch's rows first
+      __syncthreads();
+      fold_table<L>(hist, CL, slots, R, P.accum, out_stride, row0);
+      __syncthreads();
+      since_fold = 0;
+      ++b;
+      t = 0;
+      xb = static_cast<const T*>(P.x) + (int64_t)b * C * N;
+      lb = static_cast<const int64_t*>(P.target) + (int64_t)b * N;
+      row0 = (int64_t)(P.b_offset + b) * CL;
+    }
+    if (t + 1 < tpb && g + 1 < g1 && pf_x) {
+      if (tid < C) ace_prefetch_tile(xb + (int64_t)tid * N, (t + 1) * tile, tile, N, sizeof(T));
+      if (tid == C) ace_prefetch_tile(lb, (t + 1) * tile, tile, N, 8);
+    }
+    const int64_t v0 = (t * kHistThreads + tid) * V;
+    if (v0 < N) {  // V > 1 implies N % V == 0: groups are whole
+      int lab[V];
+      ace_load_labels<V>(lb + v0, lab);
+      float xv[C][V];
+#pragma unroll
+      for (int c = 0; c < C; ++c) VecIO<T, V>::load(xb + (int64_t)c * N + v0, xv[c]);
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        float p[C];
+#pragma unroll
+        for (int c = 0; c < C; ++c) p[c] = xv[c][i];
+        ace_softmax_fast<C>(p, C);
+#pragma unroll
+        for (int c = 0; c < C; ++c) {
+          if (c < off) continue;
+          const int j = (int)(__float_as_uint(__fmaf_rn(__saturatef(p[c]), Kf, kFixMagic)) -
+                              kFixMagicBits);
+          const float2 m = my_map[j * kTabCopies];
+          const float us = fminf(ACE_FMUL(ACE_FSUB(p[c], m.x), m.y), kFixScale);
+          const int a = col + c * row_stride + j * (2 * slot_stride) + (lab[i] == c ? slot_stride : 0);
+          const uint2 uw = fix2_scaled(us);
+          sadd(hist, a, 1u);
+          sadd(hist, a + 1, uw.x);
+          sadd(hist, a + 2, uw.y);
+          sadd(hist, a + 3, __float_as_uint(__fmaf_rn(us, ACE_FMUL(us, 1.0f / kFixScale), kFixMagic)));
+        }
+      }
+    }
+    if (++since_fold == P.flush_tiles && g + 1 < g1) {
+      since_fold = 0;
+      __syncthreads();
+      fold_table<L>(hist, CL, slots, R, P.accum, out_stride, row0);
+      __syncthreads();
+    }
+  }
+  ace_launch_dependents();
+  __syncthreads();
+  fold_table<L>(hist, CL, slots, R, P.accum, out_stride, row0);
+  __syncthreads();
+  __shared__ bool s_last;
+  if (tid == 0) {
+    unsigned done;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
+                 : "=r"(done)
+                 : "l"(P.counter)
+                 : "memory");
+    s_last = (done == gridDim.x * gridDim.y - 1);
+  }
+  __syncthreads();
+  if (!s_last) return;
+
+  // Last CTA: W, P, G per bin from the interval moments (as hist_kernel), each
+  // interval's moments being the sum of its two class-flag slots, and its target
+  // moments those of the flag-1 slot.
+  const int rows = P.B_total * CL;
+  const int64_t stat_stride = (int64_t)rows * K;
+  const bool stage = P.do_epilogue && 3 * stat_stride <= (int64_t)table_words;
+  float* staged = reinterpret_cast<float*>(hist);
+  const double* acc = P.accum;
+  for (int64_t e = tid; e < stat_stride; e += kHistThreads) {
+    const int64_t r = e / K;
+    const int k = (int)(e - r * K);
+    double w = 0.0, pp = 0.0, gsum = 0.0;
+    for (int side = 0; side < 2; ++side) {
+      const int j = k + side;
+      const int64_t gi = r * slots + 2 * j;
+      const double ny = __ldcg(acc + gi + 1), yu = __ldcg(acc + out_stride + gi + 1);
+      const double n = __ldcg(acc + gi) + ny;
+      const double su = __ldcg(acc + out_stride + gi) + yu;
+      if (j == 0 || j == K) {
+        w += n;
+        pp += su;
+        gsum += ny;
+        continue;
+      }
+      const double su2 = __ldcg(acc + 2 * out_stride + gi) + __ldcg(acc + 2 * out_stride + gi + 1);
+      const double lo = P.tab.lohi[j].x, span = (double)P.tab.lohi[j].y - lo;
+      const double pt = lo * su + span * su2;
+      if (side == 0) {
+        w += su;
+        pp += pt;
+        gsum += yu;
+      } else {
+        w += n - su;
+        pp += lo * n + span * su - pt;
+        gsum += ny - yu;
+      }
+    }
+    const float wf = (float)w, pf = (float)pp, gf = (float)gsum;
+    P.hist_out[e] = wf;
+    P.hist_out[stat_stride + e] = pf;
+    P.hist_out[2 * stat_stride + e] = gf;
+    if (stage) {
+      staged[e] = wf;
+      staged[stat_stride + e] = pf;
+      staged[2 * stat_stride + e] = gf;
+    }
+  }
+  __syncthreads();
+  double* accw = P.accum;
+  for (int64_t i = tid; i < L::NOUT * out_stride; i += kHistThreads) __stcg(accw + i, 0.0);
+  if (tid == 0) *P.counter = 0u;
+  if (stage) {
+    __syncthreads();
+    write_loss_if0(P.epi, epilogue_rows(P.epi, staged, rows, 0, 0, rows));
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Backward: d loss / d x in one pass (ace_kernels/impls/v2_autograd.py:88-118,
 // derivation in the reference's docs/derivation.md):
 //   hard: gp_c = g_bc * coef[b, c, bin(p_c)]
 //   soft: gp_c = g_bc * (coef_l (lw - (p - y - d_l) / S) + coef_r (rw + (p - y - d_r) / S))
 //   softmax: dx_c = p_c (gp_c - sum_c' p_c' gp_c'); sigmoid: gp p (1 - p); none: gp
 // with gp = 0 on a dropped background channel. The activation and the bins are
-// recomputed with the forward's code (same bins). Per CTA, the rows of its batch
-// sit in shared memory with g folded in: hard, cg[row][k] = g coef (0 past the
-// last bin); soft, one record per interval j, {g coef_l, d_l, g coef_r, d_r} of
-// its two bins, read with one 16-byte load. Hard binning reads no targets.
+// recomputed (hard binning: with the forward's code, so the same bins). Per CTA,
+// the rows of its batch sit in shared memory with g folded in: hard, cg[row][k] =
+// g coef (0 past the last bin); soft, one record {F, D} per row and interval j.
+// Inside interval j (centres lo = c_{j-1}, hi = c_j, S = hi - lo, inv = 1 / S) the
+// weights are rw = (p - lo) inv and lw = 1 - rw, so with A = g coef_l,
+// B = g coef_r the soft formula is affine in p and y:
+//   gp = A + (B - A) inv (p - lo) + (B - A) inv (p - y) + inv (A d_l - B d_r)
+//      = F + D (2 p - y),  D = (B - A) inv,  F = A - D lo + inv (A d_l - B d_r).
+// In the two end intervals both sides are the same bin: D = 0, F = g coef. The
+// records are built in double precision and rounded once; one 8-byte load and
+// two FMAs per value remain. Hard binning reads no targets.
 // ---------------------------------------------------------------------------
-// q = table entry of the value's interval: {lo, hi, base, 2^21 / S} (soft).
-// Inside an interval the weights are rw = t = (p - lo) / S, lw = 1 - t and
-// d w / d p = -+ 1 / S; in an end interval both sides are the same bin, where the
-// formula reduces to g coef for any weights summing to 1 (there u = p, 1 / S = 1).
 template <bool SOFT>
 __device__ __forceinline__ float grad_p(const float* __restrict__ tab, int copies, int row, int K,
-                                        int j, float4 q, float p, float y) {
+                                        int j, float p, float y) {
   // `tab` points at this lane's copy; entries are `copies` apart.
   if constexpr (!SOFT) {
     return tab[(row * (K + 1) + j) * copies];
   } else {
-    const float4 rec = reinterpret_cast<const float4*>(tab)[(row * (K + 1) + j) * copies];
-    const float inv = q.w * (1.0f / kFixScale);
-    const float rw = (p - q.z) * inv;
-    const float lw = 1.0f - rw;
-    const float resid = p - y;
-    return rec.x * (lw - inv * (resid - rec.y)) + rec.z * (rw + inv * (resid - rec.w));
+    const float2 rec = reinterpret_cast<const float2*>(tab)[(row * (K + 1) + j) * copies];
+    return __fmaf_rn(rec.y, __fmaf_rn(2.0f, p, -y), rec.x);
   }
 }
 
@@ -767,20 +966,16 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const __grid_constant__ 
   const float Kf = (float)K;
 
   // Tables in interleaved copies so that the lanes of one load phase rarely share
-  // banks (random-index gathers): the bin tables in kTabCopies copies, the
-  // per-row records in up to 8 copies (16-byte records, 8 lanes a phase) or the
+  // banks (random-index gathers): the bin table in kTabCopies copies, the per-row
+  // soft records in up to 16 copies (8-byte records, 16 lanes a phase) or the
   // hard g coef table in up to 32 copies (4-byte values, 32 lanes a phase); the
   // host lowers P.rec_copies (a power of two) when many rows would not fit.
-  float* tab = smem;  // [CL][K+1][copies] floats (hard) or float4 (soft)
+  float* tab = smem;  // [CL][K+1][copies] floats (hard) or float2 (soft)
   const int rec_copies = P.rec_copies;
-  float2* lohi_t = reinterpret_cast<float2*>(tab + (SOFT ? 4 : 1) * CL * (K + 1) * rec_copies);
-  float2* map_t = lohi_t + (K + 1) * kTabCopies;
+  float2* lohi_t = reinterpret_cast<float2*>(tab + (SOFT ? 2 : 1) * CL * (K + 1) * rec_copies);
   // many channels: per-thread gp of every channel, [c][thread][V] (fp32)
-  float* gscratch = reinterpret_cast<float*>(map_t + (K + 1) * kTabCopies);
-  for (int i = tid; i < (K + 1) * kTabCopies; i += kThreads) {
-    lohi_t[i] = P.tab.lohi[i / kTabCopies];
-    map_t[i] = P.tab.map[i / kTabCopies];
-  }
+  float* gscratch = reinterpret_cast<float*>(lohi_t + (K + 1) * kTabCopies);
+  for (int i = tid; i < (K + 1) * kTabCopies; i += kThreads) lohi_t[i] = P.tab.lohi[i / kTabCopies];
   // programmatic dependent launch: global memory only after the previous grid
   ace_grid_dependency_wait();
   const int64_t row0 = (int64_t)(P.b_offset + b) * CL;
@@ -794,22 +989,32 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const __grid_constant__ 
       tab[e] = j < K ? g * cf[j] : 0.0f;
     } else {
       const int l = max(j - 1, 0), r = min(j, K - 1);
-      reinterpret_cast<float4*>(tab)[e] = make_float4(g * cf[l], dd[l], g * cf[r], dd[r]);
+      const float a = g * cf[l], bb = g * cf[r];
+      float2 rec = make_float2(a, 0.0f);
+      if (j > 0 && j < K) {
+        const double lo = P.tab.map[j].x, inv = (double)P.tab.map[j].y / (double)kFixScale;
+        const double dd_ = ((double)bb - (double)a) * inv;
+        const double e_ = inv * ((double)a * dd[l] - (double)bb * dd[r]);
+        rec = make_float2((float)((double)a - dd_ * lo + e_), (float)dd_);
+      }
+      reinterpret_cast<float2*>(tab)[e] = rec;
     }
   }
   __syncthreads();
-  const float* my_tab = tab + (SOFT ? 4 : 1) * (tid & (rec_copies - 1));
+  const float* my_tab = tab + (SOFT ? 2 : 1) * (tid & (rec_copies - 1));
   const float2* my_lohi = lohi_t + (tid & (kTabCopies - 1));
-  const float2* my_map = map_t + (tid & (kTabCopies - 1));
 
-  auto entry = [&](int j) -> float4 {
-    const float2 lh = my_lohi[j * kTabCopies];
-    if constexpr (SOFT) {
-      const float2 m = my_map[j * kTabCopies];
-      return make_float4(lh.x, lh.y, m.x, m.y);
-    } else {
-      return make_float4(lh.x, lh.y, 0.0f, 0.0f);
-    }
+  auto entry = [&](int j) -> float2 { return my_lohi[j * kTabCopies]; };
+  // Many-channel passes: one value's exponential and probability, the same
+  // operations as ace_softmax_sel (fast for soft binning, exact for hard).
+  auto exp_c = [](float v) -> float {
+    if constexpr (SOFT) return ace_exp_fast(v);
+    else return expf(v);
+  };
+  auto expf_c = [&](float x, float m) -> float { return exp_c(ACE_FSUB(x, m)); };
+  auto prob_c = [](float e, float s, float r) -> float {
+    if constexpr (SOFT) return ACE_FMUL(e, r);
+    else return ace_div_corrected(e, s, r);
   };
 
   const T* xb = static_cast<const T*>(P.x) + (int64_t)b * C * N;
@@ -853,11 +1058,11 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const __grid_constant__ 
         float x[V];
         VecIO<T, V>::load(xr + (int64_t)c * N, x);
 #pragma unroll
-        for (int i = 0; i < V; ++i) sm[i] = ACE_FADD(sm[i], expf(ACE_FSUB(x[i], m[i])));
+        for (int i = 0; i < V; ++i) sm[i] = ACE_FADD(sm[i], exp_c(ACE_FSUB(x[i], m[i])));
       }
 #pragma unroll
       for (int i = 0; i < V; ++i) {
-        rc[i] = ace_rcp_refined(sm[i]);
+        rc[i] = SOFT ? ace_rcp_approx(sm[i]) : ace_rcp_refined(sm[i]);
         dot[i] = 0.0f;
       }
       float* gs = gscratch + tid * V;
@@ -871,7 +1076,7 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const __grid_constant__ 
         }
 #pragma unroll
         for (int i = 0; i < V; ++i) {
-          const float p = ace_div_corrected(expf(ACE_FSUB(x[i], m[i])), sm[i], rc[i]);
+          const float p = prob_c(expf_c(x[i], m[i]), sm[i], rc[i]);
           float gp = 0.0f;
           if (c >= off) {
             float2 lh;
@@ -879,7 +1084,7 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const __grid_constant__ 
             float y = 0.0f;
             if constexpr (SOFT && LABELS) y = (lab[i] == c) ? 1.0f : 0.0f;
             if constexpr (SOFT && !LABELS) y = yv[i];
-            gp = grad_p<SOFT>(my_tab, rec_copies, c - off, K, jc, entry(jc), p, y);
+            gp = grad_p<SOFT>(my_tab, rec_copies, c - off, K, jc, p, y);
           }
           dot[i] += p * gp;
           gs[c * gstride + i] = gp;
@@ -891,7 +1096,7 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const __grid_constant__ 
         VecIO<T, V>::load(xr + (int64_t)c * N, x);
 #pragma unroll
         for (int i = 0; i < V; ++i) {
-          const float p = ace_div_corrected(expf(ACE_FSUB(x[i], m[i])), sm[i], rc[i]);
+          const float p = prob_c(expf_c(x[i], m[i]), sm[i], rc[i]);
           o[i] = p * (gs[c * gstride + i] - dot[i]);
         }
         VecIO<T, V>::store(db + (int64_t)c * N + v0, o);
@@ -912,27 +1117,23 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const __grid_constant__ 
         float p[CM];
 #pragma unroll
         for (int c = 0; c < CM; ++c) p[c] = xv[c][i];
-        ace_softmax<CM>(p, C);
+        ace_softmax_sel<SOFT, CM>(p, C);
         float gp[CM];
         float dot = 0.0f;
         int j[CM];
-        float4 q[CM];
         bool ok = true;
 #pragma unroll
         for (int c = 0; c < CM; ++c) {
           if ((c > 0 || off == 0) && c < C) {
             j[c] = ace_guess(p[c], Kf, K, SOFT);
-            q[c] = entry(j[c]);
-            ok &= ace_is_count(p[c], make_float2(q[c].x, q[c].y));
+            ok &= ace_is_count(p[c], entry(j[c]));
           }
         }
         if (!ok) {
 #pragma unroll
           for (int c = 0; c < CM; ++c)
-            if ((c > 0 || off == 0) && c < C && !ace_is_count(p[c], make_float2(q[c].x, q[c].y))) {
+            if ((c > 0 || off == 0) && c < C && !ace_is_count(p[c], entry(j[c])))
               j[c] = ace_fix_count(p[c], j[c], K, my_lohi, kTabCopies).i;
-              q[c] = entry(j[c]);
-            }
         }
 #pragma unroll
         for (int c = 0; c < CM; ++c) {
@@ -942,7 +1143,7 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const __grid_constant__ 
               float y = 0.0f;
               if constexpr (SOFT && LABELS) y = (lab[i] == c) ? 1.0f : 0.0f;
               if constexpr (SOFT && !LABELS) y = yv[c][i];
-              gp[c] = grad_p<SOFT>(my_tab, rec_copies, c - off, K, j[c], q[c], p[c], y);
+              gp[c] = grad_p<SOFT>(my_tab, rec_copies, c - off, K, j[c], p[c], y);
             }
             dot += p[c] * gp[c];
           }
@@ -975,7 +1176,7 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const __grid_constant__ 
           if constexpr (SOFT && !LABELS) y = yv[i];
           float2 lh;
           const int j = ace_locate(p, my_lohi, kTabCopies, K, Kf, SOFT, lh);
-          const float gp = grad_p<SOFT>(my_tab, rec_copies, c - off, K, j, entry(j), p, y);
+          const float gp = grad_p<SOFT>(my_tab, rec_copies, c - off, K, j, p, y);
           xv[i] = sig ? gp * p * (1.0f - p) : gp;
         }
         VecIO<T, V>::store(db + (int64_t)c * N + v0, xv);
@@ -1074,6 +1275,27 @@ struct HistLauncher {
   }
 };
 
+template <typename T, int V, int C>
+struct SoftHistLauncher {
+  static int& configured() {
+    static int bytes = 0;
+    return bytes;
+  }
+  static cudaError_t run(const FwdParams& p, dim3 grid, int smem, cudaStream_t s) {
+    auto k = soft_hist_kernel<T, V, C>;
+    cudaError_t e = set_smem(k, smem, configured());
+    if (e != cudaSuccess) return e;
+    return launch_dependent(k, grid, kHistThreads, smem, s, p);
+  }
+  static int occupancy(int smem) {
+    auto k = soft_hist_kernel<T, V, C>;
+    set_smem(k, smem, configured());
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, kHistThreads, smem) != cudaSuccess) n = 1;
+    return n > 0 ? n : 1;
+  }
+};
+
 template <typename T, int V, int CM, bool SM, bool SOFT, bool LAB>
 struct GradLauncher {
   static int& configured() {
@@ -1140,9 +1362,25 @@ struct GradLauncher {
     BODY;                                                \
   }
 
+// The class-split soft forward: exact channel counts 2..4, full or single vectors.
+#define ACE_SPLIT_CASES(F, T, ...)                                                        \
+  do {                                                                                    \
+    constexpr int VM = 16 / (int)sizeof(T);                                               \
+    if (v.split) {                                                                        \
+      if (v.CM == 2 && v.V == VM) return SoftHistLauncher<T, VM, 2>::F(__VA_ARGS__);     \
+      if (v.CM == 2 && v.V == 1) return SoftHistLauncher<T, 1, 2>::F(__VA_ARGS__);       \
+      if (v.CM == 3 && v.V == VM) return SoftHistLauncher<T, VM, 3>::F(__VA_ARGS__);     \
+      if (v.CM == 3 && v.V == 1) return SoftHistLauncher<T, 1, 3>::F(__VA_ARGS__);       \
+      if (v.CM == 4 && v.V == VM) return SoftHistLauncher<T, VM, 4>::F(__VA_ARGS__);     \
+      if (v.CM == 4 && v.V == 1) return SoftHistLauncher<T, 1, 4>::F(__VA_ARGS__);       \
+    }                                                                                     \
+  } while (0)
+
 template <typename T>
 cudaError_t launch_hist(const FwdParams& p, const Variant& v, dim3 grid, int smem,
                         cudaStream_t s) {
+  ACE_SPLIT_CASES(run, T, p, grid, smem, s);
+  if (v.split) return cudaErrorInvalidValue;
   ACE_FOR_SOFT_LABELS(ACE_VARIANT_CASES(HistLauncher, run, T, p, grid, smem, s));
   return cudaErrorInvalidValue;
 }
@@ -1156,6 +1394,8 @@ cudaError_t launch_grad(const BwdParams& p, const Variant& v, dim3 grid, int sme
 
 template <typename T>
 int hist_occupancy(const Variant& v, int smem) {
+  ACE_SPLIT_CASES(occupancy, T, smem);
+  if (v.split) return 1;
   ACE_FOR_SOFT_LABELS(ACE_VARIANT_CASES(HistLauncher, occupancy, T, smem));
   return 1;
 }
