@@ -219,13 +219,7 @@ struct Acc {
 // moments are the t = 1 slot's n and u: no second update for the true class.
 struct AccSplit {
   static constexpr int NW = 5;
-  static constexpr int NOUT = 3;  // n, sum u, sum u^2 per slot
-  static constexpr int NFOLD = 3;
-  __device__ __forceinline__ static void words(int o, int& cw, int& a, int& b) {
-    cw = o == 0 ? -1 : 0;
-    a = o == 0 ? 0 : o == 1 ? 1 : 3;
-    b = o == 1 ? 2 : -1;
-  }
+  static constexpr int NOUT = 3;  // n, sum u, sum u^2 per slot (fold_split)
 };
 
 constexpr float kFixMagic = 12582912.0f;         // 1.5 * 2^23
@@ -306,6 +300,62 @@ __device__ __forceinline__ void fold_table(unsigned* hist, int CL, int slots, in
   uint4* h4 = reinterpret_cast<uint4*>(hist);
   for (int i = threadIdx.x; i < words / 4; i += blockDim.x) h4[i] = make_uint4(0u, 0u, 0u, 0u);
   for (int i = (words & ~3) + threadIdx.x; i < words; i += blockDim.x) hist[i] = 0u;
+}
+
+// Fold of the class-split soft table (AccSplit): item i takes slot e = i / G of
+// the [CL * slots] slots and a quarter (G = 4) of its R replicas, reads the four
+// words of each replica at once, removes the fixed-point bias with the replica's
+// count and adds exactly in 64-bit integers; the G lanes of a slot combine their
+// parts with shuffles and the first issues one fp64 atomic per non-zero sum
+// (n, sum u, sum u^2). No divisions by runtime values: G and the slot count per
+// item round are powers of two or loop strides. `clear`: zero the table after
+// the fold (not needed when the CTA is done with it). Called by all threads
+// between barriers.
+__device__ __forceinline__ void fold_split(unsigned* hist, int entries, int R, double* accum,
+                                           int64_t out_stride, int64_t row_base, bool clear) {
+  constexpr int NW = AccSplit::NW;
+  const int gsh = R >= 4 ? 2 : (R == 2 ? 1 : 0);
+  const int G = 1 << gsh, per = R >> gsh;
+  const double unit = 1.0 / (double)kFixScale;
+  const int total = entries << gsh;
+  for (int i0 = 0; i0 < total; i0 += blockDim.x) {  // uniform trip count: full-warp shuffles
+    const int i = i0 + (int)threadIdx.x;
+    const bool valid = i < total;
+    const int e = valid ? i >> gsh : 0, part = i & (G - 1);
+    const unsigned* base = hist + e * R * NW;
+    long long hi = 0, lo = 0, q = 0;
+    int n = 0;
+    if (valid) {
+      for (int k = 0; k < per; ++k) {
+        const unsigned* w = base + ((part * per + k + e) & (R - 1)) * NW;
+        const unsigned cnt = w[0];
+        const unsigned bias = cnt * kFixMagicBits;
+        n += (int)cnt;
+        hi += (int)(w[1] - bias);
+        lo += (int)(w[2] - bias);
+        q += (int)(w[3] - bias);
+      }
+    }
+    for (int o = 1; o < G; o <<= 1) {
+      n += __shfl_xor_sync(0xffffffffu, n, o);
+      hi += __shfl_xor_sync(0xffffffffu, hi, o);
+      lo += __shfl_xor_sync(0xffffffffu, lo, o);
+      q += __shfl_xor_sync(0xffffffffu, q, o);
+    }
+    if (valid && part == 0 && n != 0) {
+      double* a = accum + row_base + e;  // [3][rows * slots]: e = row * slots + slot
+      atomicAdd(a, (double)n);
+      atomicAdd(a + out_stride, (double)(hi * (long long)kFixScale + lo) * (unit * unit));
+      atomicAdd(a + 2 * out_stride, (double)q * unit);
+    }
+  }
+  if (clear) {
+    __syncthreads();
+    const int words = entries * R * NW;
+    uint4* h4 = reinterpret_cast<uint4*>(hist);
+    for (int i = threadIdx.x; i < words / 4; i += blockDim.x) h4[i] = make_uint4(0u, 0u, 0u, 0u);
+    for (int i = (words & ~3) + threadIdx.x; i < words; i += blockDim.x) hist[i] = 0u;
+  }
 }
 
 // Channel count of a kernel instance: exact for softmax instances with CM <= 4
@@ -803,7 +853,7 @@ __global__ void __launch_bounds__(kHistThreads) soft_hist_kernel(const __grid_co
   for (int64_t g = g0; g < g1; ++g, ++t) {
     if (t == tpb) {  // next batch: fold this batch's rows first
       __syncthreads();
-      fold_table<L>(hist, CL, slots, R, P.accum, out_stride, row0);
+      fold_split(hist, CL * slots, R, P.accum, out_stride, row0 * slots, true);
       __syncthreads();
       since_fold = 0;
       ++b;
@@ -848,13 +898,13 @@ __global__ void __launch_bounds__(kHistThreads) soft_hist_kernel(const __grid_co
     if (++since_fold == P.flush_tiles && g + 1 < g1) {
       since_fold = 0;
       __syncthreads();
-      fold_table<L>(hist, CL, slots, R, P.accum, out_stride, row0);
+      fold_split(hist, CL * slots, R, P.accum, out_stride, row0 * slots, true);
       __syncthreads();
     }
   }
   ace_launch_dependents();
   __syncthreads();
-  fold_table<L>(hist, CL, slots, R, P.accum, out_stride, row0);
+  fold_split(hist, CL * slots, R, P.accum, out_stride, row0 * slots, false);
   __syncthreads();
   __shared__ bool s_last;
   if (tid == 0) {
