@@ -572,7 +572,9 @@ int ace_b200_backward(const ace_b200_inputs* in, const ace_b200_options* opt,
   auto grad_smem = [&](int c) {
     return (size_t)(K + 1) * kTabCopies * sizeof(float2) + (size_t)(soft ? 8 : 4) * c * CL * (K + 1);
   };
-  while (copies > 1 && grad_smem(copies) > 96 * 1024) copies /= 2;
+  // (at least one 16-byte store of copies per record: 2 soft, 4 hard)
+  const int min_copies = soft ? 2 : 4;
+  while (copies > min_copies && grad_smem(copies) > 96 * 1024) copies /= 2;
   // the many-channel kernel keeps every channel's gp per thread: C x threads x V floats
   const size_t scratch =
       (v.softmax && v.CM > 4) ? (size_t)in->C * kThreads * v.V * sizeof(float) : 0;

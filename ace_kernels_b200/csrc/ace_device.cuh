@@ -349,12 +349,26 @@ __device__ __forceinline__ void ace_softmax(float (&x)[CM], int C) {
 
 // Softmax for soft binning, where no bin has to match the reference's bit for
 // bit: the soft weights are continuous in p, and the loss and gradient are
-// compared with a tolerance. exp is the hardware approximation (__expf: relative
-// error about 2^-22 + |x - m| 2^-23), the normalisation one approximate
-// reciprocal per voxel (1 ulp), so p is within a few ulp of the correctly rounded
-// softmax for the probabilities that carry weight. About a third of the
-// instructions of ace_softmax, and the same p in every kernel that calls it.
-__device__ __forceinline__ float ace_exp_fast(float v) { return __expf(v); }
+// compared with a tolerance. exp(x - m) = 2^(x log2(e) - m log2(e)): one fused
+// multiply-add against the rounded m log2(e) of the voxel (a common factor that
+// cancels in the normalisation) and the hardware base-2 exponential
+// (ex2.approx.ftz, relative error about 2^-22); the normalisation is one
+// approximate reciprocal per voxel (1 ulp). p is then within a few ulp of the
+// correctly rounded softmax for the probabilities that carry weight, at about a
+// third of the instructions of ace_softmax; every kernel that calls these
+// functions gets the same p.
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ float ace_exp2_approx(float t) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(t));
+  return y;
+}
+
+// exp(x - m) given mL = m * log2(e) (rounded once, ACE_FMUL).
+__device__ __forceinline__ float ace_exp_fast(float x, float mL) {
+  return ace_exp2_approx(__fmaf_rn(x, kLog2e, -mL));
+}
 
 template <int CM>
 __device__ __forceinline__ void ace_softmax_fast(float (&x)[CM], int C) {
@@ -362,11 +376,12 @@ __device__ __forceinline__ void ace_softmax_fast(float (&x)[CM], int C) {
 #pragma unroll
   for (int c = 1; c < CM; ++c)
     if (c < C) m = fmaxf(m, x[c]);
+  const float mL = ACE_FMUL(m, kLog2e);
   float s = 0.0f;
 #pragma unroll
   for (int c = 0; c < CM; ++c) {
     if (c < C) {
-      x[c] = ace_exp_fast(ACE_FSUB(x[c], m));
+      x[c] = ace_exp_fast(x[c], mL);
       s = ACE_FADD(s, x[c]);
     }
   }

@@ -840,31 +840,22 @@ __global__ void __launch_bounds__(kHistThreads) soft_hist_kernel(const __grid_co
   const int64_t out_stride = (int64_t)P.B_total * CL * slots;
 
   const int64_t tpb = P.g.tiles > 0 ? P.g.tiles : 1;
-  int64_t g0, g1;
-  chunk_range(P.g, g0, g1);
   int since_fold = 0;
   const int64_t tile = (int64_t)kHistThreads * V;
   const bool pf_x = ((reinterpret_cast<uintptr_t>(P.x) | (N * sizeof(T))) & 15) == 0;
-  int b = (int)(g0 / tpb);
-  int64_t t = g0 - b * tpb;
-  const T* xb = static_cast<const T*>(P.x) + (int64_t)b * C * N;
-  const int64_t* lb = static_cast<const int64_t*>(P.target) + (int64_t)b * N;
-  int64_t row0 = (int64_t)(P.b_offset + b) * CL;
-  for (int64_t g = g0; g < g1; ++g, ++t) {
-    if (t == tpb) {  // next batch: fold this batch's rows first
-      __syncthreads();
-      fold_split(hist, CL * slots, R, P.accum, out_stride, row0 * slots, true);
-      __syncthreads();
-      since_fold = 0;
-      ++b;
-      t = 0;
-      xb = static_cast<const T*>(P.x) + (int64_t)b * C * N;
-      lb = static_cast<const int64_t*>(P.target) + (int64_t)b * N;
-      row0 = (int64_t)(P.b_offset + b) * CL;
-    }
-    if (t + 1 < tpb && g + 1 < g1 && pf_x) {
-      if (tid < C) ace_prefetch_tile(xb + (int64_t)tid * N, (t + 1) * tile, tile, N, sizeof(T));
-      if (tid == C) ace_prefetch_tile(lb, (t + 1) * tile, tile, N, 8);
+  const T* xb;
+  const int64_t* lb;
+  int64_t row0;
+  auto set_batch = [&](int bb) {
+    xb = static_cast<const T*>(P.x) + (int64_t)bb * C * N;
+    lb = static_cast<const int64_t*>(P.target) + (int64_t)bb * N;
+    row0 = (int64_t)(P.b_offset + bb) * CL;
+  };
+  // One tile of the current batch; t_pf >= 0: L2 prefetch of that tile first.
+  auto tile_body = [&](int64_t t, int64_t t_pf) {
+    if (t_pf >= 0 && pf_x) {
+      if (tid < C) ace_prefetch_tile(xb + (int64_t)tid * N, t_pf * tile, tile, N, sizeof(T));
+      if (tid == C) ace_prefetch_tile(lb, t_pf * tile, tile, N, 8);
     }
     const int64_t v0 = (t * kHistThreads + tid) * V;
     if (v0 < N) {  // V > 1 implies N % V == 0: groups are whole
@@ -895,12 +886,37 @@ __global__ void __launch_bounds__(kHistThreads) soft_hist_kernel(const __grid_co
         }
       }
     }
-    if (++since_fold == P.flush_tiles && g + 1 < g1) {
+  };
+  // Every flush_tiles tiles the 32-bit words are folded before they could
+  // overflow (all threads call this: it may hold barriers).
+  auto count_tile = [&](bool more) {
+    if (++since_fold == P.flush_tiles && more) {
       since_fold = 0;
       __syncthreads();
       fold_split(hist, CL * slots, R, P.accum, out_stride, row0 * slots, true);
       __syncthreads();
     }
+  };
+
+  // CTA x streams tiles [g0, g1) (chunk_range), crossing into the next batch if
+  // the split is flat.
+  int64_t g0, g1;
+  chunk_range(P.g, g0, g1);
+  int b = (int)(g0 / tpb);
+  int64_t t = g0 - b * tpb;
+  set_batch(b);
+  for (int64_t g = g0; g < g1; ++g, ++t) {
+    if (t == tpb) {  // next batch: fold this batch's rows first
+      __syncthreads();
+      fold_split(hist, CL * slots, R, P.accum, out_stride, row0 * slots, true);
+      __syncthreads();
+      since_fold = 0;
+      ++b;
+      t = 0;
+      set_batch(b);
+    }
+    tile_body(t, (t + 1 < tpb && g + 1 < g1) ? t + 1 : -1);
+    count_tile(g + 1 < g1);
   }
   ace_launch_dependents();
   __syncthreads();
@@ -1029,14 +1045,17 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const __grid_constant__ 
   // programmatic dependent launch: global memory only after the previous grid
   ace_grid_dependency_wait();
   const int64_t row0 = (int64_t)(P.b_offset + b) * CL;
-  for (int e = tid; e < CL * (K + 1) * rec_copies; e += kThreads) {
-    const int ej = e / rec_copies;
-    const int row = ej / (K + 1), j = ej - row * (K + 1);
+  // One thread per (row, j) record; it writes all the record's copies (16-byte
+  // stores: rec_copies * record bytes is a multiple of 16).
+  for (int e = tid; e < CL * (K + 1); e += kThreads) {
+    const int row = e / (K + 1), j = e - row * (K + 1);
     const float g = P.jac[row0 + row] * (P.grad_per_row ? P.grad_out[row0 + row] : P.grad_out[0]);
     const float* cf = P.coef + (row0 + row) * K;
     const float* dd = P.d + (row0 + row) * K;
+    uint4 v;
     if constexpr (!SOFT) {
-      tab[e] = j < K ? g * cf[j] : 0.0f;
+      const unsigned u = __float_as_uint(j < K ? g * cf[j] : 0.0f);
+      v = make_uint4(u, u, u, u);
     } else {
       const int l = max(j - 1, 0), r = min(j, K - 1);
       const float a = g * cf[l], bb = g * cf[r];
@@ -1047,8 +1066,11 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const __grid_constant__ 
         const double e_ = inv * ((double)a * dd[l] - (double)bb * dd[r]);
         rec = make_float2((float)((double)a - dd_ * lo + e_), (float)dd_);
       }
-      reinterpret_cast<float2*>(tab)[e] = rec;
+      v = make_uint4(__float_as_uint(rec.x), __float_as_uint(rec.y), __float_as_uint(rec.x),
+                     __float_as_uint(rec.y));
     }
+    uint4* dst = reinterpret_cast<uint4*>(tab + (SOFT ? 2 : 1) * e * rec_copies);
+    for (int q = 0; q < (SOFT ? 2 : 1) * rec_copies / 4; ++q) dst[q] = v;
   }
   __syncthreads();
   const float* my_tab = tab + (SOFT ? 2 : 1) * (tid & (rec_copies - 1));
@@ -1057,11 +1079,10 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const __grid_constant__ 
   auto entry = [&](int j) -> float2 { return my_lohi[j * kTabCopies]; };
   // Many-channel passes: one value's exponential and probability, the same
   // operations as ace_softmax_sel (fast for soft binning, exact for hard).
-  auto exp_c = [](float v) -> float {
-    if constexpr (SOFT) return ace_exp_fast(v);
-    else return expf(v);
+  auto expf_c = [](float x, float m) -> float {
+    if constexpr (SOFT) return ace_exp_fast(x, ACE_FMUL(m, kLog2e));
+    else return expf(ACE_FSUB(x, m));
   };
-  auto expf_c = [&](float x, float m) -> float { return exp_c(ACE_FSUB(x, m)); };
   auto prob_c = [](float e, float s, float r) -> float {
     if constexpr (SOFT) return ACE_FMUL(e, r);
     else return ace_div_corrected(e, s, r);
@@ -1108,7 +1129,7 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const __grid_constant__ 
         float x[V];
         VecIO<T, V>::load(xr + (int64_t)c * N, x);
 #pragma unroll
-        for (int i = 0; i < V; ++i) sm[i] = ACE_FADD(sm[i], exp_c(ACE_FSUB(x[i], m[i])));
+        for (int i = 0; i < V; ++i) sm[i] = ACE_FADD(sm[i], expf_c(x[i], m[i]));
       }
 #pragma unroll
       for (int i = 0; i < V; ++i) {
