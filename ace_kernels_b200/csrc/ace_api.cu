@@ -342,14 +342,17 @@ int hist_impl(const ace_b200_inputs* in, const ace_b200_options* opt, float* his
   }
   Variant v = choose_variant(in, opt, nullptr, true);
   // Shared-memory table: `entries` words per lane replica. A 32-bit word of a
-  // replica takes at most (kHistThreads / R) * V additions per tile and must not
+  // replica takes at most (threads / R) * V additions per tile and must not
   // take more than 1023 between two folds (values up to 2^21 each), so R has a
   // floor; above it, as many replicas as fit in ~100 KB (32 = conflict-free),
-  // two CTAs per SM. Soft binning with labels and a softmax over <= 4 channels
-  // takes the class-split kernel: slots (interval, class flag), 5 words each,
-  // and only the {base, scale} half of the bin table.
+  // two CTAs of kHistThreads per SM. Soft binning with labels and a softmax over
+  // <= 4 channels takes the class-split kernel: one CTA of kSplitThreads per SM
+  // (so up to ~200 KB of table), slots (interval, class flag), 5 words each, and
+  // only the {base, scale} half of the bin table.
   const bool soft = opt->soft != 0;
   v.split = soft && v.softmax && v.labels && v.CM <= 4;
+  const int threads = v.split ? kSplitThreads : kHistThreads;
+  const size_t table_budget = (v.split ? 200 : 100) * 1024;
   const int words =
       v.split ? 5 : soft ? (in->target_kind == ACE_B200_TARGET_LABELS ? 7 : 9) : 3;  // odd
   const int entries = CL * (v.split ? 2 * (K + 1) : soft ? K + 1 : K) * words;
@@ -357,12 +360,12 @@ int hist_impl(const ace_b200_inputs* in, const ace_b200_options* opt, float* his
       (size_t)(K + 1) * kTabCopies * (v.split ? sizeof(float2) : sizeof(float4));
   auto r_min = [&](int V) {
     int r = 1;
-    while ((kHistThreads / r) * V > 1023) r <<= 1;
+    while ((threads / r) * V > 1023) r <<= 1;
     return r;
   };
   if (table_bytes + (size_t)entries * r_min(v.V) * 4 > 200 * 1024) v.V = 1;
   int R = 32;
-  while (R > r_min(v.V) && table_bytes + (size_t)entries * R * 4 > 100 * 1024) R >>= 1;
+  while (R > r_min(v.V) && table_bytes + (size_t)entries * R * 4 > table_budget) R >>= 1;
   const int smem = (int)(table_bytes + (size_t)entries * R * 4);
   if (smem > 200 * 1024)
     return fail(ACE_B200_EUNSUPPORTED,
@@ -374,11 +377,11 @@ int hist_impl(const ace_b200_inputs* in, const ace_b200_options* opt, float* his
   const int occ = occupancy(0, in->x_dtype, v, smem, dev);
   p.x = in->x;
   p.target = in->target;
-  p.g = make_grid(in, CL, opt->offset, v.V, kHistThreads, occ, dev, true);
+  p.g = make_grid(in, CL, opt->offset, v.V, threads, occ, dev, true);
   p.act = opt->activation;
   p.soft = soft;
   p.R = R;
-  p.flush_tiles = 1023 / ((kHistThreads / R) * v.V);
+  p.flush_tiles = 1023 / ((threads / R) * v.V);
   p.b_offset = (int)in->b_offset;
   p.B_total = (int)in->b_total;
   const Workspace w = carve(workspace, in->b_total, CL, K);

@@ -799,22 +799,28 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constan
 
 // ---------------------------------------------------------------------------
 // Forward for soft binning with class labels and a softmax over C <= 4 channels
-// (the register-tile case): the same tiling, table replicas, folds and last-CTA
-// handoff as hist_kernel, with fewer instructions per value:
+// (the register-tile case): the same table replicas, folds and last-CTA handoff
+// as hist_kernel, with fewer instructions per value:
 // - the fast softmax (ace_softmax_fast);
 // - the interval is the rounded p K of the saturated p (NaN -> 0), so it lies in
 //   [0, K] without a clamp and without the exact test (see soft_entry above);
 // - slots split by class flag (AccSplit): one update of four words per value,
 //   and no per-voxel update for the true class.
-// The last CTA merges the two slots of each interval into the n, sum t, sum t^2,
-// ny, sum t y moments of hist_kernel's reconstruction.
+// One CTA of kSplitThreads (32 warps) per SM. With per-batch chunks the warps of
+// a CTA take warp tiles (32 x V voxels) of the CTA's chunk from a shared-memory
+// counter, so no warp waits for another until the chunk is done; warps that the
+// SM schedules first simply take more tiles. A flat split (chunks that cross
+// batches) streams CTA tiles of kSplitThreads x V voxels. The last CTA merges the
+// two slots of each interval into the n, sum t, sum t^2, ny, sum t y moments of
+// hist_kernel's reconstruction.
 // ---------------------------------------------------------------------------
 template <typename T, int V, int C>
-__global__ void __launch_bounds__(kHistThreads) soft_hist_kernel(const __grid_constant__ FwdParams P) {
+__global__ void __launch_bounds__(kSplitThreads, 1) soft_hist_kernel(const __grid_constant__ FwdParams P) {
   using L = AccSplit;
   constexpr int NW = L::NW;
+  constexpr int NT = kSplitThreads;
   extern __shared__ __align__(16) float smem[];
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31;
   const int CL = P.g.CL, off = P.g.offset, K = P.tab.K;
   const int slots = 2 * (K + 1);
   const int64_t N = P.g.N;
@@ -824,12 +830,12 @@ __global__ void __launch_bounds__(kHistThreads) soft_hist_kernel(const __grid_co
   float2* map_t = reinterpret_cast<float2*>(smem);
   unsigned* hist = reinterpret_cast<unsigned*>(map_t + (K + 1) * kTabCopies);
   const int table_words = CL * slots * R * NW;
-  for (int i = tid; i < (K + 1) * kTabCopies; i += kHistThreads) map_t[i] = P.tab.map[i / kTabCopies];
+  for (int i = tid; i < (K + 1) * kTabCopies; i += NT) map_t[i] = P.tab.map[i / kTabCopies];
   const float2* my_map = map_t + (tid & (kTabCopies - 1));
   {
     uint4* h4 = reinterpret_cast<uint4*>(hist);  // 16-byte aligned: (K + 1) * 128 bytes in
-    for (int i = tid; i < table_words / 4; i += kHistThreads) h4[i] = make_uint4(0u, 0u, 0u, 0u);
-    for (int i = (table_words & ~3) + tid; i < table_words; i += kHistThreads) hist[i] = 0u;
+    for (int i = tid; i < table_words / 4; i += NT) h4[i] = make_uint4(0u, 0u, 0u, 0u);
+    for (int i = (table_words & ~3) + tid; i < table_words; i += NT) hist[i] = 0u;
   }
   ace_grid_dependency_wait();  // programmatic dependent launch (see hist_kernel)
   __syncthreads();
@@ -841,7 +847,6 @@ __global__ void __launch_bounds__(kHistThreads) soft_hist_kernel(const __grid_co
 
   const int64_t tpb = P.g.tiles > 0 ? P.g.tiles : 1;
   int since_fold = 0;
-  const int64_t tile = (int64_t)kHistThreads * V;
   const bool pf_x = ((reinterpret_cast<uintptr_t>(P.x) | (N * sizeof(T))) & 15) == 0;
   const T* xb;
   const int64_t* lb;
@@ -851,72 +856,103 @@ __global__ void __launch_bounds__(kHistThreads) soft_hist_kernel(const __grid_co
     lb = static_cast<const int64_t*>(P.target) + (int64_t)bb * N;
     row0 = (int64_t)(P.b_offset + bb) * CL;
   };
-  // One tile of the current batch; t_pf >= 0: L2 prefetch of that tile first.
-  auto tile_body = [&](int64_t t, int64_t t_pf) {
-    if (t_pf >= 0 && pf_x) {
-      if (tid < C) ace_prefetch_tile(xb + (int64_t)tid * N, t_pf * tile, tile, N, sizeof(T));
-      if (tid == C) ace_prefetch_tile(lb, t_pf * tile, tile, N, 8);
-    }
-    const int64_t v0 = (t * kHistThreads + tid) * V;
-    if (v0 < N) {  // V > 1 implies N % V == 0: groups are whole
-      int lab[V];
-      ace_load_labels<V>(lb + v0, lab);
-      float xv[C][V];
+  // L2 prefetch of `count` voxels from voxel `start` of the current batch (one
+  // lane per channel row and one for the labels).
+  auto prefetch = [&](int64_t start, int64_t count, int who) {
+    if (!pf_x) return;
+    if (who < C) ace_prefetch_tile(xb + (int64_t)who * N, start, count, N, sizeof(T));
+    if (who == C) ace_prefetch_tile(lb, start, count, N, 8);
+  };
+  // V voxels from v0 of the current batch into the table.
+  auto voxels = [&](int64_t v0) {
+    if (v0 >= N) return;  // V > 1 implies N % V == 0: groups are whole
+    int lab[V];
+    ace_load_labels<V>(lb + v0, lab);
+    float xv[C][V];
 #pragma unroll
-      for (int c = 0; c < C; ++c) VecIO<T, V>::load(xb + (int64_t)c * N + v0, xv[c]);
+    for (int c = 0; c < C; ++c) VecIO<T, V>::load(xb + (int64_t)c * N + v0, xv[c]);
 #pragma unroll
-      for (int i = 0; i < V; ++i) {
-        float p[C];
+    for (int i = 0; i < V; ++i) {
+      float p[C];
 #pragma unroll
-        for (int c = 0; c < C; ++c) p[c] = xv[c][i];
-        ace_softmax_fast<C>(p, C);
+      for (int c = 0; c < C; ++c) p[c] = xv[c][i];
+      ace_softmax_fast<C>(p, C);
 #pragma unroll
-        for (int c = 0; c < C; ++c) {
-          if (c < off) continue;
-          const int j = (int)(__float_as_uint(__fmaf_rn(__saturatef(p[c]), Kf, kFixMagic)) -
-                              kFixMagicBits);
-          const float2 m = my_map[j * kTabCopies];
-          const float us = fminf(ACE_FMUL(ACE_FSUB(p[c], m.x), m.y), kFixScale);
-          const int a = col + c * row_stride + j * (2 * slot_stride) + (lab[i] == c ? slot_stride : 0);
-          const uint2 uw = fix2_scaled(us);
-          sadd(hist, a, 1u);
-          sadd(hist, a + 1, uw.x);
-          sadd(hist, a + 2, uw.y);
-          sadd(hist, a + 3, __float_as_uint(__fmaf_rn(us, ACE_FMUL(us, 1.0f / kFixScale), kFixMagic)));
-        }
+      for (int c = 0; c < C; ++c) {
+        if (c < off) continue;
+        const int j = (int)(__float_as_uint(__fmaf_rn(__saturatef(p[c]), Kf, kFixMagic)) -
+                            kFixMagicBits);
+        const float2 m = my_map[j * kTabCopies];
+        const float us = fminf(ACE_FMUL(ACE_FSUB(p[c], m.x), m.y), kFixScale);
+        const int a = col + c * row_stride + j * (2 * slot_stride) + (lab[i] == c ? slot_stride : 0);
+        const uint2 uw = fix2_scaled(us);
+        sadd(hist, a, 1u);
+        sadd(hist, a + 1, uw.x);
+        sadd(hist, a + 2, uw.y);
+        sadd(hist, a + 3, __float_as_uint(__fmaf_rn(us, ACE_FMUL(us, 1.0f / kFixScale), kFixMagic)));
       }
     }
   };
-  // Every flush_tiles tiles the 32-bit words are folded before they could
-  // overflow (all threads call this: it may hold barriers).
-  auto count_tile = [&](bool more) {
-    if (++since_fold == P.flush_tiles && more) {
-      since_fold = 0;
-      __syncthreads();
-      fold_split(hist, CL * slots, R, P.accum, out_stride, row0 * slots, true);
-      __syncthreads();
-    }
+  auto fold_clear = [&]() {
+    __syncthreads();
+    fold_split(hist, CL * slots, R, P.accum, out_stride, row0 * slots, true);
+    __syncthreads();
   };
 
-  // CTA x streams tiles [g0, g1) (chunk_range), crossing into the next batch if
-  // the split is flat.
-  int64_t g0, g1;
-  chunk_range(P.g, g0, g1);
-  int b = (int)(g0 / tpb);
-  int64_t t = g0 - b * tpb;
-  set_batch(b);
-  for (int64_t g = g0; g < g1; ++g, ++t) {
-    if (t == tpb) {  // next batch: fold this batch's rows first
+  if (P.g.chunks_per_batch > 0) {
+    // Chunk k of batch bx: CTA tiles [k tpc, (k + 1) tpc), i.e. warp tiles 32x
+    // as many. A replica word takes at most V additions per warp tile, so the
+    // warp tiles are taken in epochs of flush_tiles * 32 (at most 1023 / V), with
+    // a fold between epochs.
+    __shared__ unsigned s_ctr;
+    constexpr int WT = 32 * V;  // voxels per warp tile
+    const int cb = P.g.chunks_per_batch;
+    const int bx = (int)blockIdx.x / cb, k = (int)blockIdx.x - bx * cb;
+    set_batch(bx);
+    const int64_t wtpb = (N + WT - 1) / WT;
+    const int64_t w_begin = (int64_t)k * P.g.tiles_per_chunk * (NT / 32);
+    const int64_t w_end = min(w_begin + P.g.tiles_per_chunk * (NT / 32), wtpb);
+    const int64_t epoch = (int64_t)P.flush_tiles * (NT / 32);
+    for (int64_t e0 = w_begin; e0 < w_end; e0 += epoch) {
+      const int64_t e1 = min(e0 + epoch, w_end);
+      if (tid == 0) s_ctr = 0u;
       __syncthreads();
-      fold_split(hist, CL * slots, R, P.accum, out_stride, row0 * slots, true);
-      __syncthreads();
-      since_fold = 0;
-      ++b;
-      t = 0;
-      set_batch(b);
+      while (true) {
+        unsigned i = 0;
+        if (lane == 0) i = atomicAdd(&s_ctr, 1u);
+        i = __shfl_sync(0xffffffffu, i, 0);
+        const int64_t wt = e0 + i;
+        if (wt >= e1) break;
+        // the warp tile about two rounds ahead, likely taken by some warp then
+        if (wt + 2 * (NT / 32) < e1) prefetch((wt + 2 * (NT / 32)) * WT, WT, lane);
+        voxels((wt * 32 + lane) * V);
+      }
+      if (e1 < w_end) fold_clear();
     }
-    tile_body(t, (t + 1 < tpb && g + 1 < g1) ? t + 1 : -1);
-    count_tile(g + 1 < g1);
+  } else {
+    // Flat: CTA x streams CTA tiles [g0, g1) (chunk_range), crossing into the
+    // next batch (after a fold of this batch's rows) where the run does.
+    const int64_t tile = (int64_t)NT * V;
+    int64_t g0, g1;
+    chunk_range(P.g, g0, g1);
+    int b = (int)(g0 / tpb);
+    int64_t t = g0 - b * tpb;
+    set_batch(b);
+    for (int64_t g = g0; g < g1; ++g, ++t) {
+      if (t == tpb) {
+        fold_clear();
+        since_fold = 0;
+        ++b;
+        t = 0;
+        set_batch(b);
+      }
+      if (t + 1 < tpb && g + 1 < g1) prefetch((t + 1) * tile, tile, tid);
+      voxels((t * NT + tid) * V);
+      if (++since_fold == P.flush_tiles && g + 1 < g1) {
+        since_fold = 0;
+        fold_clear();
+      }
+    }
   }
   ace_launch_dependents();
   __syncthreads();
@@ -942,7 +978,7 @@ __global__ void __launch_bounds__(kHistThreads) soft_hist_kernel(const __grid_co
   const bool stage = P.do_epilogue && 3 * stat_stride <= (int64_t)table_words;
   float* staged = reinterpret_cast<float*>(hist);
   const double* acc = P.accum;
-  for (int64_t e = tid; e < stat_stride; e += kHistThreads) {
+  for (int64_t e = tid; e < stat_stride; e += NT) {
     const int64_t r = e / K;
     const int k = (int)(e - r * K);
     double w = 0.0, pp = 0.0, gsum = 0.0;
@@ -983,7 +1019,7 @@ __global__ void __launch_bounds__(kHistThreads) soft_hist_kernel(const __grid_co
   }
   __syncthreads();
   double* accw = P.accum;
-  for (int64_t i = tid; i < L::NOUT * out_stride; i += kHistThreads) __stcg(accw + i, 0.0);
+  for (int64_t i = tid; i < L::NOUT * out_stride; i += NT) __stcg(accw + i, 0.0);
   if (tid == 0) *P.counter = 0u;
   if (stage) {
     __syncthreads();
@@ -1356,13 +1392,13 @@ struct SoftHistLauncher {
     auto k = soft_hist_kernel<T, V, C>;
     cudaError_t e = set_smem(k, smem, configured());
     if (e != cudaSuccess) return e;
-    return launch_dependent(k, grid, kHistThreads, smem, s, p);
+    return launch_dependent(k, grid, kSplitThreads, smem, s, p);
   }
   static int occupancy(int smem) {
     auto k = soft_hist_kernel<T, V, C>;
     set_smem(k, smem, configured());
     int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, kHistThreads, smem) != cudaSuccess) n = 1;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, kSplitThreads, smem) != cudaSuccess) n = 1;
     return n > 0 ? n : 1;
   }
 };
