@@ -378,6 +378,14 @@ int hist_impl(const ace_b200_inputs* in, const ace_b200_options* opt, float* his
   p.x = in->x;
   p.target = in->target;
   p.g = make_grid(in, CL, opt->offset, v.V, threads, occ, dev, true);
+  if (v.split && p.g.chunks_per_batch > 0) {
+    // the class-split kernel splits each batch's warp tiles evenly over its CTAs
+    const int64_t wtiles = (in->N + 32 * v.V - 1) / (32 * v.V);
+    int64_t cb = (int64_t)sm_count(dev) * occ / p.g.B;
+    cb = cb < wtiles ? cb : wtiles;
+    p.g.chunks_per_batch = (int)(cb > 0 ? cb : 1);
+    p.g.chunks = p.g.chunks_per_batch * p.g.B;
+  }
   p.act = opt->activation;
   p.soft = soft;
   p.R = R;

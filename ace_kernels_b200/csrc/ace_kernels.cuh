@@ -806,10 +806,12 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constan
 //   [0, K] without a clamp and without the exact test (see soft_entry above);
 // - slots split by class flag (AccSplit): one update of four words per value,
 //   and no per-voxel update for the true class.
-// One CTA of kSplitThreads (32 warps) per SM. With per-batch chunks the warps of
-// a CTA take warp tiles (32 x V voxels) of the CTA's chunk from a shared-memory
-// counter, so no warp waits for another until the chunk is done; warps that the
-// SM schedules first simply take more tiles. A flat split (chunks that cross
+// One CTA of kSplitThreads (24 warps) per SM. With per-batch chunks the warps of
+// a CTA take warp tiles (32 x V voxels) of the CTA's share from a shared-memory
+// counter, so no warp waits for another until the share is done (warps that the
+// SM schedules first simply take more tiles), and each warp issues the loads of
+// its next tile before it adds the current one (two tiles in flight per warp,
+// hence 24 warps of up to 85 registers). A flat split (chunks that cross
 // batches) streams CTA tiles of kSplitThreads x V voxels. The last CTA merges the
 // two slots of each interval into the n, sum t, sum t^2, ny, sum t y moments of
 // hist_kernel's reconstruction.
@@ -863,19 +865,29 @@ __global__ void __launch_bounds__(kSplitThreads, 1) soft_hist_kernel(const __gri
     if (who < C) ace_prefetch_tile(xb + (int64_t)who * N, start, count, N, sizeof(T));
     if (who == C) ace_prefetch_tile(lb, start, count, N, 8);
   };
-  // V voxels from v0 of the current batch into the table.
-  auto voxels = [&](int64_t v0) {
-    if (v0 >= N) return;  // V > 1 implies N % V == 0: groups are whole
+  // A thread's V voxels: loaded (load_group) and added into the table
+  // (add_group) as separate steps, so that the next group's loads can be in
+  // flight while this one is added. V > 1 implies N % V == 0: groups are whole.
+  struct Group {
     int lab[V];
-    ace_load_labels<V>(lb + v0, lab);
     float xv[C][V];
+  };
+  auto load_group = [&](int64_t v0, Group& gr) {
+    if (v0 >= N) return;
+    // the low word of each int64 label (one register per voxel while in flight)
 #pragma unroll
-    for (int c = 0; c < C; ++c) VecIO<T, V>::load(xb + (int64_t)c * N + v0, xv[c]);
+    for (int i = 0; i < V; ++i) gr.lab[i] = __ldg(reinterpret_cast<const int*>(lb + v0 + i));
+#pragma unroll
+    for (int c = 0; c < C; ++c) VecIO<T, V>::load(xb + (int64_t)c * N + v0, gr.xv[c]);
+  };
+  auto add_group = [&](int64_t v0, const Group& gr) {
+    if (v0 >= N) return;
+    const int (&lab)[V] = gr.lab;
 #pragma unroll
     for (int i = 0; i < V; ++i) {
       float p[C];
 #pragma unroll
-      for (int c = 0; c < C; ++c) p[c] = xv[c][i];
+      for (int c = 0; c < C; ++c) p[c] = gr.xv[c][i];
       ace_softmax_fast<C>(p, C);
 #pragma unroll
       for (int c = 0; c < C; ++c) {
@@ -900,32 +912,40 @@ __global__ void __launch_bounds__(kSplitThreads, 1) soft_hist_kernel(const __gri
   };
 
   if (P.g.chunks_per_batch > 0) {
-    // Chunk k of batch bx: CTA tiles [k tpc, (k + 1) tpc), i.e. warp tiles 32x
-    // as many. A replica word takes at most V additions per warp tile, so the
-    // warp tiles are taken in epochs of flush_tiles * 32 (at most 1023 / V), with
-    // a fold between epochs.
+    // CTA k of batch bx takes warp tiles [k W / cb, (k + 1) W / cb) of the W warp
+    // tiles (32 x V voxels) of the batch. A replica word takes at most
+    // V * 32 / R additions per warp tile, so the warp tiles are taken in epochs
+    // of at most 1023 / (V * 32 / R), with a fold between epochs. Each warp
+    // takes its next tile and issues its loads before it adds the current one.
     __shared__ unsigned s_ctr;
     constexpr int WT = 32 * V;  // voxels per warp tile
     const int cb = P.g.chunks_per_batch;
     const int bx = (int)blockIdx.x / cb, k = (int)blockIdx.x - bx * cb;
     set_batch(bx);
     const int64_t wtpb = (N + WT - 1) / WT;
-    const int64_t w_begin = (int64_t)k * P.g.tiles_per_chunk * (NT / 32);
-    const int64_t w_end = min(w_begin + P.g.tiles_per_chunk * (NT / 32), wtpb);
-    const int64_t epoch = (int64_t)P.flush_tiles * (NT / 32);
+    const int64_t w_begin = wtpb * k / cb, w_end = wtpb * (k + 1) / cb;
+    const int64_t epoch = 1023 / (V * (32 / (R < 32 ? R : 32)));
+    auto take = [&](int64_t e0) -> int64_t {
+      unsigned i = 0;
+      if (lane == 0) i = atomicAdd(&s_ctr, 1u);
+      return e0 + __shfl_sync(0xffffffffu, i, 0);
+    };
     for (int64_t e0 = w_begin; e0 < w_end; e0 += epoch) {
       const int64_t e1 = min(e0 + epoch, w_end);
       if (tid == 0) s_ctr = 0u;
       __syncthreads();
-      while (true) {
-        unsigned i = 0;
-        if (lane == 0) i = atomicAdd(&s_ctr, 1u);
-        i = __shfl_sync(0xffffffffu, i, 0);
-        const int64_t wt = e0 + i;
-        if (wt >= e1) break;
+      int64_t wt = take(e0);
+      Group cur;
+      if (wt < e1) load_group((wt * 32 + lane) * V, cur);
+      while (wt < e1) {
+        const int64_t wn = take(e0);
+        Group nxt;
+        if (wn < e1) load_group((wn * 32 + lane) * V, nxt);
         // the warp tile about two rounds ahead, likely taken by some warp then
-        if (wt + 2 * (NT / 32) < e1) prefetch((wt + 2 * (NT / 32)) * WT, WT, lane);
-        voxels((wt * 32 + lane) * V);
+        if (wn + 2 * (NT / 32) < e1) prefetch((wn + 2 * (NT / 32)) * WT, WT, lane);
+        add_group((wt * 32 + lane) * V, cur);
+        wt = wn;
+        cur = nxt;
       }
       if (e1 < w_end) fold_clear();
     }
@@ -947,7 +967,9 @@ __global__ void __launch_bounds__(kSplitThreads, 1) soft_hist_kernel(const __gri
         set_batch(b);
       }
       if (t + 1 < tpb && g + 1 < g1) prefetch((t + 1) * tile, tile, tid);
-      voxels((t * NT + tid) * V);
+      Group gr;
+      load_group((t * NT + tid) * V, gr);
+      add_group((t * NT + tid) * V, gr);
       if (++since_fold == P.flush_tiles && g + 1 < g1) {
         since_fold = 0;
         fold_clear();

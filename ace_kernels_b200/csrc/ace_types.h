@@ -14,7 +14,7 @@ constexpr int kMaxBins = ACE_B200_MAX_BINS;        // num_bins limit of the kern
 constexpr int kMaxClasses = ACE_B200_MAX_CLASSES;  // channels limit of the kernels
 constexpr int kThreads = 256;                      // threads per CTA (gradient, epilogue)
 constexpr int kHistThreads = 512;                  // threads per CTA of the histogram
-constexpr int kSplitThreads = 1024;                // threads per CTA of the class-split histogram
+constexpr int kSplitThreads = 640;                 // threads per CTA of the class-split histogram
 constexpr int kTabCopies = 16;                     // interleaved copies of the bin tables
 constexpr float kFixScale = 2097152.0f;            // 2^21: fixed-point unit of the statistics
 

@@ -219,12 +219,18 @@ def flush_l2(flush: torch.Tensor) -> None:
     flush.view(torch.int64).sum()
 
 
-def time_events(fn, flush: torch.Tensor, reps: int) -> float:  # type: ignore[no-untyped-def]
-    """Summed device milliseconds of ``reps`` calls, L2 flushed before each."""
+def time_events(fn, flush: torch.Tensor, reps: int, align=None) -> float:  # type: ignore[no-untyped-def]
+    """Summed device milliseconds of ``reps`` calls, L2 flushed before each.
+    ``align`` (N > 1): a tiny all-reduce after the flush, so that every rank's
+    step starts when the slowest rank's flush has ended (otherwise a rank whose
+    flush ended early would count its wait for the other ranks inside the step's
+    collective)."""
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
     for i in range(reps):
         flush_l2(flush)
+        if align is not None:
+            align()
         starts[i].record()
         fn()
         ends[i].record()
@@ -243,7 +249,9 @@ def capture(fn, warmup: int = 3) -> torch.cuda.CUDAGraph:  # type: ignore[no-unt
     # capture on the warm-up stream: per-stream state (the kernels' workspace) is
     # then created outside the graph
     g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g, stream=s):
+    # thread-local capture: other host threads (NCCL's watchdog) may keep making
+    # CUDA calls while this thread captures
+    with torch.cuda.graph(g, stream=s, capture_error_mode="thread_local"):
         fn()
     torch.cuda.synchronize()
     return g
@@ -284,13 +292,21 @@ def run_ours(args: argparse.Namespace) -> None:
         return g
 
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    align = None
+    if world > 1:
+        token = torch.zeros(1, device=dev)
+
+        def align() -> None:
+            dist.all_reduce(token)
+
     for _ in range(max(3, args.warmup)):
         step()
     torch.cuda.synchronize()
-    # One CUDA graph per step at N = 1; N > 1 runs eagerly (a captured step with
-    # the NCCL all-reduce inside hung in this bench, so it is not captured)
-    graph = None if (args.eager or world > 1) else capture(step)
+    # One CUDA graph per step (with N > 1 it holds the NCCL all-reduce; every
+    # reference to it is dropped before the process group is destroyed)
+    graph = None if args.eager else capture(step)
     run = step if graph is None else graph.replay
+    mode = "eager" if graph is None else "cuda_graph"
 
     # ---- value: K steps, device time, max over ranks
     for _ in range(max(3, args.warmup)):
@@ -301,7 +317,7 @@ def run_ours(args: argparse.Namespace) -> None:
     torch.cuda.synchronize()
     sampler = ClockSampler(local)
     with sampler:
-        total_ms = time_events(run, flush, args.steps)
+        total_ms = time_events(run, flush, args.steps, align)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -312,7 +328,7 @@ def run_ours(args: argparse.Namespace) -> None:
     value = voxels_all / (ms_per_step * 1e-3)
 
     # eager (no graph) for information
-    eager_ms = time_events(step, flush, min(args.steps, 100)) / min(args.steps, 100)
+    eager_ms = time_events(step, flush, min(args.steps, 100), align) / min(args.steps, 100)
     if world > 1:
         t = torch.tensor([eager_ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -342,7 +358,7 @@ def run_ours(args: argparse.Namespace) -> None:
     e2e_reps = min(args.steps, 50)
     if world > 1:
         dist.barrier()
-    e2e_ms = time_events(e2e_step, flush, e2e_reps) / e2e_reps
+    e2e_ms = time_events(e2e_step, flush, e2e_reps, align) / e2e_reps
     if world > 1:
         t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -390,7 +406,7 @@ def run_ours(args: argparse.Namespace) -> None:
             "binning": cfg.binning,
             "num_bins": cfg.num_bins,
             "parallelism": f"batch-sharded dp{world}" if world > 1 else "single GPU",
-            "mode": "eager" if graph is None else "cuda_graph",
+            "mode": mode,
             "l2": "flushed before every step: 512 MiB written, then read back, outside the events",
         },
         "hbm_frac_of_ideal_bytes": (step_bytes * world / (ms_per_step * 1e-3) / 1e9) / (peak * world),
@@ -418,7 +434,7 @@ def run_ours(args: argparse.Namespace) -> None:
         },
     }
     if world > 1:
-        del graph, g_hist, g_grad
+        del run, graph, g_hist, g_grad
         torch.cuda.synchronize()
         dist.barrier()
         dist.destroy_process_group()
