@@ -1003,20 +1003,28 @@ __global__ void __launch_bounds__(kSplitThreads, 1) soft_hist_kernel(const __gri
   for (int64_t e = tid; e < stat_stride; e += NT) {
     const int64_t r = e / K;
     const int k = (int)(e - r * K);
+    // the four slots of intervals k and k + 1 (flags 0, 1 each) are consecutive:
+    // all twelve sums are loaded before any is used (one L2 round trip)
+    const int64_t g0 = r * slots + 2 * k;
+    double m[3][4];
+#pragma unroll
+    for (int o = 0; o < 3; ++o)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) m[o][q] = __ldcg(acc + o * out_stride + g0 + q);
     double w = 0.0, pp = 0.0, gsum = 0.0;
+#pragma unroll
     for (int side = 0; side < 2; ++side) {
       const int j = k + side;
-      const int64_t gi = r * slots + 2 * j;
-      const double ny = __ldcg(acc + gi + 1), yu = __ldcg(acc + out_stride + gi + 1);
-      const double n = __ldcg(acc + gi) + ny;
-      const double su = __ldcg(acc + out_stride + gi) + yu;
+      const double ny = m[0][2 * side + 1], yu = m[1][2 * side + 1];
+      const double n = m[0][2 * side] + ny;
+      const double su = m[1][2 * side] + yu;
       if (j == 0 || j == K) {
         w += n;
         pp += su;
         gsum += ny;
         continue;
       }
-      const double su2 = __ldcg(acc + 2 * out_stride + gi) + __ldcg(acc + 2 * out_stride + gi + 1);
+      const double su2 = m[2][2 * side] + m[2][2 * side + 1];
       const double lo = P.tab.lohi[j].x, span = (double)P.tab.lohi[j].y - lo;
       const double pt = lo * su + span * su2;
       if (side == 0) {
