@@ -15,11 +15,11 @@ namespace ace {
 // The kernel instances live in ace_kern_{f32,bf16,f16}.cu.
 #define ACE_EXTERN(T)                                                                      \
   extern template cudaError_t launch_hist<T>(const FwdParams&, const Variant&, dim3, int, \
-                                             cudaStream_t);                                \
+                                             cudaStream_t, int);                           \
   extern template cudaError_t launch_grad<T>(const BwdParams&, const Variant&, dim3, int, \
-                                             cudaStream_t);                                \
-  extern template int hist_occupancy<T>(const Variant&, int);                              \
-  extern template int grad_occupancy<T>(const Variant&, int);                              \
+                                             cudaStream_t, int);                           \
+  extern template int hist_occupancy<T>(const Variant&, int, int);                         \
+  extern template int grad_occupancy<T>(const Variant&, int, int);                         \
   extern template cudaError_t launch_probs<T>(const void*, float*, int64_t, int, int64_t, \
                                               int, cudaStream_t);
 ACE_EXTERN(float)
@@ -99,13 +99,19 @@ int sm_count(int dev) {
 
 size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-// Workspace layout: [accumulators: up to 6 * b_total * cl * (K + 1) doubles]
-// [histogram counter][epilogue counter][epilogue partial sums: one per epilogue
-// CTA], each part 256-byte aligned. Counters and accumulators are zero between
-// calls.
+// Workspace layout, each part 256-byte aligned:
+//   [accumulators: 8 * b_total * cl * (K + 1) 8-byte words: hist_kernel's
+//    [6, rows, K + 1] fp64 sums, or soft_fwd_kernel's [4, rows, K + 1, 2]
+//    64-bit integer moments]
+//   [histogram counter][epilogue counter]
+//   [tile-pool counters: one per batch]
+//   [epilogue partial sums: one per epilogue CTA].
+// Counters and accumulators are zero between calls.
 size_t accum_bytes(int64_t b_total, int64_t cl, int K) {
-  return round_up((size_t)6 * b_total * cl * (K + 1) * sizeof(double), 256);
+  return round_up((size_t)8 * b_total * cl * (K + 1) * sizeof(double), 256);
 }
+
+size_t pool_bytes(int64_t b_total) { return round_up((size_t)b_total * sizeof(unsigned), 256); }
 
 int64_t epi_ctas(int64_t rows) { return (rows + kEpiRowsPerCta - 1) / kEpiRowsPerCta; }
 
@@ -113,6 +119,7 @@ struct Workspace {
   double* accum;
   unsigned* hist_counter;
   unsigned* epi_counter;
+  unsigned* pool;
   float* epi_partial;
 };
 
@@ -123,7 +130,8 @@ Workspace carve(void* ws, int64_t b_total, int64_t cl, int K) {
   w.accum = reinterpret_cast<double*>(base);
   w.hist_counter = reinterpret_cast<unsigned*>(base + a);
   w.epi_counter = reinterpret_cast<unsigned*>(base + a + 256);
-  w.epi_partial = reinterpret_cast<float*>(base + a + 512);
+  w.pool = reinterpret_cast<unsigned*>(base + a + 512);
+  w.epi_partial = reinterpret_cast<float*>(base + a + 512 + pool_bytes(b_total));
   return w;
 }
 
@@ -163,13 +171,13 @@ int occupancy(int kind, int dtype, const Variant& v, int smem, int dev) {
   }
   int n = 1;
   if (kind == 0) {
-    if (dtype == ACE_B200_F32) n = hist_occupancy<float>(v, smem);
-    else if (dtype == ACE_B200_BF16) n = hist_occupancy<__nv_bfloat16>(v, smem);
-    else n = hist_occupancy<__half>(v, smem);
+    if (dtype == ACE_B200_F32) n = hist_occupancy<float>(v, smem, dev);
+    else if (dtype == ACE_B200_BF16) n = hist_occupancy<__nv_bfloat16>(v, smem, dev);
+    else n = hist_occupancy<__half>(v, smem, dev);
   } else {
-    if (dtype == ACE_B200_F32) n = grad_occupancy<float>(v, smem);
-    else if (dtype == ACE_B200_BF16) n = grad_occupancy<__nv_bfloat16>(v, smem);
-    else n = grad_occupancy<__half>(v, smem);
+    if (dtype == ACE_B200_F32) n = grad_occupancy<float>(v, smem, dev);
+    else if (dtype == ACE_B200_BF16) n = grad_occupancy<__nv_bfloat16>(v, smem, dev);
+    else n = grad_occupancy<__half>(v, smem, dev);
   }
   std::lock_guard<std::mutex> lock(mu);
   cache[key] = n;
@@ -322,6 +330,70 @@ int fill_epi(EpiParams& e, int64_t b_total, int CL, double rows_global,
   return ACE_B200_OK;
 }
 
+// Shared-memory budget of one soft_fwd_kernel CTA (dynamic part; the static
+// barriers and epilogue scratch take well under 1 KB of the 227 KB).
+constexpr size_t kSoftSmemBudget = 225 * 1024;
+
+cudaError_t launch_hist_any(const FwdParams& p, const Variant& v, dim3 grid, int smem,
+                            int dtype, cudaStream_t s, int dev) {
+  if (dtype == ACE_B200_F32) return launch_hist<float>(p, v, grid, smem, s, dev);
+  if (dtype == ACE_B200_BF16) return launch_hist<__nv_bfloat16>(p, v, grid, smem, s, dev);
+  return launch_hist<__half>(p, v, grid, smem, s, dev);
+}
+
+// soft_fwd_kernel: soft binning, int64 labels, softmax over C <= 4 channels,
+// inputs whose rows are whole 16-byte vectors (the bulk copies move 16-byte
+// multiples). Shared memory: the table [K + 1][C][2][R][5] words (all C channels
+// get rows; a dropped background row stays empty), then the ring of stages. R
+// lane replicas (32: a warp's lanes never share a bank), reduced while the table
+// and two stages do not fit; a replica word takes at most 4 * 16 * 32 / R
+// additions per tile and 1023 between folds (2^21-unit values), which bounds the
+// tiles of an epoch. Returns false when the case does not fit (hist_kernel then
+// takes it).
+bool soft_fwd_setup(const ace_b200_inputs* in, const ace_b200_options* opt, const Variant& v,
+                    FwdParams& p, const Workspace& w, int dev, bool want_epilogue, int& smem,
+                    dim3& grid) {
+  const int K = opt->num_bins, C = (int)in->C;
+  const int es = elem_size(in->x_dtype);
+  if (v.V != 16 / es) return false;
+  const size_t stage_bytes = (size_t)kSoftTileVoxels * (C * es + 8);
+  const size_t replica_bytes = (size_t)(K + 1) * C * 2 * kSoftNW * 4;
+  int R = 32;
+  auto table = [&](int r) { return round_up(replica_bytes * r, 128); };
+  while (R > 4 && table(R) + 2 * stage_bytes > kSoftSmemBudget) R >>= 1;
+  if (table(R) + 2 * stage_bytes > kSoftSmemBudget) return false;
+  int stages = (int)((kSoftSmemBudget - table(R)) / stage_bytes);
+  if (stages > kSoftMaxStages) stages = kSoftMaxStages;
+  const int adds_per_tile = kSoftLaneVoxels * kSoftConsumerWarps * (32 / R);
+  smem = (int)(table(R) + stages * stage_bytes);
+  const int64_t tiles = (in->N + kSoftTileVoxels - 1) / kSoftTileVoxels;
+  int64_t ctas = (int64_t)sm_count(dev);  // one CTA per SM
+  if (ctas > in->B * tiles) ctas = in->B * tiles;
+  if (ctas < 1) ctas = 1;
+  p.iacc = reinterpret_cast<unsigned long long*>(w.accum);
+  p.pool_ctr = w.pool;
+  p.wt_batch = tiles;
+  p.epoch = 1023 / adds_per_tile;
+  p.stages = stages;
+  p.table_bytes = (int)table(R);
+  p.R = R;
+  p.flush_tiles = 0;
+  p.g.N = in->N;
+  p.g.B = (int)in->B;
+  p.g.C = C;
+  p.g.CL = C - opt->offset;
+  p.g.offset = opt->offset;
+  p.g.chunks = (int)ctas;
+  p.g.tiles = tiles;
+  p.g.tiles_per_chunk = 0;
+  p.g.chunks_per_batch = 0;
+  const int64_t stats = 3 * in->b_total * p.g.CL * K;
+  const int64_t rows = in->b_total * p.g.CL;
+  p.do_epilogue = want_epilogue && stats * 4 <= (int64_t)table(R) && rows <= 8 * kEpiRowsPerCta;
+  grid = dim3((unsigned)ctas, 1u);
+  return true;
+}
+
 int hist_impl(const ace_b200_inputs* in, const ace_b200_options* opt, float* hist,
               const ace_b200_epilogue_out* out, void* workspace, size_t ws_bytes, void* stream) {
   int CL = 0;
@@ -341,23 +413,52 @@ int hist_impl(const ace_b200_inputs* in, const ace_b200_options* opt, float* his
     if (rc) return rc;
   }
   Variant v = choose_variant(in, opt, nullptr, true);
-  // Shared-memory table: `entries` words per lane replica. A 32-bit word of a
-  // replica takes at most (threads / R) * V additions per tile and must not
-  // take more than 1023 between two folds (values up to 2^21 each), so R has a
-  // floor; above it, as many replicas as fit in ~100 KB (32 = conflict-free),
-  // two CTAs of kHistThreads per SM. Soft binning with labels and a softmax over
-  // <= 4 channels takes the class-split kernel: one CTA of kSplitThreads per SM
-  // (so up to ~200 KB of table), slots (interval, class flag), 5 words each, and
-  // only the {base, scale} half of the bin table.
   const bool soft = opt->soft != 0;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  const Workspace w = carve(workspace, in->b_total, CL, K);
+  p.x = in->x;
+  p.target = in->target;
+  p.act = opt->activation;
+  p.soft = soft;
+  p.b_offset = (int)in->b_offset;
+  p.B_total = (int)in->b_total;
+  p.accum = w.accum;
+  p.counter = w.hist_counter;
+  p.hist_out = hist;
+  build_table(K, soft, opt->right != 0, p.tab);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+
+  // Soft binning with labels and a softmax over <= 4 channels: soft_fwd_kernel.
+  // Its interval distances use the true centres: `right` only decides ties of p
+  // with a centre, where both intervals give the same weights.
   v.split = soft && v.softmax && v.labels && v.CM <= 4;
-  const int threads = v.split ? kSplitThreads : kHistThreads;
-  const size_t table_budget = (v.split ? 200 : 100) * 1024;
-  const int words =
-      v.split ? 5 : soft ? (in->target_kind == ACE_B200_TARGET_LABELS ? 7 : 9) : 3;  // odd
-  const int entries = CL * (v.split ? 2 * (K + 1) : soft ? K + 1 : K) * words;
-  const size_t table_bytes =
-      (size_t)(K + 1) * kTabCopies * (v.split ? sizeof(float2) : sizeof(float4));
+  v.offset = opt->offset;
+  int soft_smem = 0;
+  dim3 soft_grid;
+  if (v.split) v.split = soft_fwd_setup(in, opt, v, p, w, dev, out != nullptr, soft_smem, soft_grid);
+  if (v.split) {
+    build_table(K, true, false, p.tab);
+    e = launch_hist_any(p, v, soft_grid, soft_smem, in->x_dtype, s, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "soft histogram kernel launch");
+    if (out && !p.do_epilogue) {
+      e = launch_epilogue(hist, p.epi, w.epi_counter, w.epi_partial, s);
+      if (e != cudaSuccess) return cuda_fail(e, "epilogue kernel launch");
+    }
+    return ACE_B200_OK;
+  }
+
+  // hist_kernel. Shared-memory table: `entries` words per lane replica. A 32-bit
+  // word of a replica takes at most (threads / R) * V additions per tile and must
+  // not take more than 1023 between two folds (values up to 2^21 each), so R has
+  // a floor; above it, as many replicas as fit in ~100 KB (32 = conflict-free),
+  // two CTAs of kHistThreads per SM.
+  const int threads = kHistThreads;
+  const size_t table_budget = 100 * 1024;
+  const int words = soft ? (in->target_kind == ACE_B200_TARGET_LABELS ? 7 : 9) : 3;  // odd
+  const int entries = CL * (soft ? K + 1 : K) * words;
+  const size_t table_bytes = (size_t)(K + 1) * kTabCopies * sizeof(float4);
   auto r_min = [&](int V) {
     int r = 1;
     while ((threads / r) * V > 1023) r <<= 1;
@@ -371,32 +472,10 @@ int hist_impl(const ace_b200_inputs* in, const ace_b200_options* opt, float* his
     return fail(ACE_B200_EUNSUPPORTED,
                 "statistics table of %d channels x %d bins does not fit in shared memory", CL, K);
 
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   const int occ = occupancy(0, in->x_dtype, v, smem, dev);
-  p.x = in->x;
-  p.target = in->target;
   p.g = make_grid(in, CL, opt->offset, v.V, threads, occ, dev, true);
-  if (v.split && p.g.chunks_per_batch > 0) {
-    // the class-split kernel splits each batch's warp tiles evenly over its CTAs
-    const int64_t wtiles = (in->N + 32 * v.V - 1) / (32 * v.V);
-    int64_t cb = (int64_t)sm_count(dev) * occ / p.g.B;
-    cb = cb < wtiles ? cb : wtiles;
-    p.g.chunks_per_batch = (int)(cb > 0 ? cb : 1);
-    p.g.chunks = p.g.chunks_per_batch * p.g.B;
-  }
-  p.act = opt->activation;
-  p.soft = soft;
   p.R = R;
   p.flush_tiles = 1023 / ((threads / R) * v.V);
-  p.b_offset = (int)in->b_offset;
-  p.B_total = (int)in->b_total;
-  const Workspace w = carve(workspace, in->b_total, CL, K);
-  p.accum = w.accum;
-  p.counter = w.hist_counter;
-  p.hist_out = hist;
-  build_table(K, soft, opt->right != 0, p.tab);
   // The last CTA runs the epilogue itself when all statistics fit in its (then
   // free) shared-memory table and the rows are few; otherwise a multi-CTA
   // epilogue kernel follows.
@@ -406,10 +485,7 @@ int hist_impl(const ace_b200_inputs* in, const ace_b200_options* opt, float* his
   p.do_epilogue = fused ? 1 : 0;
 
   const dim3 grid((unsigned)p.g.chunks, 1u);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (in->x_dtype == ACE_B200_F32) e = launch_hist<float>(p, v, grid, smem, s);
-  else if (in->x_dtype == ACE_B200_BF16) e = launch_hist<__nv_bfloat16>(p, v, grid, smem, s);
-  else e = launch_hist<__half>(p, v, grid, smem, s);
+  e = launch_hist_any(p, v, grid, smem, in->x_dtype, s, dev);
   if (e != cudaSuccess) return cuda_fail(e, "histogram kernel launch");
   if (out && !fused) {
     e = launch_epilogue(hist, p.epi, w.epi_counter, w.epi_partial, s);
@@ -506,7 +582,7 @@ extern "C" {
 
 size_t ace_b200_workspace_bytes(int64_t b_total, int64_t cl, int32_t num_bins) {
   if (b_total < 1 || cl < 1 || num_bins < 1) return 1024;
-  return accum_bytes(b_total, cl, num_bins) + 512 +
+  return accum_bytes(b_total, cl, num_bins) + 512 + pool_bytes(b_total) +
          round_up((size_t)epi_ctas(b_total * cl) * sizeof(float), 256);
 }
 
@@ -611,9 +687,9 @@ int ace_b200_backward(const ace_b200_inputs* in, const ace_b200_options* opt,
   build_table(K, soft, opt->right != 0, p.tab);
   const dim3 grid((unsigned)p.g.chunks_per_batch, (unsigned)p.g.B);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (in->x_dtype == ACE_B200_F32) e = launch_grad<float>(p, v, grid, smem, s);
-  else if (in->x_dtype == ACE_B200_BF16) e = launch_grad<__nv_bfloat16>(p, v, grid, smem, s);
-  else e = launch_grad<__half>(p, v, grid, smem, s);
+  if (in->x_dtype == ACE_B200_F32) e = launch_grad<float>(p, v, grid, smem, s, dev);
+  else if (in->x_dtype == ACE_B200_BF16) e = launch_grad<__nv_bfloat16>(p, v, grid, smem, s, dev);
+  else e = launch_grad<__half>(p, v, grid, smem, s, dev);
   if (e != cudaSuccess) return cuda_fail(e, "gradient kernel launch");
   return ACE_B200_OK;
 }

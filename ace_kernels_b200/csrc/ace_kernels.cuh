@@ -18,23 +18,25 @@ struct Variant {
   bool softmax; // activation softmax over C > 1 channels (else none / sigmoid)
   bool soft;    // soft binning
   bool labels;  // int64 labels (else dense fp32 targets)
-  bool split;   // forward only: soft_hist_kernel (softmax, CM <= 4, soft, labels)
+  bool split;   // forward only: soft_fwd_kernel (softmax, CM <= 4, soft, labels)
+  int offset;   // soft_fwd_kernel: 1 when the background channel is dropped
 };
 
 template <typename T>
 cudaError_t launch_hist(const FwdParams& p, const Variant& v, dim3 grid, int smem,
-                        cudaStream_t s);
+                        cudaStream_t s, int dev);
 template <typename T>
 cudaError_t launch_grad(const BwdParams& p, const Variant& v, dim3 grid, int smem,
-                        cudaStream_t s);
+                        cudaStream_t s, int dev);
 template <typename T>
 cudaError_t launch_probs(const void* x, float* probs, int64_t B, int C, int64_t N, int act,
                          cudaStream_t s);
-// Occupancy (CTAs per SM) of the variant's kernel with `smem` dynamic bytes.
+// Occupancy (CTAs per SM) of the variant's kernel with `smem` dynamic bytes on
+// device `dev` (the current device).
 template <typename T>
-int hist_occupancy(const Variant& v, int smem);
+int hist_occupancy(const Variant& v, int smem, int dev);
 template <typename T>
-int grad_occupancy(const Variant& v, int smem);
+int grad_occupancy(const Variant& v, int smem, int dev);
 
 // Multi-CTA epilogue on [3, B_total, CL, K] statistics; `ws` holds a counter
 // (left at zero) and one partial sum per CTA.
@@ -212,16 +214,6 @@ struct Acc {
   }
 };
 
-// Soft binning with class labels and a register-tile softmax (soft_hist_kernel):
-// the slots are (interval j, class flag t), slot 2 j + t, where t = 1 when the row
-// is the voxel's class. Every value then makes exactly one update of four words,
-// 0 n, 1-2 u, 3 u^2 (word 4 pads the stride to an odd count), and the target
-// moments are the t = 1 slot's n and u: no second update for the true class.
-struct AccSplit {
-  static constexpr int NW = 5;
-  static constexpr int NOUT = 3;  // n, sum u, sum u^2 per slot (fold_split)
-};
-
 constexpr float kFixMagic = 12582912.0f;         // 1.5 * 2^23
 constexpr unsigned kFixMagicBits = 0x4B400000u;  // bits of kFixMagic
 
@@ -300,62 +292,6 @@ __device__ __forceinline__ void fold_table(unsigned* hist, int CL, int slots, in
   uint4* h4 = reinterpret_cast<uint4*>(hist);
   for (int i = threadIdx.x; i < words / 4; i += blockDim.x) h4[i] = make_uint4(0u, 0u, 0u, 0u);
   for (int i = (words & ~3) + threadIdx.x; i < words; i += blockDim.x) hist[i] = 0u;
-}
-
-// Fold of the class-split soft table (AccSplit): item i takes slot e = i / G of
-// the [CL * slots] slots and a quarter (G = 4) of its R replicas, reads the four
-// words of each replica at once, removes the fixed-point bias with the replica's
-// count and adds exactly in 64-bit integers; the G lanes of a slot combine their
-// parts with shuffles and the first issues one fp64 atomic per non-zero sum
-// (n, sum u, sum u^2). No divisions by runtime values: G and the slot count per
-// item round are powers of two or loop strides. `clear`: zero the table after
-// the fold (not needed when the CTA is done with it). Called by all threads
-// between barriers.
-__device__ __forceinline__ void fold_split(unsigned* hist, int entries, int R, double* accum,
-                                           int64_t out_stride, int64_t row_base, bool clear) {
-  constexpr int NW = AccSplit::NW;
-  const int gsh = R >= 4 ? 2 : (R == 2 ? 1 : 0);
-  const int G = 1 << gsh, per = R >> gsh;
-  const double unit = 1.0 / (double)kFixScale;
-  const int total = entries << gsh;
-  for (int i0 = 0; i0 < total; i0 += blockDim.x) {  // uniform trip count: full-warp shuffles
-    const int i = i0 + (int)threadIdx.x;
-    const bool valid = i < total;
-    const int e = valid ? i >> gsh : 0, part = i & (G - 1);
-    const unsigned* base = hist + e * R * NW;
-    long long hi = 0, lo = 0, q = 0;
-    int n = 0;
-    if (valid) {
-      for (int k = 0; k < per; ++k) {
-        const unsigned* w = base + ((part * per + k + e) & (R - 1)) * NW;
-        const unsigned cnt = w[0];
-        const unsigned bias = cnt * kFixMagicBits;
-        n += (int)cnt;
-        hi += (int)(w[1] - bias);
-        lo += (int)(w[2] - bias);
-        q += (int)(w[3] - bias);
-      }
-    }
-    for (int o = 1; o < G; o <<= 1) {
-      n += __shfl_xor_sync(0xffffffffu, n, o);
-      hi += __shfl_xor_sync(0xffffffffu, hi, o);
-      lo += __shfl_xor_sync(0xffffffffu, lo, o);
-      q += __shfl_xor_sync(0xffffffffu, q, o);
-    }
-    if (valid && part == 0 && n != 0) {
-      double* a = accum + row_base + e;  // [3][rows * slots]: e = row * slots + slot
-      atomicAdd(a, (double)n);
-      atomicAdd(a + out_stride, (double)(hi * (long long)kFixScale + lo) * (unit * unit));
-      atomicAdd(a + 2 * out_stride, (double)q * unit);
-    }
-  }
-  if (clear) {
-    __syncthreads();
-    const int words = entries * R * NW;
-    uint4* h4 = reinterpret_cast<uint4*>(hist);
-    for (int i = threadIdx.x; i < words / 4; i += blockDim.x) h4[i] = make_uint4(0u, 0u, 0u, 0u);
-    for (int i = (words & ~3) + threadIdx.x; i < words; i += blockDim.x) hist[i] = 0u;
-  }
 }
 
 // Channel count of a kernel instance: exact for softmax instances with CM <= 4
@@ -797,265 +733,11 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constan
   }
 }
 
-// ---------------------------------------------------------------------------
-// Forward for soft binning with class labels and a softmax over C <= 4 channels
-// (the register-tile case): the same table replicas, folds and last-CTA handoff
-// as hist_kernel, with fewer instructions per value:
-// - the fast softmax (ace_softmax_fast);
-// - the interval is the rounded p K of the saturated p (NaN -> 0), so it lies in
-//   [0, K] without a clamp and without the exact test (see soft_entry above);
-// - slots split by class flag (AccSplit): one update of four words per value,
-//   and no per-voxel update for the true class.
-// One CTA of kSplitThreads (24 warps) per SM. With per-batch chunks the warps of
-// a CTA take warp tiles (32 x V voxels) of the CTA's share from a shared-memory
-// counter, so no warp waits for another until the share is done (warps that the
-// SM schedules first simply take more tiles), and each warp issues the loads of
-// its next tile before it adds the current one (two tiles in flight per warp,
-// hence 24 warps of up to 85 registers). A flat split (chunks that cross
-// batches) streams CTA tiles of kSplitThreads x V voxels. The last CTA merges the
-// two slots of each interval into the n, sum t, sum t^2, ny, sum t y moments of
-// hist_kernel's reconstruction.
-// ---------------------------------------------------------------------------
-template <typename T, int V, int C>
-__global__ void __launch_bounds__(kSplitThreads, 1) soft_hist_kernel(const __grid_constant__ FwdParams P) {
-  using L = AccSplit;
-  constexpr int NW = L::NW;
-  constexpr int NT = kSplitThreads;
-  extern __shared__ __align__(16) float smem[];
-  const int tid = threadIdx.x, lane = tid & 31;
-  const int CL = P.g.CL, off = P.g.offset, K = P.tab.K;
-  const int slots = 2 * (K + 1);
-  const int64_t N = P.g.N;
-  const int R = P.R;
-  const float Kf = (float)K;
+}  // namespace ace
 
-  float2* map_t = reinterpret_cast<float2*>(smem);
-  unsigned* hist = reinterpret_cast<unsigned*>(map_t + (K + 1) * kTabCopies);
-  const int table_words = CL * slots * R * NW;
-  for (int i = tid; i < (K + 1) * kTabCopies; i += NT) map_t[i] = P.tab.map[i / kTabCopies];
-  const float2* my_map = map_t + (tid & (kTabCopies - 1));
-  {
-    uint4* h4 = reinterpret_cast<uint4*>(hist);  // 16-byte aligned: (K + 1) * 128 bytes in
-    for (int i = tid; i < table_words / 4; i += NT) h4[i] = make_uint4(0u, 0u, 0u, 0u);
-    for (int i = (table_words & ~3) + tid; i < table_words; i += NT) hist[i] = 0u;
-  }
-  ace_grid_dependency_wait();  // programmatic dependent launch (see hist_kernel)
-  __syncthreads();
+#include "ace_soft_fwd.cuh"  // soft_fwd_kernel (uses the helpers above)
 
-  const int slot_stride = R * NW, row_stride = slots * slot_stride;
-  // word offset of row (c - off), interval 0, flag 0, this lane's replica
-  const int col = (tid & (R - 1)) * NW - off * row_stride;
-  const int64_t out_stride = (int64_t)P.B_total * CL * slots;
-
-  const int64_t tpb = P.g.tiles > 0 ? P.g.tiles : 1;
-  int since_fold = 0;
-  const bool pf_x = ((reinterpret_cast<uintptr_t>(P.x) | (N * sizeof(T))) & 15) == 0;
-  const T* xb;
-  const int64_t* lb;
-  int64_t row0;
-  auto set_batch = [&](int bb) {
-    xb = static_cast<const T*>(P.x) + (int64_t)bb * C * N;
-    lb = static_cast<const int64_t*>(P.target) + (int64_t)bb * N;
-    row0 = (int64_t)(P.b_offset + bb) * CL;
-  };
-  // L2 prefetch of `count` voxels from voxel `start` of the current batch (one
-  // lane per channel row and one for the labels).
-  auto prefetch = [&](int64_t start, int64_t count, int who) {
-    if (!pf_x) return;
-    if (who < C) ace_prefetch_tile(xb + (int64_t)who * N, start, count, N, sizeof(T));
-    if (who == C) ace_prefetch_tile(lb, start, count, N, 8);
-  };
-  // A thread's V voxels: loaded (load_group) and added into the table
-  // (add_group) as separate steps, so that the next group's loads can be in
-  // flight while this one is added. V > 1 implies N % V == 0: groups are whole.
-  struct Group {
-    int lab[V];
-    float xv[C][V];
-  };
-  auto load_group = [&](int64_t v0, Group& gr) {
-    if (v0 >= N) return;
-    // the low word of each int64 label (one register per voxel while in flight)
-#pragma unroll
-    for (int i = 0; i < V; ++i) gr.lab[i] = __ldg(reinterpret_cast<const int*>(lb + v0 + i));
-#pragma unroll
-    for (int c = 0; c < C; ++c) VecIO<T, V>::load(xb + (int64_t)c * N + v0, gr.xv[c]);
-  };
-  auto add_group = [&](int64_t v0, const Group& gr) {
-    if (v0 >= N) return;
-    const int (&lab)[V] = gr.lab;
-#pragma unroll
-    for (int i = 0; i < V; ++i) {
-      float p[C];
-#pragma unroll
-      for (int c = 0; c < C; ++c) p[c] = gr.xv[c][i];
-      ace_softmax_fast<C>(p, C);
-#pragma unroll
-      for (int c = 0; c < C; ++c) {
-        if (c < off) continue;
-        const int j = (int)(__float_as_uint(__fmaf_rn(__saturatef(p[c]), Kf, kFixMagic)) -
-                            kFixMagicBits);
-        const float2 m = my_map[j * kTabCopies];
-        const float us = fminf(ACE_FMUL(ACE_FSUB(p[c], m.x), m.y), kFixScale);
-        const int a = col + c * row_stride + j * (2 * slot_stride) + (lab[i] == c ? slot_stride : 0);
-        const uint2 uw = fix2_scaled(us);
-        sadd(hist, a, 1u);
-        sadd(hist, a + 1, uw.x);
-        sadd(hist, a + 2, uw.y);
-        sadd(hist, a + 3, __float_as_uint(__fmaf_rn(us, ACE_FMUL(us, 1.0f / kFixScale), kFixMagic)));
-      }
-    }
-  };
-  auto fold_clear = [&]() {
-    __syncthreads();
-    fold_split(hist, CL * slots, R, P.accum, out_stride, row0 * slots, true);
-    __syncthreads();
-  };
-
-  if (P.g.chunks_per_batch > 0) {
-    // CTA k of batch bx takes warp tiles [k W / cb, (k + 1) W / cb) of the W warp
-    // tiles (32 x V voxels) of the batch. A replica word takes at most
-    // V * 32 / R additions per warp tile, so the warp tiles are taken in epochs
-    // of at most 1023 / (V * 32 / R), with a fold between epochs. Each warp
-    // takes its next tile and issues its loads before it adds the current one.
-    __shared__ unsigned s_ctr;
-    constexpr int WT = 32 * V;  // voxels per warp tile
-    const int cb = P.g.chunks_per_batch;
-    const int bx = (int)blockIdx.x / cb, k = (int)blockIdx.x - bx * cb;
-    set_batch(bx);
-    const int64_t wtpb = (N + WT - 1) / WT;
-    const int64_t w_begin = wtpb * k / cb, w_end = wtpb * (k + 1) / cb;
-    const int64_t epoch = 1023 / (V * (32 / (R < 32 ? R : 32)));
-    auto take = [&](int64_t e0) -> int64_t {
-      unsigned i = 0;
-      if (lane == 0) i = atomicAdd(&s_ctr, 1u);
-      return e0 + __shfl_sync(0xffffffffu, i, 0);
-    };
-    for (int64_t e0 = w_begin; e0 < w_end; e0 += epoch) {
-      const int64_t e1 = min(e0 + epoch, w_end);
-      if (tid == 0) s_ctr = 0u;
-      __syncthreads();
-      int64_t wt = take(e0);
-      Group cur;
-      if (wt < e1) load_group((wt * 32 + lane) * V, cur);
-      while (wt < e1) {
-        const int64_t wn = take(e0);
-        Group nxt;
-        if (wn < e1) load_group((wn * 32 + lane) * V, nxt);
-        // the warp tile about two rounds ahead, likely taken by some warp then
-        if (wn + 2 * (NT / 32) < e1) prefetch((wn + 2 * (NT / 32)) * WT, WT, lane);
-        add_group((wt * 32 + lane) * V, cur);
-        wt = wn;
-        cur = nxt;
-      }
-      if (e1 < w_end) fold_clear();
-    }
-  } else {
-    // Flat: CTA x streams CTA tiles [g0, g1) (chunk_range), crossing into the
-    // next batch (after a fold of this batch's rows) where the run does.
-    const int64_t tile = (int64_t)NT * V;
-    int64_t g0, g1;
-    chunk_range(P.g, g0, g1);
-    int b = (int)(g0 / tpb);
-    int64_t t = g0 - b * tpb;
-    set_batch(b);
-    for (int64_t g = g0; g < g1; ++g, ++t) {
-      if (t == tpb) {
-        fold_clear();
-        since_fold = 0;
-        ++b;
-        t = 0;
-        set_batch(b);
-      }
-      if (t + 1 < tpb && g + 1 < g1) prefetch((t + 1) * tile, tile, tid);
-      Group gr;
-      load_group((t * NT + tid) * V, gr);
-      add_group((t * NT + tid) * V, gr);
-      if (++since_fold == P.flush_tiles && g + 1 < g1) {
-        since_fold = 0;
-        fold_clear();
-      }
-    }
-  }
-  ace_launch_dependents();
-  __syncthreads();
-  fold_split(hist, CL * slots, R, P.accum, out_stride, row0 * slots, false);
-  __syncthreads();
-  __shared__ bool s_last;
-  if (tid == 0) {
-    unsigned done;
-    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
-                 : "=r"(done)
-                 : "l"(P.counter)
-                 : "memory");
-    s_last = (done == gridDim.x * gridDim.y - 1);
-  }
-  __syncthreads();
-  if (!s_last) return;
-
-  // Last CTA: W, P, G per bin from the interval moments (as hist_kernel), each
-  // interval's moments being the sum of its two class-flag slots, and its target
-  // moments those of the flag-1 slot.
-  const int rows = P.B_total * CL;
-  const int64_t stat_stride = (int64_t)rows * K;
-  const bool stage = P.do_epilogue && 3 * stat_stride <= (int64_t)table_words;
-  float* staged = reinterpret_cast<float*>(hist);
-  const double* acc = P.accum;
-  for (int64_t e = tid; e < stat_stride; e += NT) {
-    const int64_t r = e / K;
-    const int k = (int)(e - r * K);
-    // the four slots of intervals k and k + 1 (flags 0, 1 each) are consecutive:
-    // all twelve sums are loaded before any is used (one L2 round trip)
-    const int64_t g0 = r * slots + 2 * k;
-    double m[3][4];
-#pragma unroll
-    for (int o = 0; o < 3; ++o)
-#pragma unroll
-      for (int q = 0; q < 4; ++q) m[o][q] = __ldcg(acc + o * out_stride + g0 + q);
-    double w = 0.0, pp = 0.0, gsum = 0.0;
-#pragma unroll
-    for (int side = 0; side < 2; ++side) {
-      const int j = k + side;
-      const double ny = m[0][2 * side + 1], yu = m[1][2 * side + 1];
-      const double n = m[0][2 * side] + ny;
-      const double su = m[1][2 * side] + yu;
-      if (j == 0 || j == K) {
-        w += n;
-        pp += su;
-        gsum += ny;
-        continue;
-      }
-      const double su2 = m[2][2 * side] + m[2][2 * side + 1];
-      const double lo = P.tab.lohi[j].x, span = (double)P.tab.lohi[j].y - lo;
-      const double pt = lo * su + span * su2;
-      if (side == 0) {
-        w += su;
-        pp += pt;
-        gsum += yu;
-      } else {
-        w += n - su;
-        pp += lo * n + span * su - pt;
-        gsum += ny - yu;
-      }
-    }
-    const float wf = (float)w, pf = (float)pp, gf = (float)gsum;
-    P.hist_out[e] = wf;
-    P.hist_out[stat_stride + e] = pf;
-    P.hist_out[2 * stat_stride + e] = gf;
-    if (stage) {
-      staged[e] = wf;
-      staged[stat_stride + e] = pf;
-      staged[2 * stat_stride + e] = gf;
-    }
-  }
-  __syncthreads();
-  double* accw = P.accum;
-  for (int64_t i = tid; i < L::NOUT * out_stride; i += NT) __stcg(accw + i, 0.0);
-  if (tid == 0) *P.counter = 0u;
-  if (stage) {
-    __syncthreads();
-    write_loss_if0(P.epi, epilogue_rows(P.epi, staged, rows, 0, 0, rows));
-  }
-}
+namespace ace {
 
 // ---------------------------------------------------------------------------
 // Backward: d loss / d x in one pass (ace_kernels/impls/v2_autograd.py:88-118,
@@ -1382,77 +1064,50 @@ cudaError_t launch_dependent(K* kernel, dim3 grid, int threads, int smem, cudaSt
 }
 
 // Opt a kernel in to `smem` dynamic shared-memory bytes when static + dynamic
-// would exceed the default 48 KB (once per kernel and size).
+// would exceed the default 48 KB. The attribute belongs to the current device
+// only, so the size already granted is kept per device (`granted[dev]`): a
+// process that drives several GPUs opts in on each of them.
 template <typename K>
-cudaError_t set_smem(K* kernel, int smem, int& configured) {
-  if (smem <= 40 * 1024 || smem <= configured) return cudaSuccess;
+cudaError_t set_smem(K* kernel, int smem, int* granted, int dev) {
+  if (smem <= 40 * 1024) return cudaSuccess;
+  if (dev >= 0 && dev < kMaxDevices && smem <= granted[dev]) return cudaSuccess;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e == cudaSuccess) configured = smem;
+  if (e == cudaSuccess && dev >= 0 && dev < kMaxDevices) granted[dev] = smem;
   return e;
 }
 
-template <typename T, int V, int CM, bool SM, bool SOFT, bool LAB>
-struct HistLauncher {
-  static int& configured() {
-    static int bytes = 0;  // dynamic shared memory this instance is opted in to
-    return bytes;
+// One launcher per kernel instance: `granted` is its per-device opt-in state.
+#define ACE_LAUNCHER(NAME, KERNEL, THREADS, PARAMS)                                       \
+  struct NAME {                                                                          \
+    static int* granted() {                                                              \
+      static int bytes[kMaxDevices] = {0};                                               \
+      return bytes;                                                                      \
+    }                                                                                    \
+    static cudaError_t run(const PARAMS& p, dim3 grid, int smem, cudaStream_t s, int dev) { \
+      cudaError_t e = set_smem(KERNEL, smem, granted(), dev);                            \
+      if (e != cudaSuccess) return e;                                                    \
+      return launch_dependent(KERNEL, grid, THREADS, smem, s, p);                        \
+    }                                                                                    \
+    static int occupancy(int smem, int dev) {                                            \
+      set_smem(KERNEL, smem, granted(), dev);                                            \
+      int n = 0;                                                                         \
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, KERNEL, THREADS, smem) !=    \
+          cudaSuccess)                                                                   \
+        n = 1;                                                                           \
+      return n > 0 ? n : 1;                                                              \
+    }                                                                                    \
   }
-  static cudaError_t run(const FwdParams& p, dim3 grid, int smem, cudaStream_t s) {
-    auto k = hist_kernel<T, V, CM, SM, SOFT, LAB>;
-    cudaError_t e = set_smem(k, smem, configured());
-    if (e != cudaSuccess) return e;
-    return launch_dependent(k, grid, kHistThreads, smem, s, p);
-  }
-  static int occupancy(int smem) {
-    auto k = hist_kernel<T, V, CM, SM, SOFT, LAB>;
-    set_smem(k, smem, configured());
-    int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, kHistThreads, smem) != cudaSuccess) n = 1;
-    return n > 0 ? n : 1;
-  }
-};
-
-template <typename T, int V, int C>
-struct SoftHistLauncher {
-  static int& configured() {
-    static int bytes = 0;
-    return bytes;
-  }
-  static cudaError_t run(const FwdParams& p, dim3 grid, int smem, cudaStream_t s) {
-    auto k = soft_hist_kernel<T, V, C>;
-    cudaError_t e = set_smem(k, smem, configured());
-    if (e != cudaSuccess) return e;
-    return launch_dependent(k, grid, kSplitThreads, smem, s, p);
-  }
-  static int occupancy(int smem) {
-    auto k = soft_hist_kernel<T, V, C>;
-    set_smem(k, smem, configured());
-    int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, kSplitThreads, smem) != cudaSuccess) n = 1;
-    return n > 0 ? n : 1;
-  }
-};
 
 template <typename T, int V, int CM, bool SM, bool SOFT, bool LAB>
-struct GradLauncher {
-  static int& configured() {
-    static int bytes = 0;
-    return bytes;
-  }
-  static cudaError_t run(const BwdParams& p, dim3 grid, int smem, cudaStream_t s) {
-    auto k = grad_kernel<T, V, CM, SM, SOFT, LAB>;
-    cudaError_t e = set_smem(k, smem, configured());
-    if (e != cudaSuccess) return e;
-    return launch_dependent(k, grid, kThreads, smem, s, p);
-  }
-  static int occupancy(int smem) {
-    auto k = grad_kernel<T, V, CM, SM, SOFT, LAB>;
-    set_smem(k, smem, configured());
-    int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, kThreads, smem) != cudaSuccess) n = 1;
-    return n > 0 ? n : 1;
-  }
-};
+ACE_LAUNCHER(HistLauncher, (hist_kernel<T, V, CM, SM, SOFT, LAB>), kHistThreads, FwdParams);
+
+template <typename T, int C, int OFF>
+ACE_LAUNCHER(SoftFwdLauncher, (soft_fwd_kernel<T, C, OFF>), kSoftThreads, FwdParams);
+
+template <typename T, int V, int CM, bool SM, bool SOFT, bool LAB>
+ACE_LAUNCHER(GradLauncher, (grad_kernel<T, V, CM, SM, SOFT, LAB>), kThreads, BwdParams);
+
+#undef ACE_LAUNCHER
 
 }  // namespace
 
@@ -1499,47 +1154,48 @@ struct GradLauncher {
     BODY;                                                \
   }
 
-// The class-split soft forward: exact channel counts 2..4, full or single vectors.
-#define ACE_SPLIT_CASES(F, T, ...)                                                        \
+// The soft forward for labels and C <= 4: exact channel counts 2..4, background
+// kept (offset 0) or dropped (offset 1); full vectors only (v.V is the dtype's
+// 16-byte width: the bulk copies move 16-byte multiples).
+#define ACE_SOFT_FWD_CASES(F, T, ...)                                                     \
   do {                                                                                    \
-    constexpr int VM = 16 / (int)sizeof(T);                                               \
     if (v.split) {                                                                        \
-      if (v.CM == 2 && v.V == VM) return SoftHistLauncher<T, VM, 2>::F(__VA_ARGS__);     \
-      if (v.CM == 2 && v.V == 1) return SoftHistLauncher<T, 1, 2>::F(__VA_ARGS__);       \
-      if (v.CM == 3 && v.V == VM) return SoftHistLauncher<T, VM, 3>::F(__VA_ARGS__);     \
-      if (v.CM == 3 && v.V == 1) return SoftHistLauncher<T, 1, 3>::F(__VA_ARGS__);       \
-      if (v.CM == 4 && v.V == VM) return SoftHistLauncher<T, VM, 4>::F(__VA_ARGS__);     \
-      if (v.CM == 4 && v.V == 1) return SoftHistLauncher<T, 1, 4>::F(__VA_ARGS__);       \
+      if (v.CM == 2 && v.offset == 0) return SoftFwdLauncher<T, 2, 0>::F(__VA_ARGS__);   \
+      if (v.CM == 2 && v.offset == 1) return SoftFwdLauncher<T, 2, 1>::F(__VA_ARGS__);   \
+      if (v.CM == 3 && v.offset == 0) return SoftFwdLauncher<T, 3, 0>::F(__VA_ARGS__);   \
+      if (v.CM == 3 && v.offset == 1) return SoftFwdLauncher<T, 3, 1>::F(__VA_ARGS__);   \
+      if (v.CM == 4 && v.offset == 0) return SoftFwdLauncher<T, 4, 0>::F(__VA_ARGS__);   \
+      if (v.CM == 4 && v.offset == 1) return SoftFwdLauncher<T, 4, 1>::F(__VA_ARGS__);   \
     }                                                                                     \
   } while (0)
 
 template <typename T>
 cudaError_t launch_hist(const FwdParams& p, const Variant& v, dim3 grid, int smem,
-                        cudaStream_t s) {
-  ACE_SPLIT_CASES(run, T, p, grid, smem, s);
+                        cudaStream_t s, int dev) {
+  ACE_SOFT_FWD_CASES(run, T, p, grid, smem, s, dev);
   if (v.split) return cudaErrorInvalidValue;
-  ACE_FOR_SOFT_LABELS(ACE_VARIANT_CASES(HistLauncher, run, T, p, grid, smem, s));
+  ACE_FOR_SOFT_LABELS(ACE_VARIANT_CASES(HistLauncher, run, T, p, grid, smem, s, dev));
   return cudaErrorInvalidValue;
 }
 
 template <typename T>
 cudaError_t launch_grad(const BwdParams& p, const Variant& v, dim3 grid, int smem,
-                        cudaStream_t s) {
-  ACE_FOR_SOFT_LABELS(ACE_VARIANT_CASES(GradLauncher, run, T, p, grid, smem, s));
+                        cudaStream_t s, int dev) {
+  ACE_FOR_SOFT_LABELS(ACE_VARIANT_CASES(GradLauncher, run, T, p, grid, smem, s, dev));
   return cudaErrorInvalidValue;
 }
 
 template <typename T>
-int hist_occupancy(const Variant& v, int smem) {
-  ACE_SPLIT_CASES(occupancy, T, smem);
+int hist_occupancy(const Variant& v, int smem, int dev) {
+  ACE_SOFT_FWD_CASES(occupancy, T, smem, dev);
   if (v.split) return 1;
-  ACE_FOR_SOFT_LABELS(ACE_VARIANT_CASES(HistLauncher, occupancy, T, smem));
+  ACE_FOR_SOFT_LABELS(ACE_VARIANT_CASES(HistLauncher, occupancy, T, smem, dev));
   return 1;
 }
 
 template <typename T>
-int grad_occupancy(const Variant& v, int smem) {
-  ACE_FOR_SOFT_LABELS(ACE_VARIANT_CASES(GradLauncher, occupancy, T, smem));
+int grad_occupancy(const Variant& v, int smem, int dev) {
+  ACE_FOR_SOFT_LABELS(ACE_VARIANT_CASES(GradLauncher, occupancy, T, smem, dev));
   return 1;
 }
 
@@ -1557,11 +1213,11 @@ cudaError_t launch_probs(const void* x, float* probs, int64_t B, int C, int64_t 
 
 #define ACE_INSTANTIATE(T)                                                                   \
   template cudaError_t launch_hist<T>(const FwdParams&, const Variant&, dim3, int,          \
-                                      cudaStream_t);                                         \
+                                      cudaStream_t, int);                                    \
   template cudaError_t launch_grad<T>(const BwdParams&, const Variant&, dim3, int,          \
-                                      cudaStream_t);                                         \
-  template int hist_occupancy<T>(const Variant&, int);                                       \
-  template int grad_occupancy<T>(const Variant&, int);                                       \
+                                      cudaStream_t, int);                                    \
+  template int hist_occupancy<T>(const Variant&, int, int);                                  \
+  template int grad_occupancy<T>(const Variant&, int, int);                                  \
   template cudaError_t launch_probs<T>(const void*, float*, int64_t, int, int64_t, int,     \
                                        cudaStream_t);
 

@@ -1,0 +1,530 @@
+// soft_fwd_kernel: the forward of soft binning with int64 class labels and a
+// softmax over C <= 4 channels (the headline workload's case), on B200 (sm_100a).
+// Included by ace_kernels.cuh after the shared helpers (epilogue, fixed point).
+//
+// It computes what hist_kernel computes for that case (the reference's
+// binning.soft_stats, ace_kernels/binning.py:74-116, via the two-bin linear
+// assignment of ace_kernels/common.py:43-61, then the epilogue) as a pipeline
+// whose memory side never waits for its arithmetic side:
+//
+// - Warp specialisation and a TMA ring. One producer thread streams tiles of
+//   kSoftTileVoxels voxels (the C logit rows and the labels of one batch) from
+//   HBM into a ring of shared-memory stages with bulk copies
+//   (cp.async.bulk ... mbarrier::complete_tx), up to `stages` tiles ahead (~80
+//   to 120 KB in flight per SM). kSoftConsumerWarps consumer warps wait on a
+//   stage's "full" barrier, read their 4 voxels with 16-byte shared loads, release
+//   the stage on its "empty" barrier and add the voxels into the statistics.
+// - Dynamic tile scheduler. The producer claims tiles from a per-batch global
+//   counter, one claim ahead (its latency hides behind the stages in flight).
+//   CTAs start spread over the batches; a CTA whose batch runs out moves on to
+//   another batch with tiles left, so SMs that run faster take more tiles.
+// - Interval coordinate without a table lookup. The value's interval j (between
+//   bin centres j-1 and j; the end intervals 0 and K hold one end bin each) is
+//   the rounded p K, and its coordinate is r = p K - j in [-1/2, 1/2], taken from
+//   the same fused multiply-add (exact before its one rounding). The reference's
+//   right-bin weight u = (p - c_{j-1}) / (c_j - c_{j-1}), with its fp32 centres,
+//   is affine in r: u = a_j r + b_j. The kernel sums n, sum r and sum r^2 per
+//   slot; the last CTA maps them to sum u and sum u^2 exactly (in double). (The
+//   rounded p K can differ from the exact interval only for p within a few ulp of
+//   a centre, where both intervals give the centre's bin the same weight ~1.)
+// - Slots split by class flag: slot (j, channel c, f) with f = 1 when c is the
+//   voxel's class. Every value makes exactly one update of four 32-bit words
+//   (n, sum r in two words, sum r^2), and the target moments of a row are its
+//   flag-1 slots: no second update for the true class.
+// - The words are integer fixed point in shared memory (2^21 units; sum r has a
+//   second word of the residual, 2^-42 units), updated with red.shared.add.u32
+//   (native; a float shared-memory add is a compare-and-swap loop), lane-
+//   replicated R ways so that the 32 lanes of a warp never share a bank.
+// - Folds add the replicas exactly in 64-bit integers and issue 64-bit integer
+//   global atomics: the sums do not depend on the order of anything, so every
+//   run gives the same bits whichever CTA took which tile.
+//
+// Every wait on a barrier is bounded (kSoftWaitNs); a wait that runs out sets
+// the workspace's error word and the CTA leaves its loops (after the copies it
+// issued have landed), and the last CTA then writes a NaN loss.
+#pragma once
+
+namespace ace {
+
+constexpr int kSoftConsumerWarps = 16;
+constexpr int kSoftThreads = (kSoftConsumerWarps + 1) * 32;  // + one producer warp
+constexpr int kSoftLaneVoxels = 4;                            // voxels per consumer lane per tile
+constexpr int kSoftTileVoxels = kSoftConsumerWarps * 32 * kSoftLaneVoxels;
+constexpr int kSoftMaxStages = 4;
+constexpr int kSoftNW = 5;  // words per slot replica: n, r hi, r lo, r^2, pad (odd)
+constexpr unsigned long long kSoftWaitNs = 1000000000ull;  // bound of every barrier wait (1 s)
+
+__device__ __forceinline__ unsigned smem_addr(const void* p) {
+  return static_cast<unsigned>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ unsigned long long ace_now_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// mbarrier and bulk-copy primitives (shared addresses of this CTA).
+__device__ __forceinline__ void mbar_init(unsigned bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(unsigned bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_tx(unsigned bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(unsigned bar, unsigned parity) {
+  unsigned ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Waits until the barrier's phase of parity `parity` has completed; false if
+// that takes longer than kSoftWaitNs.
+__device__ __forceinline__ bool mbar_wait(unsigned bar, unsigned parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = ace_now_ns();
+  while (!mbar_try_wait(bar, parity))
+    if (ace_now_ns() - t0 > kSoftWaitNs) return false;
+  return true;
+}
+// Bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) from
+// global memory into this CTA's shared memory, completing on barrier `bar`.
+__device__ __forceinline__ void bulk_load(unsigned dst, const void* src, unsigned bytes,
+                                          unsigned bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+// Barrier of the consumer warps only (the producer runs ahead meanwhile).
+__device__ __forceinline__ void consumer_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kSoftConsumerWarps * 32) : "memory");
+}
+
+// One value's four words into the slot replica at shared byte address a.
+__device__ __forceinline__ void red_slot(unsigned a, unsigned n, unsigned hi, unsigned lo,
+                                         unsigned q) {
+  asm volatile(
+      "red.shared.add.u32 [%0], %1;\n\t"
+      "red.shared.add.u32 [%0+4], %2;\n\t"
+      "red.shared.add.u32 [%0+8], %3;\n\t"
+      "red.shared.add.u32 [%0+12], %4;" ::"r"(a),
+      "r"(n), "r"(hi), "r"(lo), "r"(q));
+}
+
+// A lane's kSoftLaneVoxels logits of one channel from a stage, widened to fp32.
+template <typename T>
+__device__ __forceinline__ void lds_logits(unsigned a, float (&x)[4]);
+template <>
+__device__ __forceinline__ void lds_logits<float>(unsigned a, float (&x)[4]) {
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(x[0]), "=f"(x[1]), "=f"(x[2]), "=f"(x[3])
+               : "r"(a));
+}
+template <>
+__device__ __forceinline__ void lds_logits<__nv_bfloat16>(unsigned a, float (&x)[4]) {
+  unsigned w0, w1;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(w0), "=r"(w1) : "r"(a));
+  x[0] = __uint_as_float(w0 << 16);
+  x[1] = __uint_as_float(w0 & 0xffff0000u);
+  x[2] = __uint_as_float(w1 << 16);
+  x[3] = __uint_as_float(w1 & 0xffff0000u);
+}
+template <>
+__device__ __forceinline__ void lds_logits<__half>(unsigned a, float (&x)[4]) {
+  unsigned w0, w1;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(w0), "=r"(w1) : "r"(a));
+  const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&w0));
+  const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&w1));
+  x[0] = f0.x;
+  x[1] = f0.y;
+  x[2] = f1.x;
+  x[3] = f1.y;
+}
+
+// The low words of a lane's kSoftLaneVoxels int64 labels from a stage.
+__device__ __forceinline__ void lds_labels(unsigned a, int (&lab)[4]) {
+  unsigned long long l0, l1, l2, l3;
+  asm volatile("ld.shared.v2.u64 {%0, %1}, [%2];" : "=l"(l0), "=l"(l1) : "r"(a));
+  asm volatile("ld.shared.v2.u64 {%0, %1}, [%2];" : "=l"(l2), "=l"(l3) : "r"(a + 16));
+  lab[0] = (int)l0;
+  lab[1] = (int)l1;
+  lab[2] = (int)l2;
+  lab[3] = (int)l3;
+}
+
+// Fold of the table into the workspace, by the consumer threads. Slot
+// e = (j * C + c) * 2 + f of the (K + 1) * C * 2 slots; item i takes slot i >> gsh
+// and part i & (G - 1) of its R replicas (G = 4 lanes per slot): it removes each
+// replica's fixed-point bias with the replica's count, adds exactly in 64-bit
+// integers, the G lanes combine their parts with shuffles and the first issues
+// four 64-bit integer atomics (n, sum r high and low words, sum r^2) for a
+// non-empty slot of a loss channel. acc layout: [4][rows][K + 1][2] (moment
+// stride `ms`), rows = b_total * CL; `row0` is the global row of loss channel 0
+// of the batch folded. `clear`: zero the table afterwards.
+template <int C, int OFF>
+__device__ __forceinline__ void fold_soft(unsigned* hist, int K, int R, unsigned long long* acc,
+                                          int64_t ms, int64_t row0, bool clear) {
+  constexpr int NW = kSoftNW, NCT = kSoftConsumerWarps * 32;
+  const int slots = (K + 1) * C * 2;
+  const int gsh = R >= 4 ? 2 : (R == 2 ? 1 : 0);
+  const int G = 1 << gsh, per = R >> gsh;
+  const int total = slots << gsh;
+  for (int i0 = 0; i0 < total; i0 += NCT) {  // uniform trip count: full-warp shuffles
+    const int i = i0 + (int)threadIdx.x;
+    const bool valid = i < total;
+    const int e = valid ? i >> gsh : 0, part = i & (G - 1);
+    const unsigned* base = hist + e * R * NW;
+    long long hi = 0, lo = 0, q = 0;
+    unsigned n = 0;
+    if (valid) {
+      for (int k = 0; k < per; ++k) {
+        const unsigned* w = base + ((part * per + k + e) & (R - 1)) * NW;
+        const unsigned cnt = w[0];
+        const unsigned bias = cnt * kFixMagicBits;
+        n += cnt;
+        hi += (int)(w[1] - bias);
+        lo += (int)(w[2] - bias);
+        q += (int)(w[3] - bias);
+      }
+    }
+    for (int o = 1; o < G; o <<= 1) {
+      n += __shfl_xor_sync(0xffffffffu, n, o);
+      hi += __shfl_xor_sync(0xffffffffu, hi, o);
+      lo += __shfl_xor_sync(0xffffffffu, lo, o);
+      q += __shfl_xor_sync(0xffffffffu, q, o);
+    }
+    if (valid && part == 0 && n != 0) {
+      const int f = e & 1, jc = e >> 1;
+      const int j = jc / C, c = jc - j * C;
+      if (c >= OFF) {
+        unsigned long long* a = acc + ((row0 + c - OFF) * (K + 1) + j) * 2 + f;
+        atomicAdd(a, (unsigned long long)n);
+        atomicAdd(a + ms, (unsigned long long)hi);
+        atomicAdd(a + 2 * ms, (unsigned long long)lo);
+        atomicAdd(a + 3 * ms, (unsigned long long)q);
+      }
+    }
+  }
+  if (clear) {
+    consumer_sync();
+    const int words = slots * R * NW;
+    uint4* h4 = reinterpret_cast<uint4*>(hist);
+    for (int i = threadIdx.x; i < words / 4; i += NCT) h4[i] = make_uint4(0u, 0u, 0u, 0u);
+    for (int i = (words & ~3) + threadIdx.x; i < words; i += NCT) hist[i] = 0u;
+  }
+}
+
+template <typename T, int C, int OFF>
+__global__ void __launch_bounds__(kSoftThreads, 1) soft_fwd_kernel(const __grid_constant__ FwdParams P) {
+  constexpr int NCW = kSoftConsumerWarps, NT = kSoftThreads, NW = kSoftNW;
+  constexpr int TV = kSoftTileVoxels, VL = kSoftLaneVoxels;
+  constexpr unsigned XB = TV * sizeof(T);  // bytes of one logit row of a stage
+  constexpr unsigned SB = C * XB + TV * 8;  // bytes of a stage (rows, then labels)
+  static_assert(VL == 4, "lds_logits / lds_labels load four voxels");
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  __shared__ __align__(8) unsigned long long s_full[kSoftMaxStages], s_empty[kSoftMaxStages];
+  __shared__ int4 s_meta[kSoftMaxStages];  // {tile, batch, voxels, 0}; tile < 0: no more tiles
+  __shared__ volatile int s_abort;
+  __shared__ bool s_last;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int CL = C - OFF;
+  const int K = P.tab.K, R = P.R, S = P.stages;
+  const int64_t N = P.g.N;
+  unsigned* hist = reinterpret_cast<unsigned*>(smem_raw);
+  const int table_words = (K + 1) * C * 2 * R * NW;
+  const unsigned stage0 = smem_addr(smem_raw) + (unsigned)P.table_bytes;
+  auto full_bar = [&](int s) { return smem_addr(&s_full[s]); };
+  auto empty_bar = [&](int s) { return smem_addr(&s_empty[s]); };
+  {
+    uint4* h4 = reinterpret_cast<uint4*>(hist);
+    for (int i = tid; i < table_words / 4; i += NT) h4[i] = make_uint4(0u, 0u, 0u, 0u);
+    for (int i = (table_words & ~3) + tid; i < table_words; i += NT) hist[i] = 0u;
+  }
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full_bar(s), 1u);
+      mbar_init(empty_bar(s), (unsigned)NCW);
+    }
+    s_abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  // programmatic dependent launch: global memory only after the previous grid
+  ace_grid_dependency_wait();
+  __syncthreads();
+
+  unsigned* err = P.counter + 1;  // the workspace's error word
+  auto abort_cta = [&]() {
+    s_abort = 1;
+    atomicExch(err, 1u);
+  };
+  const int64_t mstride = (int64_t)P.B_total * CL * (K + 1) * 2;
+  const int B = P.g.B;
+  const int64_t tpb = P.wt_batch;  // tiles per batch
+
+  if (warp == NCW) {
+    // ---------------- producer (one thread) ----------------
+    if (lane == 0) {
+      const T* x = static_cast<const T*>(P.x);
+      const int64_t* lab = static_cast<const int64_t*>(P.target);
+      unsigned* ctr = P.pool_ctr;
+      int b = (int)((int64_t)blockIdx.x * B / gridDim.x);
+      unsigned pend = atomicAdd(ctr + b, 1u);  // claimed one tile ahead
+      int pend_b = b;
+      int issued = 0;
+      for (int i = 0;; ++i) {
+        const int s = i % S;
+        const unsigned use = (unsigned)(i / S);
+        int64_t tile = pend;
+        int tb = pend_b;
+        if (tile >= tpb) {  // this batch is done: take a tile of another one
+          tile = -1;
+          for (int k = 1; k < B; ++k) {
+            const int bb = (pend_b + k) % B;
+            const unsigned t2 = atomicAdd(ctr + bb, 1u);
+            if ((int64_t)t2 < tpb) {
+              tile = t2;
+              tb = bb;
+              break;
+            }
+          }
+        }
+        if (tile >= 0) {
+          pend = atomicAdd(ctr + tb, 1u);
+          pend_b = tb;
+        }
+        // the stage's previous tile must have been read
+        if (use > 0 && !mbar_wait(empty_bar(s), (use - 1) & 1u)) {
+          abort_cta();
+          break;
+        }
+        if (s_abort) break;
+        if (tile < 0) {  // no tiles left: the end marker (no copies)
+          s_meta[s] = make_int4(-1, 0, 0, 0);
+          mbar_arrive(full_bar(s));
+          break;
+        }
+        const int64_t v0 = tile * TV;
+        const int cnt = (int)min((int64_t)TV, N - v0);
+        s_meta[s] = make_int4((int)tile, tb, cnt, 0);
+        const unsigned xb = (unsigned)cnt * (unsigned)sizeof(T), lb = (unsigned)cnt * 8u;
+        mbar_arrive_tx(full_bar(s), C * xb + lb);
+        const unsigned dst = stage0 + (unsigned)s * SB;
+        const T* gx = x + (int64_t)tb * C * N + v0;
+#pragma unroll
+        for (int c = 0; c < C; ++c) bulk_load(dst + c * XB, gx + (int64_t)c * N, xb, full_bar(s));
+        bulk_load(dst + C * XB, lab + (int64_t)tb * N + v0, lb, full_bar(s));
+        issued = i + 1;
+      }
+      // After an abort no copy may still be in flight when the CTA leaves: wait
+      // (bounded) for the last fill of every stage. (Otherwise the consumers
+      // have consumed every fill before the CTA's final barrier.)
+      if (s_abort)
+        for (int i = issued - S > 0 ? issued - S : 0; i < issued; ++i)
+          mbar_wait(full_bar(i % S), (unsigned)(i / S) & 1u);
+    }
+  } else {
+    // ---------------- consumers ----------------
+    // Shared byte address of row c, flag 0, of the interval whose rounding
+    // pattern is t (bits(t) - magic = j): bits(t) * A + base[c] (mod 2^32).
+    const unsigned sb = (unsigned)(R * NW * 4);  // bytes of one slot (all replicas)
+    const unsigned A = 2u * C * sb;               // bytes of one interval
+    unsigned base[C];
+    {
+      const unsigned t0 =
+          smem_addr(hist) + (unsigned)((lane & (R - 1)) * NW * 4) - kFixMagicBits * A;
+#pragma unroll
+      for (int c = 0; c < C; ++c) base[c] = t0 + (unsigned)c * 2u * sb;
+    }
+    const float Kf = (float)K, KfS = (float)K * kFixScale;
+    const int vo = (warp * 32 + lane) * VL;  // this lane's first voxel of a tile
+    int cur_b = -1, since = 0;
+    for (int i = 0;; ++i) {
+      const int s = i % S;
+      if (!mbar_wait(full_bar(s), (unsigned)(i / S) & 1u)) {
+        abort_cta();
+        break;
+      }
+      const int4 m = s_meta[s];
+      if (m.x < 0 || s_abort) break;
+      if (m.y != cur_b || since == P.epoch) {
+        // a new batch, or the 32-bit words' range: fold the table first
+        if (cur_b >= 0) {
+          consumer_sync();
+          fold_soft<C, OFF>(hist, K, R, P.iacc, mstride, (int64_t)(P.b_offset + cur_b) * CL, true);
+          consumer_sync();
+        }
+        cur_b = m.y;
+        since = 0;
+      }
+      ++since;
+      const unsigned st = stage0 + (unsigned)s * SB;
+      float xv[C][4];
+      int lab[4];
+#pragma unroll
+      for (int c = 0; c < C; ++c) lds_logits<T>(st + c * XB + vo * (unsigned)sizeof(T), xv[c]);
+      lds_labels(st + C * XB + vo * 8u, lab);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty_bar(s));  // the stage may be refilled now
+      if (vo >= m.z) continue;                    // past the batch's last voxel
+#pragma unroll
+      for (int v = 0; v < VL; ++v) {
+        // softmax: exp(x - m) = 2^(x log2 e - m log2 e) (ace_softmax_fast)
+        float e[C];
+        float mx = xv[0][v];
+#pragma unroll
+        for (int c = 1; c < C; ++c) mx = fmaxf(mx, xv[c][v]);
+        const float mL = __fmul_rn(mx, kLog2e);
+        float sum = 0.0f;
+#pragma unroll
+        for (int c = 0; c < C; ++c) {
+          e[c] = ace_exp_fast(xv[c][v], mL);
+          sum = __fadd_rn(sum, e[c]);
+        }
+        const float y = ace_rcp_approx(sum);
+#pragma unroll
+        for (int c = OFF; c < C; ++c) {
+          // p in [0, 1] (NaN -> 0); t = magic + j, j = round(p K) in [0, K]
+          const float p = __saturatef(__fmul_rn(e[c], y));
+          const float t = __fmaf_rn(p, Kf, kFixMagic);
+          // rs = (p K - j) 2^21, exact before its one rounding (|rs| <= 2^20)
+          const float rs = __fmaf_rn(p, KfS, __fmaf_rn(t, -kFixScale, kFixMagic * kFixScale));
+          const float hb = __fadd_rn(rs, kFixMagic);                 // magic + round(rs)
+          const float rl = __fsub_rn(rs, __fsub_rn(hb, kFixMagic));  // residual, exact
+          const unsigned lo = __float_as_uint(__fmaf_rn(rl, kFixScale, kFixMagic));
+          const unsigned q =
+              __float_as_uint(__fmaf_rn(rs, __fmul_rn(rs, 1.0f / kFixScale), kFixMagic));
+          unsigned a = __float_as_uint(t) * A + base[c];
+          if (lab[v] == c) a += sb;
+          red_slot(a, 1u, __float_as_uint(hb), lo, q);
+        }
+      }
+    }
+    consumer_sync();
+    if (cur_b >= 0)
+      fold_soft<C, OFF>(hist, K, R, P.iacc, mstride, (int64_t)(P.b_offset + cur_b) * CL, false);
+  }
+
+  ace_launch_dependents();  // a dependent launch may begin its own setup now
+  __syncthreads();
+  if (tid == 0) {
+    // The ticket is a release (this CTA's sums, ordered before it by the
+    // barrier) and an acquire (the other CTAs' sums, for the last CTA).
+    unsigned done;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
+                 : "=r"(done)
+                 : "l"(P.counter)
+                 : "memory");
+    s_last = (done == gridDim.x - 1);
+  }
+  __syncthreads();
+  if (!s_last) return;
+
+  // Last CTA: W, P, G per bin k of each row from the slots of intervals k and
+  // k + 1 (flags 0 and 1; the four slots are consecutive). Interval j in 1..K-1,
+  // between lo = c_{j-1} and lo + S = c_j: with r = p K - j, the reference's
+  // right-bin weight is u = (p - lo) / S = a r + b, a = 1 / (K S),
+  // b = (j / K - lo) / S, so sum u = a R1 + b n and sum u^2 = a^2 R2 + 2 a b R1
+  // + b^2 n. Bin j gets the u share, W += sum u, P += lo sum u + S sum u^2,
+  // G += the flag-1 slot's sum u; bin j - 1 the 1 - u share, W += n - sum u,
+  // P += lo n + S sum u - (lo sum u + S sum u^2), G += the flag-1 n - sum u.
+  // The end intervals (j = 0, K) give all of n, sum p = (R1 + j n) / K and the
+  // flag-1 n to bins 0 and K - 1, as the reference's two scatters.
+  const int rows = P.B_total * CL;
+  const int64_t stat_stride = (int64_t)rows * K;
+  const bool stage = P.do_epilogue && 3 * stat_stride <= (int64_t)table_words;
+  float* staged = reinterpret_cast<float*>(hist);
+  const unsigned long long* acc = P.iacc;
+  const double u21 = 1.0 / (double)kFixScale, u42 = u21 * u21, invK = 1.0 / (double)K;
+  const bool failed = __ldcg(err) != 0u;  // a CTA's wait ran out: the sums are incomplete
+  for (int64_t e = tid; e < stat_stride; e += NT) {
+    const int64_t r = e / K;
+    const int k = (int)(e - r * K);
+    const int64_t s0 = (r * (K + 1) + k) * 2;  // slots (k, 0), (k, 1), (k+1, 0), (k+1, 1)
+    long long mo[4][4];
+#pragma unroll
+    for (int o = 0; o < 4; ++o) {
+      const ulonglong2 a = __ldcg(reinterpret_cast<const ulonglong2*>(acc + o * mstride + s0));
+      const ulonglong2 c = __ldcg(reinterpret_cast<const ulonglong2*>(acc + o * mstride + s0 + 2));
+      mo[o][0] = (long long)a.x;
+      mo[o][1] = (long long)a.y;
+      mo[o][2] = (long long)c.x;
+      mo[o][3] = (long long)c.y;
+    }
+    double w = 0.0, pp = 0.0, gs = 0.0;
+#pragma unroll
+    for (int side = 0; side < 2; ++side) {
+      const int j = k + side;
+      double n[2], r1[2], r2[2];
+#pragma unroll
+      for (int f = 0; f < 2; ++f) {
+        const int q = 2 * side + f;
+        n[f] = (double)mo[0][q];
+        r1[f] = (double)mo[1][q] * u21 + (double)mo[2][q] * u42;
+        r2[f] = (double)mo[3][q] * u21;
+      }
+      if (j == 0 || j == K) {
+        w += n[0] + n[1];
+        pp += (r1[0] + r1[1] + (double)j * (n[0] + n[1])) * invK;
+        gs += n[1];
+        continue;
+      }
+      const double lo = P.tab.lohi[j].x, span = (double)P.tab.lohi[j].y - lo;
+      const double a = invK / span, bb = ((double)j * invK - lo) / span;
+      double su[2], su2 = 0.0;
+#pragma unroll
+      for (int f = 0; f < 2; ++f) {
+        su[f] = a * r1[f] + bb * n[f];
+        su2 += a * a * r2[f] + 2.0 * a * bb * r1[f] + bb * bb * n[f];
+      }
+      const double nt = n[0] + n[1], sut = su[0] + su[1];
+      const double pt = lo * sut + span * su2;  // sum u p
+      if (side == 0) {
+        w += sut;
+        pp += pt;
+        gs += su[1];
+      } else {
+        w += nt - sut;
+        pp += lo * nt + span * sut - pt;
+        gs += n[1] - su[1];
+      }
+    }
+    const float nan = __int_as_float(0x7fc00000);
+    const float wf = failed ? nan : (float)w, pf = failed ? nan : (float)pp;
+    const float gf = failed ? nan : (float)gs;
+    P.hist_out[e] = wf;
+    P.hist_out[stat_stride + e] = pf;
+    P.hist_out[2 * stat_stride + e] = gf;
+    if (stage) {
+      staged[e] = wf;
+      staged[stat_stride + e] = pf;
+      staged[2 * stat_stride + e] = gf;
+    }
+  }
+  __syncthreads();
+  unsigned long long* accw = P.iacc;
+  for (int64_t i = tid; i < 4 * mstride; i += NT) __stcg(accw + i, 0ull);
+  for (int i = tid; i < B; i += NT) P.pool_ctr[i] = 0u;
+  if (stage) {
+    __syncthreads();
+    write_loss_if0(P.epi, epilogue_rows(P.epi, staged, rows, 0, 0, rows));
+  }
+  __syncthreads();
+  if (tid == 0) {
+    *err = 0u;
+    *P.counter = 0u;
+  }
+}
+
+}  // namespace ace

@@ -14,7 +14,7 @@ constexpr int kMaxBins = ACE_B200_MAX_BINS;        // num_bins limit of the kern
 constexpr int kMaxClasses = ACE_B200_MAX_CLASSES;  // channels limit of the kernels
 constexpr int kThreads = 256;                      // threads per CTA (gradient, epilogue)
 constexpr int kHistThreads = 512;                  // threads per CTA of the histogram
-constexpr int kSplitThreads = 640;                 // threads per CTA of the class-split histogram
+constexpr int kMaxDevices = 64;                    // devices a process may drive (per-device state)
 constexpr int kTabCopies = 16;                     // interleaved copies of the bin tables
 constexpr float kFixScale = 2097152.0f;            // 2^21: fixed-point unit of the statistics
 
@@ -79,7 +79,14 @@ struct FwdParams {
   int b_offset;        // first statistics row of this launch
   int B_total;
   double* accum;       // workspace: [NOUT, B_total, CL, slots] sums (self-cleaning)
-  unsigned* counter;   // workspace: finished-CTA counter (self-cleaning)
+  // soft_fwd_kernel only (the same workspace bytes as accum):
+  unsigned long long* iacc;  // [4, B_total, CL, K + 1, 2] integer moments (self-cleaning)
+  unsigned* pool_ctr;  // [B] tile-claim counters, one per batch (self-cleaning)
+  int64_t wt_batch;    // tiles (kSoftTileVoxels voxels) per batch
+  int epoch;           // tiles a CTA adds between two folds (32-bit word range)
+  int stages;          // shared-memory ring stages (<= kSoftMaxStages)
+  int table_bytes;     // shared-memory bytes of the statistics table (128-aligned)
+  unsigned* counter;   // workspace: finished-CTA counter, then an error word (self-cleaning)
   float* hist_out;     // [3, B_total, CL, K] statistics (W, P, G)
   int do_epilogue;
   BinTable tab;
