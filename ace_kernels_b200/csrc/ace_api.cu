@@ -108,7 +108,8 @@ size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 //   [epilogue partial sums: one per epilogue CTA].
 // Counters and accumulators are zero between calls.
 size_t accum_bytes(int64_t b_total, int64_t cl, int K) {
-  return round_up((size_t)8 * b_total * cl * (K + 1) * sizeof(double), 256);
+  const size_t pad = kSoftAccPad > 1 ? kSoftAccPad : 1;
+  return round_up((size_t)8 * pad * b_total * cl * (K + 1) * sizeof(double), 256);
 }
 
 size_t pool_bytes(int64_t b_total) { return round_up((size_t)b_total * sizeof(unsigned), 256); }
@@ -330,9 +331,10 @@ int fill_epi(EpiParams& e, int64_t b_total, int CL, double rows_global,
   return ACE_B200_OK;
 }
 
-// Shared-memory budget of one soft_fwd_kernel CTA (dynamic part; the static
-// barriers and epilogue scratch take well under 1 KB of the 227 KB).
-constexpr size_t kSoftSmemBudget = 225 * 1024;
+// Shared-memory budget of one soft_fwd_kernel CTA (dynamic part; its static
+// barriers, interval constants and epilogue scratch take under 5 KB of the
+// 227 KB).
+constexpr size_t kSoftSmemBudget = 221 * 1024;
 
 cudaError_t launch_hist_any(const FwdParams& p, const Variant& v, dim3 grid, int smem,
                             int dtype, cudaStream_t s, int dev) {
@@ -343,12 +345,12 @@ cudaError_t launch_hist_any(const FwdParams& p, const Variant& v, dim3 grid, int
 
 // soft_fwd_kernel: soft binning, int64 labels, softmax over C <= 4 channels,
 // inputs whose rows are whole 16-byte vectors (the bulk copies move 16-byte
-// multiples). Shared memory: the table [K + 1][C][2][R][5] words (all C channels
+// multiples). Shared memory: the table [K + 1][C][2][R][3] words (all C channels
 // get rows; a dropped background row stays empty), then the ring of stages. R
 // lane replicas (32: a warp's lanes never share a bank), reduced while the table
 // and two stages do not fit; a replica word takes at most 4 * 16 * 32 / R
-// additions per tile and 1023 between folds (2^21-unit values), which bounds the
-// tiles of an epoch. Returns false when the case does not fit (hist_kernel then
+// additions per tile and 1023 between folds (values up to 2^21 units), which
+// bounds the tiles of an epoch. Returns false when the case does not fit (hist_kernel then
 // takes it).
 bool soft_fwd_setup(const ace_b200_inputs* in, const ace_b200_options* opt, const Variant& v,
                     FwdParams& p, const Workspace& w, int dev, bool want_epilogue, int& smem,
@@ -387,9 +389,8 @@ bool soft_fwd_setup(const ace_b200_inputs* in, const ace_b200_options* opt, cons
   p.g.tiles = tiles;
   p.g.tiles_per_chunk = 0;
   p.g.chunks_per_batch = 0;
-  const int64_t stats = 3 * in->b_total * p.g.CL * K;
   const int64_t rows = in->b_total * p.g.CL;
-  p.do_epilogue = want_epilogue && stats * 4 <= (int64_t)table(R) && rows <= 8 * kEpiRowsPerCta;
+  p.do_epilogue = want_epilogue && rows <= 8 * kEpiRowsPerCta;
   grid = dim3((unsigned)ctas, 1u);
   return true;
 }
@@ -440,6 +441,11 @@ int hist_impl(const ace_b200_inputs* in, const ace_b200_options* opt, float* his
   if (v.split) v.split = soft_fwd_setup(in, opt, v, p, w, dev, out != nullptr, soft_smem, soft_grid);
   if (v.split) {
     build_table(K, true, false, p.tab);
+    const double invK = 1.0 / (double)K;
+    for (int j = 1; j < K; ++j) {
+      const double lo = p.tab.lohi[j].x, span = (double)p.tab.lohi[j].y - lo;
+      p.soft_ab[j] = make_double2(invK / span, ((double)j * invK - lo) / span);
+    }
     e = launch_hist_any(p, v, soft_grid, soft_smem, in->x_dtype, s, dev);
     if (e != cudaSuccess) return cuda_fail(e, "soft histogram kernel launch");
     if (out && !p.do_epilogue) {

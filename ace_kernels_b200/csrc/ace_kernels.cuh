@@ -73,80 +73,102 @@ __device__ __forceinline__ int warp_sum_i(int v) {
   return v;
 }
 
-// Rows [r0, r1) of the epilogue; `st` points at [3, R_total, K] statistics
-// (shared or global memory) and row r of it is statistics row r - st_row0.
-// Returns (on every thread) this CTA's sum of f over its rows, in fixed order.
-__device__ __forceinline__ float epilogue_rows(const EpiParams& E, const float* st, int st_rows,
-                                               int st_row0, int r0, int r1) {
-  __shared__ float wsum[32];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+// Epilogue of row r by one warp, from the row's W, P, G held by its lanes (lane
+// l has bins l, l + 32, l + 64, l + 96; entries past K are ignored). Writes d,
+// coef, f and jac of the row and returns f (on every lane).
+__device__ __forceinline__ float epilogue_row(const EpiParams& E, int r, const float (&w)[4],
+                                              const float (&p)[4], const float (&g)[4]) {
+  const int lane = threadIdx.x & 31;
   const int K = E.K;
-  const int64_t RK = (int64_t)st_rows * K;
   const float nan = __int_as_float(0x7fc00000);
-  const float rows = (float)E.rows_global;
-  float mine = 0.0f;
-  for (int r = r0 + warp; r < r1; r += nwarps) {
-    const int64_t base = (int64_t)(r - st_row0) * K;
-    float dk[4], wk[4];
-    bool ne[4];
-    int kne = 0;
-    float err = 0.0f, gsum = 0.0f;
+  float dk[4], wk[4];
+  bool ne[4];
+  int kne = 0;
+  float err = 0.0f, gsum = 0.0f;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int k = lane + 32 * q;
-      dk[q] = 0.0f;
-      wk[q] = 1.0f;
-      ne[q] = false;
-      if (k < K) {
-        const float w = st[base + k];
-        const float pp = st[RK + base + k];
-        const float g = st[2 * RK + base + k];
-        gsum = ACE_FADD(gsum, g);
-        ne[q] = E.soft ? (w >= E.empty_weight) : (w != 0.0f);
-        if (ne[q]) {
-          wk[q] = w;
-          dk[q] = ACE_FSUB(ACE_FDIV(pp, w), ACE_FDIV(g, w));
-          err = ACE_FADD(err, fabsf(dk[q]));
-          ++kne;
-        }
+  for (int q = 0; q < 4; ++q) {
+    const int k = lane + 32 * q;
+    dk[q] = 0.0f;
+    wk[q] = 1.0f;
+    ne[q] = false;
+    if (k < K) {
+      gsum = ACE_FADD(gsum, g[q]);
+      ne[q] = E.soft ? (w[q] >= E.empty_weight) : (w[q] != 0.0f);
+      if (ne[q]) {
+        wk[q] = w[q];
+        dk[q] = ACE_FSUB(ACE_FDIV(p[q], w[q]), ACE_FDIV(g[q], w[q]));
+        err = ACE_FADD(err, fabsf(dk[q]));
+        ++kne;
       }
     }
-    kne = warp_sum_i(kne);
-    err = warp_sum(err);
-    gsum = warp_sum(gsum);
-    const float kf = (float)kne;
-    const int64_t out = (int64_t)r * K;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int k = lane + 32 * q;
-      if (k < K) {
-        const float sg = dk[q] > 0.0f ? 1.0f : (dk[q] < 0.0f ? -1.0f : 0.0f);
-        E.d[out + k] = dk[q];
-        E.coef[out + k] = ne[q] ? ACE_FDIV(sg, ACE_FMUL(kf, wk[q])) : 0.0f;
-      }
-    }
-    float f = kne > 0 ? ACE_FDIV(err, kf) : nan;
-    const float present = gsum > 0.0f ? 1.0f : 0.0f;
-    const float wc = E.class_w[r % E.CL];
-    float scale = wc;
-    if (E.ignore_empty) {
-      f = ACE_FMUL(f, present);  // NaN stays NaN, as the reference
-      scale = ACE_FMUL(present, wc);
-    }
-    f = ACE_FMUL(f, wc);
-    if (E.reduction == ACE_B200_REDUCTION_MEAN) scale = ACE_FDIV(scale, rows);
-    if (lane == 0) {
-      E.f[r] = f;
-      E.jac[r] = scale;
-    }
-    mine = ACE_FADD(mine, f);
   }
+  kne = warp_sum_i(kne);
+  err = warp_sum(err);
+  gsum = warp_sum(gsum);
+  const float kf = (float)kne;
+  const int64_t out = (int64_t)r * K;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int k = lane + 32 * q;
+    if (k < K) {
+      const float sg = dk[q] > 0.0f ? 1.0f : (dk[q] < 0.0f ? -1.0f : 0.0f);
+      E.d[out + k] = dk[q];
+      E.coef[out + k] = ne[q] ? ACE_FDIV(sg, ACE_FMUL(kf, wk[q])) : 0.0f;
+    }
+  }
+  float f = kne > 0 ? ACE_FDIV(err, kf) : nan;
+  const float present = gsum > 0.0f ? 1.0f : 0.0f;
+  const float wc = E.class_w[r % E.CL];
+  float scale = wc;
+  if (E.ignore_empty) {
+    f = ACE_FMUL(f, present);  // NaN stays NaN, as the reference
+    scale = ACE_FMUL(present, wc);
+  }
+  f = ACE_FMUL(f, wc);
+  if (E.reduction == ACE_B200_REDUCTION_MEAN) scale = ACE_FDIV(scale, (float)E.rows_global);
+  if (lane == 0) {
+    E.f[r] = f;
+    E.jac[r] = scale;
+  }
+  return f;
+}
+
+// Sum over the CTA of each warp's `mine` (the sum of f over the rows the warp
+// took), in warp order: a fixed order, so the loss is deterministic. Called by
+// all threads; returns the total on every thread.
+__device__ __forceinline__ float cta_sum_in_warp_order(float mine) {
+  __shared__ float wsum[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   if (lane == 0) wsum[warp] = mine;
   __syncthreads();
   float total = 0.0f;
   for (int w = 0; w < nwarps; ++w) total = ACE_FADD(total, wsum[w]);
   __syncthreads();
   return total;
+}
+
+// Rows [r0, r1) of the epilogue; `st` points at [3, R_total, K] statistics
+// (shared or global memory) and row r of it is statistics row r - st_row0.
+// Returns (on every thread) this CTA's sum of f over its rows, in fixed order.
+__device__ __forceinline__ float epilogue_rows(const EpiParams& E, const float* st, int st_rows,
+                                               int st_row0, int r0, int r1) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const int K = E.K;
+  const int64_t RK = (int64_t)st_rows * K;
+  float mine = 0.0f;
+  for (int r = r0 + warp; r < r1; r += nwarps) {
+    const int64_t base = (int64_t)(r - st_row0) * K;
+    float w[4], p[4], g[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int k = lane + 32 * q;
+      w[q] = k < K ? st[base + k] : 0.0f;
+      p[q] = k < K ? st[RK + base + k] : 0.0f;
+      g[q] = k < K ? st[2 * RK + base + k] : 0.0f;
+    }
+    mine = ACE_FADD(mine, epilogue_row(E, r, w, p, g));
+  }
+  return cta_sum_in_warp_order(mine);
 }
 
 __device__ __forceinline__ void write_loss(const EpiParams& E, float total) {

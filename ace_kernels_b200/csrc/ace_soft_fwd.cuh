@@ -28,13 +28,14 @@
 //   rounded p K can differ from the exact interval only for p within a few ulp of
 //   a centre, where both intervals give the centre's bin the same weight ~1.)
 // - Slots split by class flag: slot (j, channel c, f) with f = 1 when c is the
-//   voxel's class. Every value makes exactly one update of four 32-bit words
-//   (n, sum r in two words, sum r^2), and the target moments of a row are its
-//   flag-1 slots: no second update for the true class.
-// - The words are integer fixed point in shared memory (2^21 units; sum r has a
-//   second word of the residual, 2^-42 units), updated with red.shared.add.u32
-//   (native; a float shared-memory add is a compare-and-swap loop), lane-
-//   replicated R ways so that the 32 lanes of a warp never share a bank.
+//   voxel's class. Every value makes exactly one update of three 32-bit words
+//   (n, sum r, sum r^2), and the target moments of a row are its flag-1 slots:
+//   no second update for the true class.
+// - The words are integer fixed point in shared memory (r in 2^-22 units, r^2 in
+//   2^-23 units: at most 1.2e-7 of rounding per value, against the loss's 1e-5
+//   tolerance), updated with red.shared.add.u32 (native; a float shared-memory
+//   add is a compare-and-swap loop), lane-replicated R ways so that the 32 lanes
+//   of a warp never share a bank.
 // - Folds add the replicas exactly in 64-bit integers and issue 64-bit integer
 //   global atomics: the sums do not depend on the order of anything, so every
 //   run gives the same bits whichever CTA took which tile.
@@ -51,8 +52,16 @@ constexpr int kSoftThreads = (kSoftConsumerWarps + 1) * 32;  // + one producer w
 constexpr int kSoftLaneVoxels = 4;                            // voxels per consumer lane per tile
 constexpr int kSoftTileVoxels = kSoftConsumerWarps * 32 * kSoftLaneVoxels;
 constexpr int kSoftMaxStages = 4;
-constexpr int kSoftNW = 5;  // words per slot replica: n, r hi, r lo, r^2, pad (odd)
+constexpr int kSoftNW = 3;  // words per slot replica: n, r, r^2 (odd: no bank conflicts)
+constexpr int kSoftMoments = 3;
+constexpr float kSoftRScale = 4194304.0f;  // 2^22: unit of sum r (|r| <= 1/2: |r 2^22| <= 2^21)
 constexpr unsigned long long kSoftWaitNs = 1000000000ull;  // bound of every barrier wait (1 s)
+// Stride, in 8-byte words, between consecutive accumulators in the workspace:
+// spreads the folds' 64-bit atomics of all CTAs over more L2 slices.
+#ifndef ACE_SOFT_ACC_PAD
+#define ACE_SOFT_ACC_PAD 1
+#endif
+constexpr int kSoftAccPad = ACE_SOFT_ACC_PAD;
 
 __device__ __forceinline__ unsigned smem_addr(const void* p) {
   return static_cast<unsigned>(__cvta_generic_to_shared(p));
@@ -100,7 +109,7 @@ __device__ __forceinline__ bool mbar_wait(unsigned bar, unsigned parity) {
 __device__ __forceinline__ void bulk_load(unsigned dst, const void* src, unsigned bytes,
                                           unsigned bar) {
   asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
           dst),
       "l"(src), "r"(bytes), "r"(bar)
       : "memory");
@@ -111,15 +120,13 @@ __device__ __forceinline__ void consumer_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(kSoftConsumerWarps * 32) : "memory");
 }
 
-// One value's four words into the slot replica at shared byte address a.
-__device__ __forceinline__ void red_slot(unsigned a, unsigned n, unsigned hi, unsigned lo,
-                                         unsigned q) {
+// One value's three words into the slot replica at shared byte address a.
+__device__ __forceinline__ void red_slot(unsigned a, unsigned n, unsigned r, unsigned q) {
   asm volatile(
       "red.shared.add.u32 [%0], %1;\n\t"
       "red.shared.add.u32 [%0+4], %2;\n\t"
-      "red.shared.add.u32 [%0+8], %3;\n\t"
-      "red.shared.add.u32 [%0+12], %4;" ::"r"(a),
-      "r"(n), "r"(hi), "r"(lo), "r"(q));
+      "red.shared.add.u32 [%0+8], %3;" ::"r"(a),
+      "r"(n), "r"(r), "r"(q));
 }
 
 // A lane's kSoftLaneVoxels logits of one channel from a stage, widened to fp32.
@@ -168,10 +175,11 @@ __device__ __forceinline__ void lds_labels(unsigned a, int (&lab)[4]) {
 // and part i & (G - 1) of its R replicas (G = 4 lanes per slot): it removes each
 // replica's fixed-point bias with the replica's count, adds exactly in 64-bit
 // integers, the G lanes combine their parts with shuffles and the first issues
-// four 64-bit integer atomics (n, sum r high and low words, sum r^2) for a
-// non-empty slot of a loss channel. acc layout: [4][rows][K + 1][2] (moment
-// stride `ms`), rows = b_total * CL; `row0` is the global row of loss channel 0
-// of the batch folded. `clear`: zero the table afterwards.
+// three 64-bit integer atomics (n, sum r, sum r^2) for a non-empty slot of a loss
+// channel. acc layout: [3][rows][K + 1][2] (moment
+// stride `ms`), rows = b_total * CL, each accumulator kSoftAccPad words apart;
+// `row0` is the global row of loss channel 0 of the batch folded. `clear`: zero
+// the table afterwards.
 template <int C, int OFF>
 __device__ __forceinline__ void fold_soft(unsigned* hist, int K, int R, unsigned long long* acc,
                                           int64_t ms, int64_t row0, bool clear) {
@@ -185,34 +193,33 @@ __device__ __forceinline__ void fold_soft(unsigned* hist, int K, int R, unsigned
     const bool valid = i < total;
     const int e = valid ? i >> gsh : 0, part = i & (G - 1);
     const unsigned* base = hist + e * R * NW;
-    long long hi = 0, lo = 0, q = 0;
+    long long sr = 0, q = 0;
     unsigned n = 0;
     if (valid) {
+#pragma unroll 8
       for (int k = 0; k < per; ++k) {
         const unsigned* w = base + ((part * per + k + e) & (R - 1)) * NW;
         const unsigned cnt = w[0];
         const unsigned bias = cnt * kFixMagicBits;
         n += cnt;
-        hi += (int)(w[1] - bias);
-        lo += (int)(w[2] - bias);
-        q += (int)(w[3] - bias);
+        sr += (int)(w[1] - bias);
+        q += (int)(w[2] - bias);
       }
     }
     for (int o = 1; o < G; o <<= 1) {
       n += __shfl_xor_sync(0xffffffffu, n, o);
-      hi += __shfl_xor_sync(0xffffffffu, hi, o);
-      lo += __shfl_xor_sync(0xffffffffu, lo, o);
+      sr += __shfl_xor_sync(0xffffffffu, sr, o);
       q += __shfl_xor_sync(0xffffffffu, q, o);
     }
     if (valid && part == 0 && n != 0) {
       const int f = e & 1, jc = e >> 1;
       const int j = jc / C, c = jc - j * C;
       if (c >= OFF) {
-        unsigned long long* a = acc + ((row0 + c - OFF) * (K + 1) + j) * 2 + f;
+        unsigned long long* a = acc + (((row0 + c - OFF) * (K + 1) + j) * 2 + f) * kSoftAccPad;
+        const int64_t m = ms * kSoftAccPad;
         atomicAdd(a, (unsigned long long)n);
-        atomicAdd(a + ms, (unsigned long long)hi);
-        atomicAdd(a + 2 * ms, (unsigned long long)lo);
-        atomicAdd(a + 3 * ms, (unsigned long long)q);
+        atomicAdd(a + m, (unsigned long long)sr);
+        atomicAdd(a + 2 * m, (unsigned long long)q);
       }
     }
   }
@@ -237,6 +244,10 @@ __global__ void __launch_bounds__(kSoftThreads, 1) soft_fwd_kernel(const __grid_
   __shared__ int4 s_meta[kSoftMaxStages];  // {tile, batch, voxels, 0}; tile < 0: no more tiles
   __shared__ volatile int s_abort;
   __shared__ bool s_last;
+  // per interval j: {lo, span, a, b} of the last CTA's reconstruction, staged
+  // once here (indexing the parameters by a lane's own j would serialise the
+  // lanes of a warp on the constant bank)
+  __shared__ double4 s_iv[kMaxBins + 1];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   constexpr int CL = C - OFF;
   const int K = P.tab.K, R = P.R, S = P.stages;
@@ -251,6 +262,10 @@ __global__ void __launch_bounds__(kSoftThreads, 1) soft_fwd_kernel(const __grid_
     for (int i = tid; i < table_words / 4; i += NT) h4[i] = make_uint4(0u, 0u, 0u, 0u);
     for (int i = (table_words & ~3) + tid; i < table_words; i += NT) hist[i] = 0u;
   }
+  for (int j = warp; j <= K; j += NT / 32)
+    if (lane == 0)
+      s_iv[j] = make_double4(P.tab.lohi[j].x, (double)P.tab.lohi[j].y - (double)P.tab.lohi[j].x,
+                             P.soft_ab[j].x, P.soft_ab[j].y);
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(full_bar(s), 1u);
@@ -347,7 +362,7 @@ __global__ void __launch_bounds__(kSoftThreads, 1) soft_fwd_kernel(const __grid_
 #pragma unroll
       for (int c = 0; c < C; ++c) base[c] = t0 + (unsigned)c * 2u * sb;
     }
-    const float Kf = (float)K, KfS = (float)K * kFixScale;
+    const float Kf = (float)K, KfS = (float)K * kSoftRScale;
     const int vo = (warp * 32 + lane) * VL;  // this lane's first voxel of a tile
     int cur_b = -1, since = 0;
     for (int i = 0;; ++i) {
@@ -398,16 +413,15 @@ __global__ void __launch_bounds__(kSoftThreads, 1) soft_fwd_kernel(const __grid_
           // p in [0, 1] (NaN -> 0); t = magic + j, j = round(p K) in [0, K]
           const float p = __saturatef(__fmul_rn(e[c], y));
           const float t = __fmaf_rn(p, Kf, kFixMagic);
-          // rs = (p K - j) 2^21, exact before its one rounding (|rs| <= 2^20)
-          const float rs = __fmaf_rn(p, KfS, __fmaf_rn(t, -kFixScale, kFixMagic * kFixScale));
-          const float hb = __fadd_rn(rs, kFixMagic);                 // magic + round(rs)
-          const float rl = __fsub_rn(rs, __fsub_rn(hb, kFixMagic));  // residual, exact
-          const unsigned lo = __float_as_uint(__fmaf_rn(rl, kFixScale, kFixMagic));
+          // rs = (p K - j) 2^22, exact before its one rounding (|rs| <= 2^21)
+          const float rs = __fmaf_rn(p, KfS, __fmaf_rn(t, -kSoftRScale, kFixMagic * kSoftRScale));
+          // magic + round(rs); magic + round(r^2 2^23) = magic + round(rs^2 2^-21)
+          const unsigned rw = __float_as_uint(__fadd_rn(rs, kFixMagic));
           const unsigned q =
               __float_as_uint(__fmaf_rn(rs, __fmul_rn(rs, 1.0f / kFixScale), kFixMagic));
           unsigned a = __float_as_uint(t) * A + base[c];
           if (lab[v] == c) a += sb;
-          red_slot(a, 1u, __float_as_uint(hb), lo, q);
+          red_slot(a, 1u, rw, q);
         }
       }
     }
@@ -431,95 +445,96 @@ __global__ void __launch_bounds__(kSoftThreads, 1) soft_fwd_kernel(const __grid_
   __syncthreads();
   if (!s_last) return;
 
-  // Last CTA: W, P, G per bin k of each row from the slots of intervals k and
-  // k + 1 (flags 0 and 1; the four slots are consecutive). Interval j in 1..K-1,
-  // between lo = c_{j-1} and lo + S = c_j: with r = p K - j, the reference's
-  // right-bin weight is u = (p - lo) / S = a r + b, a = 1 / (K S),
-  // b = (j / K - lo) / S, so sum u = a R1 + b n and sum u^2 = a^2 R2 + 2 a b R1
-  // + b^2 n. Bin j gets the u share, W += sum u, P += lo sum u + S sum u^2,
-  // G += the flag-1 slot's sum u; bin j - 1 the 1 - u share, W += n - sum u,
-  // P += lo n + S sum u - (lo sum u + S sum u^2), G += the flag-1 n - sum u.
-  // The end intervals (j = 0, K) give all of n, sum p = (R1 + j n) / K and the
-  // flag-1 n to bins 0 and K - 1, as the reference's two scatters.
+  // Last CTA, one warp per row r: lane l takes bins k = l + 32 q. W, P, G of bin k
+  // come from the slots of intervals k and k + 1 (flags 0 and 1). Interval j in
+  // 1..K-1, between lo = c_{j-1} and lo + S = c_j: with r = p K - j, the
+  // reference's right-bin weight is u = (p - lo) / S = a r + b, a = 1 / (K S),
+  // b = (j / K - lo) / S (P.soft_ab, from the host), so sum u = a R1 + b n and
+  // sum u^2 = a^2 R2 + 2 a b R1 + b^2 n. Bin j gets the u share, W += sum u,
+  // P += lo sum u + S sum u^2, G += the flag-1 slot's sum u; bin j - 1 the 1 - u
+  // share, W += n - sum u, P += lo n + S sum u - (lo sum u + S sum u^2), G += the
+  // flag-1 n - sum u. The end intervals (j = 0, K) give all of n,
+  // sum p = (R1 + j n) / K and the flag-1 n to bins 0 and K - 1, as the
+  // reference's two scatters. The warp then zeroes the row's accumulators and,
+  // when the epilogue is fused, runs the row's epilogue from registers.
   const int rows = P.B_total * CL;
   const int64_t stat_stride = (int64_t)rows * K;
-  const bool stage = P.do_epilogue && 3 * stat_stride <= (int64_t)table_words;
-  float* staged = reinterpret_cast<float*>(hist);
-  const unsigned long long* acc = P.iacc;
-  const double u21 = 1.0 / (double)kFixScale, u42 = u21 * u21, invK = 1.0 / (double)K;
+  const int64_t m = mstride * kSoftAccPad;
+  unsigned long long* acc = P.iacc;
+  const double ur = 1.0 / (double)kSoftRScale, uq = ur * 0.5, invK = 1.0 / (double)K;
   const bool failed = __ldcg(err) != 0u;  // a CTA's wait ran out: the sums are incomplete
-  for (int64_t e = tid; e < stat_stride; e += NT) {
-    const int64_t r = e / K;
-    const int k = (int)(e - r * K);
-    const int64_t s0 = (r * (K + 1) + k) * 2;  // slots (k, 0), (k, 1), (k+1, 0), (k+1, 1)
-    long long mo[4][4];
+  const float nan = __int_as_float(0x7fc00000);
+  float mine = 0.0f;
+  for (int r = warp; r < rows; r += NT / 32) {
+    float wv[4], pv[4], gv[4];
+    const int64_t row_slot = (int64_t)r * (K + 1) * 2;
 #pragma unroll
-    for (int o = 0; o < 4; ++o) {
-      const ulonglong2 a = __ldcg(reinterpret_cast<const ulonglong2*>(acc + o * mstride + s0));
-      const ulonglong2 c = __ldcg(reinterpret_cast<const ulonglong2*>(acc + o * mstride + s0 + 2));
-      mo[o][0] = (long long)a.x;
-      mo[o][1] = (long long)a.y;
-      mo[o][2] = (long long)c.x;
-      mo[o][3] = (long long)c.y;
+    for (int qq = 0; qq < 4; ++qq) {
+      const int k = lane + 32 * qq;
+      wv[qq] = pv[qq] = gv[qq] = 0.0f;
+      if (k >= K) continue;
+      long long mo[kSoftMoments][4];  // [moment][slot (k,0), (k,1), (k+1,0), (k+1,1)]
+#pragma unroll
+      for (int o = 0; o < kSoftMoments; ++o)
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          mo[o][q] = (long long)__ldcg(acc + o * m + (row_slot + 2 * k + q) * kSoftAccPad);
+      double w = 0.0, pp = 0.0, gs = 0.0;
+#pragma unroll
+      for (int side = 0; side < 2; ++side) {
+        const int j = k + side;
+        double n[2], r1[2], r2[2];
+#pragma unroll
+        for (int f = 0; f < 2; ++f) {
+          const int q = 2 * side + f;
+          n[f] = (double)mo[0][q];
+          r1[f] = (double)mo[1][q] * ur;
+          r2[f] = (double)mo[2][q] * uq;
+        }
+        if (j == 0 || j == K) {
+          w += n[0] + n[1];
+          pp += (r1[0] + r1[1] + (double)j * (n[0] + n[1])) * invK;
+          gs += n[1];
+          continue;
+        }
+        const double4 iv = s_iv[j];
+        const double lo = iv.x, span = iv.y, a = iv.z, bb = iv.w;
+        double su[2], su2 = 0.0;
+#pragma unroll
+        for (int f = 0; f < 2; ++f) {
+          su[f] = a * r1[f] + bb * n[f];
+          su2 += a * a * r2[f] + 2.0 * a * bb * r1[f] + bb * bb * n[f];
+        }
+        const double nt = n[0] + n[1], sut = su[0] + su[1];
+        const double pt = lo * sut + span * su2;  // sum u p
+        if (side == 0) {
+          w += sut;
+          pp += pt;
+          gs += su[1];
+        } else {
+          w += nt - sut;
+          pp += lo * nt + span * sut - pt;
+          gs += n[1] - su[1];
+        }
+      }
+      wv[qq] = failed ? nan : (float)w;
+      pv[qq] = failed ? nan : (float)pp;
+      gv[qq] = failed ? nan : (float)gs;
+      const int64_t e = (int64_t)r * K + k;
+      P.hist_out[e] = wv[qq];
+      P.hist_out[stat_stride + e] = pv[qq];
+      P.hist_out[2 * stat_stride + e] = gv[qq];
     }
-    double w = 0.0, pp = 0.0, gs = 0.0;
+    __syncwarp();  // every lane has read the row's slots
+    for (int j = lane; j <= K; j += 32)
 #pragma unroll
-    for (int side = 0; side < 2; ++side) {
-      const int j = k + side;
-      double n[2], r1[2], r2[2];
+      for (int o = 0; o < kSoftMoments; ++o)
 #pragma unroll
-      for (int f = 0; f < 2; ++f) {
-        const int q = 2 * side + f;
-        n[f] = (double)mo[0][q];
-        r1[f] = (double)mo[1][q] * u21 + (double)mo[2][q] * u42;
-        r2[f] = (double)mo[3][q] * u21;
-      }
-      if (j == 0 || j == K) {
-        w += n[0] + n[1];
-        pp += (r1[0] + r1[1] + (double)j * (n[0] + n[1])) * invK;
-        gs += n[1];
-        continue;
-      }
-      const double lo = P.tab.lohi[j].x, span = (double)P.tab.lohi[j].y - lo;
-      const double a = invK / span, bb = ((double)j * invK - lo) / span;
-      double su[2], su2 = 0.0;
-#pragma unroll
-      for (int f = 0; f < 2; ++f) {
-        su[f] = a * r1[f] + bb * n[f];
-        su2 += a * a * r2[f] + 2.0 * a * bb * r1[f] + bb * bb * n[f];
-      }
-      const double nt = n[0] + n[1], sut = su[0] + su[1];
-      const double pt = lo * sut + span * su2;  // sum u p
-      if (side == 0) {
-        w += sut;
-        pp += pt;
-        gs += su[1];
-      } else {
-        w += nt - sut;
-        pp += lo * nt + span * sut - pt;
-        gs += n[1] - su[1];
-      }
-    }
-    const float nan = __int_as_float(0x7fc00000);
-    const float wf = failed ? nan : (float)w, pf = failed ? nan : (float)pp;
-    const float gf = failed ? nan : (float)gs;
-    P.hist_out[e] = wf;
-    P.hist_out[stat_stride + e] = pf;
-    P.hist_out[2 * stat_stride + e] = gf;
-    if (stage) {
-      staged[e] = wf;
-      staged[stat_stride + e] = pf;
-      staged[2 * stat_stride + e] = gf;
-    }
+        for (int f = 0; f < 2; ++f) __stcg(acc + o * m + (row_slot + 2 * j + f) * kSoftAccPad, 0ull);
+    if (P.do_epilogue) mine = ACE_FADD(mine, epilogue_row(P.epi, r, wv, pv, gv));
   }
-  __syncthreads();
-  unsigned long long* accw = P.iacc;
-  for (int64_t i = tid; i < 4 * mstride; i += NT) __stcg(accw + i, 0ull);
   for (int i = tid; i < B; i += NT) P.pool_ctr[i] = 0u;
-  if (stage) {
-    __syncthreads();
-    write_loss_if0(P.epi, epilogue_rows(P.epi, staged, rows, 0, 0, rows));
-  }
+  if (P.do_epilogue) write_loss_if0(P.epi, cta_sum_in_warp_order(mine));
   __syncthreads();
   if (tid == 0) {
     *err = 0u;

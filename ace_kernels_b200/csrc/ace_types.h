@@ -86,6 +86,7 @@ struct FwdParams {
   int epoch;           // tiles a CTA adds between two folds (32-bit word range)
   int stages;          // shared-memory ring stages (<= kSoftMaxStages)
   int table_bytes;     // shared-memory bytes of the statistics table (128-aligned)
+  double2 soft_ab[kMaxBins + 1];  // interval j: u = a r + b (see soft_fwd_kernel)
   unsigned* counter;   // workspace: finished-CTA counter, then an error word (self-cleaning)
   float* hist_out;     // [3, B_total, CL, K] statistics (W, P, G)
   int do_epilogue;
