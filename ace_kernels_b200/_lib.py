@@ -64,6 +64,21 @@ class Inputs(Structure):
     ]
 
 
+KERNEL_HIST, KERNEL_SOFT_PIPE, KERNEL_GRAD, KERNEL_GRAD_PIPE = 0, 1, 2, 3
+
+
+class Plan(Structure):
+    _fields_ = [
+        ("kernel", c_int32),
+        ("ctas", c_int32),
+        ("crosses_batches", c_int32),
+        ("stages", c_int32),
+        ("replicas", c_int32),
+        ("fused_epilogue", c_int32),
+        ("tiles_per_batch", c_int64),
+    ]
+
+
 class EpilogueOut(Structure):
     _fields_ = [
         ("coef", c_void_p),
@@ -121,6 +136,7 @@ SIGNATURES: list[tuple[str, object, list[object]]] = [
         [POINTER(c_float), c_int64, c_int32, c_int32, c_int32, POINTER(c_int32)],
     ),
     ("ace_b200_last_error", c_char_p, []),
+    ("ace_b200_last_plan", c_int, [POINTER(Plan)]),
     ("ace_b200_version", c_char_p, []),
 ]
 
@@ -147,6 +163,14 @@ def load() -> ctypes.CDLL:
                 fn.argtypes = argtypes
             _lib = lib
     return _lib
+
+
+def last_plan() -> Plan:
+    """How the last forward / statistics / backward call on this thread was
+    launched (``ace_b200_last_plan``)."""
+    plan = Plan()
+    check(load().ace_b200_last_plan(ctypes.byref(plan)), "ace_b200_last_plan")
+    return plan
 
 
 def check(rc: int, what: str) -> None:

@@ -30,6 +30,18 @@ ACE_EXTERN(__half)
 namespace {
 
 thread_local char g_err[512] = "";
+thread_local ace_b200_plan g_plan = {-1, 0, 0, 0, 0, 0, 0};
+
+void set_plan(int kernel, int64_t ctas, bool crosses, int stages, int replicas, bool fused,
+              int64_t tiles_per_batch) {
+  g_plan.kernel = kernel;
+  g_plan.ctas = (int32_t)ctas;
+  g_plan.crosses_batches = crosses ? 1 : 0;
+  g_plan.stages = stages;
+  g_plan.replicas = replicas;
+  g_plan.fused_epilogue = fused ? 1 : 0;
+  g_plan.tiles_per_batch = tiles_per_batch;
+}
 
 int fail(int code, const char* fmt, ...) {
   va_list ap;
@@ -101,15 +113,14 @@ size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 // Workspace layout, each part 256-byte aligned:
 //   [accumulators: 8 * b_total * cl * (K + 1) 8-byte words: hist_kernel's
-//    [6, rows, K + 1] fp64 sums, or soft_fwd_kernel's [4, rows, K + 1, 2]
+//    [6, rows, K + 1] fp64 sums, or soft_fwd_kernel's [3, rows, K + 1, 2]
 //    64-bit integer moments]
 //   [histogram counter][epilogue counter]
 //   [tile-pool counters: one per batch]
 //   [epilogue partial sums: one per epilogue CTA].
 // Counters and accumulators are zero between calls.
 size_t accum_bytes(int64_t b_total, int64_t cl, int K) {
-  const size_t pad = kSoftAccPad > 1 ? kSoftAccPad : 1;
-  return round_up((size_t)8 * pad * b_total * cl * (K + 1) * sizeof(double), 256);
+  return round_up((size_t)8 * b_total * cl * (K + 1) * sizeof(double), 256);
 }
 
 size_t pool_bytes(int64_t b_total) { return round_up((size_t)b_total * sizeof(unsigned), 256); }
@@ -358,17 +369,17 @@ bool soft_fwd_setup(const ace_b200_inputs* in, const ace_b200_options* opt, cons
   const int K = opt->num_bins, C = (int)in->C;
   const int es = elem_size(in->x_dtype);
   if (v.V != 16 / es) return false;
-  const size_t stage_bytes = (size_t)kSoftTileVoxels * (C * es + 8);
+  const size_t stage_bytes = (size_t)kPipeTileVoxels * (C * es + 8);
   const size_t replica_bytes = (size_t)(K + 1) * C * 2 * kSoftNW * 4;
   int R = 32;
   auto table = [&](int r) { return round_up(replica_bytes * r, 128); };
   while (R > 4 && table(R) + 2 * stage_bytes > kSoftSmemBudget) R >>= 1;
   if (table(R) + 2 * stage_bytes > kSoftSmemBudget) return false;
   int stages = (int)((kSoftSmemBudget - table(R)) / stage_bytes);
-  if (stages > kSoftMaxStages) stages = kSoftMaxStages;
-  const int adds_per_tile = kSoftLaneVoxels * kSoftConsumerWarps * (32 / R);
+  if (stages > kPipeMaxStages) stages = kPipeMaxStages;
+  const int adds_per_tile = kPipeLaneVoxels * kPipeConsumerWarps * (32 / R);
   smem = (int)(table(R) + stages * stage_bytes);
-  const int64_t tiles = (in->N + kSoftTileVoxels - 1) / kSoftTileVoxels;
+  const int64_t tiles = (in->N + kPipeTileVoxels - 1) / kPipeTileVoxels;
   int64_t ctas = (int64_t)sm_count(dev);  // one CTA per SM
   if (ctas > in->B * tiles) ctas = in->B * tiles;
   if (ctas < 1) ctas = 1;
@@ -441,13 +452,12 @@ int hist_impl(const ace_b200_inputs* in, const ace_b200_options* opt, float* his
   if (v.split) v.split = soft_fwd_setup(in, opt, v, p, w, dev, out != nullptr, soft_smem, soft_grid);
   if (v.split) {
     build_table(K, true, false, p.tab);
-    const double invK = 1.0 / (double)K;
-    for (int j = 1; j < K; ++j) {
-      const double lo = p.tab.lohi[j].x, span = (double)p.tab.lohi[j].y - lo;
-      p.soft_ab[j] = make_double2(invK / span, ((double)j * invK - lo) / span);
-    }
     e = launch_hist_any(p, v, soft_grid, soft_smem, in->x_dtype, s, dev);
     if (e != cudaSuccess) return cuda_fail(e, "soft histogram kernel launch");
+    // CTAs start spread over the batches and move on to others' tiles when theirs
+    // run out, so any launch with more than one batch may cross batches
+    set_plan(ACE_B200_KERNEL_SOFT_PIPE, soft_grid.x, in->B > 1, p.stages, p.R, p.do_epilogue,
+             p.wt_batch);
     if (out && !p.do_epilogue) {
       e = launch_epilogue(hist, p.epi, w.epi_counter, w.epi_partial, s);
       if (e != cudaSuccess) return cuda_fail(e, "epilogue kernel launch");
@@ -493,6 +503,8 @@ int hist_impl(const ace_b200_inputs* in, const ace_b200_options* opt, float* his
   const dim3 grid((unsigned)p.g.chunks, 1u);
   e = launch_hist_any(p, v, grid, smem, in->x_dtype, s, dev);
   if (e != cudaSuccess) return cuda_fail(e, "histogram kernel launch");
+  set_plan(ACE_B200_KERNEL_HIST, p.g.chunks, p.g.chunks_per_batch == 0 && p.g.B > 1, 0, R, fused,
+           p.g.tiles);
   if (out && !fused) {
     e = launch_epilogue(hist, p.epi, w.epi_counter, w.epi_partial, s);
     if (e != cudaSuccess) return cuda_fail(e, "epilogue kernel launch");
@@ -658,9 +670,71 @@ int ace_b200_backward(const ace_b200_inputs* in, const ace_b200_options* opt,
   const int K = opt->num_bins;
   BwdParams p;
   memset(&p, 0, sizeof(p));
-  const Variant v = choose_variant(in, opt, dx, false);
+  Variant v = choose_variant(in, opt, dx, false);
   const bool soft = opt->soft != 0;
-  // Record copies: as many as fit in 96 KB (two CTAs per SM keep their tables).
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  p.x = in->x;
+  p.target = in->target;
+  p.dx = dx;
+  p.act = opt->activation;
+  p.soft = soft;
+  p.b_offset = (int)in->b_offset;
+  p.coef = coef;
+  p.d = d;
+  p.jac = jac;
+  p.grad_out = grad_output;
+  p.grad_per_row = grad_per_row != 0;
+  build_table(K, soft, opt->right != 0, p.tab);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+
+  // grad_tma_kernel: softmax over 2..4 channels, soft binning with labels or hard
+  // binning, rows of whole 16-byte vectors. Shared memory: the records of all
+  // local batches in `copies` interleaved copies (fewer while the records, the
+  // bin table and two stages do not fit), the bin table, then the ring.
+  v.offset = opt->offset;
+  v.split = v.softmax && v.CM <= 4 && (!soft || v.labels) && v.V == 16 / elem_size(in->x_dtype);
+  if (v.split) {
+    const size_t stage_bytes =
+        (size_t)kPipeTileVoxels * (in->C * elem_size(in->x_dtype) + (soft ? 8 : 0));
+    const size_t table_bytes = (size_t)(K + 1) * kTabCopies * sizeof(float2);
+    int copies = soft ? 16 : 32;
+    const int min_copies = soft ? 2 : 4;
+    auto fixed = [&](int c) {
+      return round_up((size_t)(soft ? 8 : 4) * c * in->B * CL * (K + 1) + table_bytes, 128);
+    };
+    while (copies > min_copies && fixed(copies) + 2 * stage_bytes > kSoftSmemBudget) copies /= 2;
+    if (fixed(copies) + 2 * stage_bytes <= kSoftSmemBudget) {
+      int stages = (int)((kSoftSmemBudget - fixed(copies)) / stage_bytes);
+      if (stages > kPipeMaxStages) stages = kPipeMaxStages;
+      const int64_t tiles = (in->N + kPipeTileVoxels - 1) / kPipeTileVoxels;
+      int64_t ctas = sm_count(dev);
+      if (ctas > tiles * in->B) ctas = tiles * in->B;
+      if (ctas < 1) ctas = 1;
+      p.rec_copies = copies;
+      p.stages = stages;
+      p.stage_offset = (int)fixed(copies);
+      p.tiles_per_batch = tiles;
+      p.g.N = in->N;
+      p.g.B = (int)in->B;
+      p.g.C = (int)in->C;
+      p.g.CL = CL;
+      p.g.offset = opt->offset;
+      const int smem = (int)(fixed(copies) + stages * stage_bytes);
+      const dim3 grid((unsigned)ctas, 1u);
+      if (in->x_dtype == ACE_B200_F32) e = launch_grad<float>(p, v, grid, smem, s, dev);
+      else if (in->x_dtype == ACE_B200_BF16) e = launch_grad<__nv_bfloat16>(p, v, grid, smem, s, dev);
+      else e = launch_grad<__half>(p, v, grid, smem, s, dev);
+      if (e != cudaSuccess) return cuda_fail(e, "gradient kernel launch");
+      set_plan(ACE_B200_KERNEL_GRAD_PIPE, ctas, in->B > 1, stages, 0, false, tiles);
+      return ACE_B200_OK;
+    }
+    v.split = false;
+  }
+
+  // grad_kernel. Record copies: as many as fit in 96 KB (two CTAs per SM keep
+  // their tables).
   int copies = soft ? 16 : 32;
   auto grad_smem = [&](int c) {
     return (size_t)(K + 1) * kTabCopies * sizeof(float2) + (size_t)(soft ? 8 : 4) * c * CL * (K + 1);
@@ -674,29 +748,15 @@ int ace_b200_backward(const ace_b200_inputs* in, const ace_b200_options* opt,
   const int smem = (int)(grad_smem(copies) + scratch);
   if (smem > 227 * 1024) return fail(ACE_B200_EUNSUPPORTED, "gradient tables do not fit");
   p.rec_copies = copies;
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   const int occ = occupancy(1, in->x_dtype, v, smem, dev);
-  p.x = in->x;
-  p.target = in->target;
-  p.dx = dx;
   p.g = make_grid(in, CL, opt->offset, v.V, kThreads, occ, dev, false);
-  p.act = opt->activation;
-  p.soft = soft;
-  p.b_offset = (int)in->b_offset;
-  p.coef = coef;
-  p.d = d;
-  p.jac = jac;
-  p.grad_out = grad_output;
-  p.grad_per_row = grad_per_row != 0;
-  build_table(K, soft, opt->right != 0, p.tab);
   const dim3 grid((unsigned)p.g.chunks_per_batch, (unsigned)p.g.B);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (in->x_dtype == ACE_B200_F32) e = launch_grad<float>(p, v, grid, smem, s, dev);
   else if (in->x_dtype == ACE_B200_BF16) e = launch_grad<__nv_bfloat16>(p, v, grid, smem, s, dev);
   else e = launch_grad<__half>(p, v, grid, smem, s, dev);
   if (e != cudaSuccess) return cuda_fail(e, "gradient kernel launch");
+  set_plan(ACE_B200_KERNEL_GRAD, (int64_t)p.g.chunks_per_batch * p.g.B, false, 0, 0, false,
+           p.g.tiles);
   return ACE_B200_OK;
 }
 
@@ -742,6 +802,12 @@ int ace_b200_bin_index_host(const float* p, int64_t n, int32_t num_bins, int32_t
 }
 
 const char* ace_b200_last_error(void) { return g_err; }
+
+int ace_b200_last_plan(ace_b200_plan* out) {
+  if (!out) return fail(ACE_B200_EINVAL, "out is null");
+  *out = g_plan;
+  return ACE_B200_OK;
+}
 
 const char* ace_b200_version(void) { return "ace_b200 0.1.0 (sm_100a)"; }
 

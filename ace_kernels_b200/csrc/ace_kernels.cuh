@@ -757,6 +757,7 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constan
 
 }  // namespace ace
 
+#include "ace_tma.cuh"       // pipeline primitives
 #include "ace_soft_fwd.cuh"  // soft_fwd_kernel (uses the helpers above)
 
 namespace ace {
@@ -1026,6 +1027,12 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const __grid_constant__ 
   }
 }
 
+}  // namespace ace
+
+#include "ace_grad_tma.cuh"  // grad_tma_kernel (uses grad_p above)
+
+namespace ace {
+
 // ---------------------------------------------------------------------------
 // Test hook: the activated probabilities, computed by the same functions as the
 // two kernels above.
@@ -1124,10 +1131,13 @@ template <typename T, int V, int CM, bool SM, bool SOFT, bool LAB>
 ACE_LAUNCHER(HistLauncher, (hist_kernel<T, V, CM, SM, SOFT, LAB>), kHistThreads, FwdParams);
 
 template <typename T, int C, int OFF>
-ACE_LAUNCHER(SoftFwdLauncher, (soft_fwd_kernel<T, C, OFF>), kSoftThreads, FwdParams);
+ACE_LAUNCHER(SoftFwdLauncher, (soft_fwd_kernel<T, C, OFF>), kPipeThreads, FwdParams);
 
 template <typename T, int V, int CM, bool SM, bool SOFT, bool LAB>
 ACE_LAUNCHER(GradLauncher, (grad_kernel<T, V, CM, SM, SOFT, LAB>), kThreads, BwdParams);
+
+template <typename T, int C, int OFF, bool SOFT>
+ACE_LAUNCHER(GradTmaLauncher, (grad_tma_kernel<T, C, OFF, SOFT>), kPipeThreads, BwdParams);
 
 #undef ACE_LAUNCHER
 
@@ -1200,9 +1210,34 @@ cudaError_t launch_hist(const FwdParams& p, const Variant& v, dim3 grid, int sme
   return cudaErrorInvalidValue;
 }
 
+// The pipelined backward: softmax over C = 2..4 channels, soft binning with
+// labels or hard binning, background kept or dropped.
+#define ACE_GRAD_TMA_CASES(F, T, ...)                                                    \
+  do {                                                                                   \
+    if (v.split) {                                                                       \
+      if (v.soft) {                                                                      \
+        if (v.CM == 2 && v.offset == 0) return GradTmaLauncher<T, 2, 0, true>::F(__VA_ARGS__); \
+        if (v.CM == 2 && v.offset == 1) return GradTmaLauncher<T, 2, 1, true>::F(__VA_ARGS__); \
+        if (v.CM == 3 && v.offset == 0) return GradTmaLauncher<T, 3, 0, true>::F(__VA_ARGS__); \
+        if (v.CM == 3 && v.offset == 1) return GradTmaLauncher<T, 3, 1, true>::F(__VA_ARGS__); \
+        if (v.CM == 4 && v.offset == 0) return GradTmaLauncher<T, 4, 0, true>::F(__VA_ARGS__); \
+        if (v.CM == 4 && v.offset == 1) return GradTmaLauncher<T, 4, 1, true>::F(__VA_ARGS__); \
+      } else {                                                                           \
+        if (v.CM == 2 && v.offset == 0) return GradTmaLauncher<T, 2, 0, false>::F(__VA_ARGS__); \
+        if (v.CM == 2 && v.offset == 1) return GradTmaLauncher<T, 2, 1, false>::F(__VA_ARGS__); \
+        if (v.CM == 3 && v.offset == 0) return GradTmaLauncher<T, 3, 0, false>::F(__VA_ARGS__); \
+        if (v.CM == 3 && v.offset == 1) return GradTmaLauncher<T, 3, 1, false>::F(__VA_ARGS__); \
+        if (v.CM == 4 && v.offset == 0) return GradTmaLauncher<T, 4, 0, false>::F(__VA_ARGS__); \
+        if (v.CM == 4 && v.offset == 1) return GradTmaLauncher<T, 4, 1, false>::F(__VA_ARGS__); \
+      }                                                                                  \
+      return cudaErrorInvalidValue;                                                      \
+    }                                                                                    \
+  } while (0)
+
 template <typename T>
 cudaError_t launch_grad(const BwdParams& p, const Variant& v, dim3 grid, int smem,
                         cudaStream_t s, int dev) {
+  ACE_GRAD_TMA_CASES(run, T, p, grid, smem, s, dev);
   ACE_FOR_SOFT_LABELS(ACE_VARIANT_CASES(GradLauncher, run, T, p, grid, smem, s, dev));
   return cudaErrorInvalidValue;
 }
@@ -1217,6 +1252,7 @@ int hist_occupancy(const Variant& v, int smem, int dev) {
 
 template <typename T>
 int grad_occupancy(const Variant& v, int smem, int dev) {
+  if (v.split) return 1;
   ACE_FOR_SOFT_LABELS(ACE_VARIANT_CASES(GradLauncher, occupancy, T, smem, dev));
   return 1;
 }

@@ -8,10 +8,10 @@
 // whose memory side never waits for its arithmetic side:
 //
 // - Warp specialisation and a TMA ring. One producer thread streams tiles of
-//   kSoftTileVoxels voxels (the C logit rows and the labels of one batch) from
+//   kPipeTileVoxels voxels (the C logit rows and the labels of one batch) from
 //   HBM into a ring of shared-memory stages with bulk copies
 //   (cp.async.bulk ... mbarrier::complete_tx), up to `stages` tiles ahead (~80
-//   to 120 KB in flight per SM). kSoftConsumerWarps consumer warps wait on a
+//   to 120 KB in flight per SM). kPipeConsumerWarps consumer warps wait on a
 //   stage's "full" barrier, read their 4 voxels with 16-byte shared loads, release
 //   the stage on its "empty" barrier and add the voxels into the statistics.
 // - Dynamic tile scheduler. The producer claims tiles from a per-batch global
@@ -40,85 +40,16 @@
 //   global atomics: the sums do not depend on the order of anything, so every
 //   run gives the same bits whichever CTA took which tile.
 //
-// Every wait on a barrier is bounded (kSoftWaitNs); a wait that runs out sets
+// Every wait on a barrier is bounded (kPipeWaitNs); a wait that runs out sets
 // the workspace's error word and the CTA leaves its loops (after the copies it
 // issued have landed), and the last CTA then writes a NaN loss.
 #pragma once
 
 namespace ace {
 
-constexpr int kSoftConsumerWarps = 16;
-constexpr int kSoftThreads = (kSoftConsumerWarps + 1) * 32;  // + one producer warp
-constexpr int kSoftLaneVoxels = 4;                            // voxels per consumer lane per tile
-constexpr int kSoftTileVoxels = kSoftConsumerWarps * 32 * kSoftLaneVoxels;
-constexpr int kSoftMaxStages = 4;
 constexpr int kSoftNW = 3;  // words per slot replica: n, r, r^2 (odd: no bank conflicts)
 constexpr int kSoftMoments = 3;
 constexpr float kSoftRScale = 4194304.0f;  // 2^22: unit of sum r (|r| <= 1/2: |r 2^22| <= 2^21)
-constexpr unsigned long long kSoftWaitNs = 1000000000ull;  // bound of every barrier wait (1 s)
-// Stride, in 8-byte words, between consecutive accumulators in the workspace:
-// spreads the folds' 64-bit atomics of all CTAs over more L2 slices.
-#ifndef ACE_SOFT_ACC_PAD
-#define ACE_SOFT_ACC_PAD 1
-#endif
-constexpr int kSoftAccPad = ACE_SOFT_ACC_PAD;
-
-__device__ __forceinline__ unsigned smem_addr(const void* p) {
-  return static_cast<unsigned>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ unsigned long long ace_now_ns() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-// mbarrier and bulk-copy primitives (shared addresses of this CTA).
-__device__ __forceinline__ void mbar_init(unsigned bar, unsigned count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(unsigned bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_tx(unsigned bar, unsigned bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(unsigned bar, unsigned parity) {
-  unsigned ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Waits until the barrier's phase of parity `parity` has completed; false if
-// that takes longer than kSoftWaitNs.
-__device__ __forceinline__ bool mbar_wait(unsigned bar, unsigned parity) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const unsigned long long t0 = ace_now_ns();
-  while (!mbar_try_wait(bar, parity))
-    if (ace_now_ns() - t0 > kSoftWaitNs) return false;
-  return true;
-}
-// Bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) from
-// global memory into this CTA's shared memory, completing on barrier `bar`.
-__device__ __forceinline__ void bulk_load(unsigned dst, const void* src, unsigned bytes,
-                                          unsigned bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          dst),
-      "l"(src), "r"(bytes), "r"(bar)
-      : "memory");
-}
-
-// Barrier of the consumer warps only (the producer runs ahead meanwhile).
-__device__ __forceinline__ void consumer_sync() {
-  asm volatile("bar.sync 1, %0;" ::"n"(kSoftConsumerWarps * 32) : "memory");
-}
 
 // One value's three words into the slot replica at shared byte address a.
 __device__ __forceinline__ void red_slot(unsigned a, unsigned n, unsigned r, unsigned q) {
@@ -129,47 +60,6 @@ __device__ __forceinline__ void red_slot(unsigned a, unsigned n, unsigned r, uns
       "r"(n), "r"(r), "r"(q));
 }
 
-// A lane's kSoftLaneVoxels logits of one channel from a stage, widened to fp32.
-template <typename T>
-__device__ __forceinline__ void lds_logits(unsigned a, float (&x)[4]);
-template <>
-__device__ __forceinline__ void lds_logits<float>(unsigned a, float (&x)[4]) {
-  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(x[0]), "=f"(x[1]), "=f"(x[2]), "=f"(x[3])
-               : "r"(a));
-}
-template <>
-__device__ __forceinline__ void lds_logits<__nv_bfloat16>(unsigned a, float (&x)[4]) {
-  unsigned w0, w1;
-  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(w0), "=r"(w1) : "r"(a));
-  x[0] = __uint_as_float(w0 << 16);
-  x[1] = __uint_as_float(w0 & 0xffff0000u);
-  x[2] = __uint_as_float(w1 << 16);
-  x[3] = __uint_as_float(w1 & 0xffff0000u);
-}
-template <>
-__device__ __forceinline__ void lds_logits<__half>(unsigned a, float (&x)[4]) {
-  unsigned w0, w1;
-  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(w0), "=r"(w1) : "r"(a));
-  const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&w0));
-  const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&w1));
-  x[0] = f0.x;
-  x[1] = f0.y;
-  x[2] = f1.x;
-  x[3] = f1.y;
-}
-
-// The low words of a lane's kSoftLaneVoxels int64 labels from a stage.
-__device__ __forceinline__ void lds_labels(unsigned a, int (&lab)[4]) {
-  unsigned long long l0, l1, l2, l3;
-  asm volatile("ld.shared.v2.u64 {%0, %1}, [%2];" : "=l"(l0), "=l"(l1) : "r"(a));
-  asm volatile("ld.shared.v2.u64 {%0, %1}, [%2];" : "=l"(l2), "=l"(l3) : "r"(a + 16));
-  lab[0] = (int)l0;
-  lab[1] = (int)l1;
-  lab[2] = (int)l2;
-  lab[3] = (int)l3;
-}
-
 // Fold of the table into the workspace, by the consumer threads. Slot
 // e = (j * C + c) * 2 + f of the (K + 1) * C * 2 slots; item i takes slot i >> gsh
 // and part i & (G - 1) of its R replicas (G = 4 lanes per slot): it removes each
@@ -177,13 +67,12 @@ __device__ __forceinline__ void lds_labels(unsigned a, int (&lab)[4]) {
 // integers, the G lanes combine their parts with shuffles and the first issues
 // three 64-bit integer atomics (n, sum r, sum r^2) for a non-empty slot of a loss
 // channel. acc layout: [3][rows][K + 1][2] (moment
-// stride `ms`), rows = b_total * CL, each accumulator kSoftAccPad words apart;
-// `row0` is the global row of loss channel 0 of the batch folded. `clear`: zero
-// the table afterwards.
+// stride `ms`), rows = b_total * CL; `row0` is the global row of loss channel 0
+// of the batch folded. `clear`: zero the table afterwards.
 template <int C, int OFF>
 __device__ __forceinline__ void fold_soft(unsigned* hist, int K, int R, unsigned long long* acc,
                                           int64_t ms, int64_t row0, bool clear) {
-  constexpr int NW = kSoftNW, NCT = kSoftConsumerWarps * 32;
+  constexpr int NW = kSoftNW, NCT = kPipeConsumerWarps * 32;
   const int slots = (K + 1) * C * 2;
   const int gsh = R >= 4 ? 2 : (R == 2 ? 1 : 0);
   const int G = 1 << gsh, per = R >> gsh;
@@ -215,11 +104,10 @@ __device__ __forceinline__ void fold_soft(unsigned* hist, int K, int R, unsigned
       const int f = e & 1, jc = e >> 1;
       const int j = jc / C, c = jc - j * C;
       if (c >= OFF) {
-        unsigned long long* a = acc + (((row0 + c - OFF) * (K + 1) + j) * 2 + f) * kSoftAccPad;
-        const int64_t m = ms * kSoftAccPad;
+        unsigned long long* a = acc + ((row0 + c - OFF) * (K + 1) + j) * 2 + f;
         atomicAdd(a, (unsigned long long)n);
-        atomicAdd(a + m, (unsigned long long)sr);
-        atomicAdd(a + 2 * m, (unsigned long long)q);
+        atomicAdd(a + ms, (unsigned long long)sr);
+        atomicAdd(a + 2 * ms, (unsigned long long)q);
       }
     }
   }
@@ -233,15 +121,15 @@ __device__ __forceinline__ void fold_soft(unsigned* hist, int K, int R, unsigned
 }
 
 template <typename T, int C, int OFF>
-__global__ void __launch_bounds__(kSoftThreads, 1) soft_fwd_kernel(const __grid_constant__ FwdParams P) {
-  constexpr int NCW = kSoftConsumerWarps, NT = kSoftThreads, NW = kSoftNW;
-  constexpr int TV = kSoftTileVoxels, VL = kSoftLaneVoxels;
+__global__ void __launch_bounds__(kPipeThreads, 1) soft_fwd_kernel(const __grid_constant__ FwdParams P) {
+  constexpr int NCW = kPipeConsumerWarps, NT = kPipeThreads, NW = kSoftNW;
+  constexpr int TV = kPipeTileVoxels, VL = kPipeLaneVoxels;
   constexpr unsigned XB = TV * sizeof(T);  // bytes of one logit row of a stage
   constexpr unsigned SB = C * XB + TV * 8;  // bytes of a stage (rows, then labels)
   static_assert(VL == 4, "lds_logits / lds_labels load four voxels");
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  __shared__ __align__(8) unsigned long long s_full[kSoftMaxStages], s_empty[kSoftMaxStages];
-  __shared__ int4 s_meta[kSoftMaxStages];  // {tile, batch, voxels, 0}; tile < 0: no more tiles
+  __shared__ __align__(8) unsigned long long s_full[kPipeMaxStages], s_empty[kPipeMaxStages];
+  __shared__ int4 s_meta[kPipeMaxStages];  // {tile, batch, voxels, 0}; tile < 0: no more tiles
   __shared__ volatile int s_abort;
   __shared__ bool s_last;
   // per interval j: {lo, span, a, b} of the last CTA's reconstruction, staged
@@ -262,10 +150,13 @@ __global__ void __launch_bounds__(kSoftThreads, 1) soft_fwd_kernel(const __grid_
     for (int i = tid; i < table_words / 4; i += NT) h4[i] = make_uint4(0u, 0u, 0u, 0u);
     for (int i = (table_words & ~3) + tid; i < table_words; i += NT) hist[i] = 0u;
   }
-  for (int j = warp; j <= K; j += NT / 32)
-    if (lane == 0)
-      s_iv[j] = make_double4(P.tab.lohi[j].x, (double)P.tab.lohi[j].y - (double)P.tab.lohi[j].x,
-                             P.soft_ab[j].x, P.soft_ab[j].y);
+  for (int j = warp; j <= K; j += NT / 32) {
+    if (lane == 0) {
+      const double lo = P.tab.lohi[j].x, span = (double)P.tab.lohi[j].y - lo;
+      const double invK = 1.0 / (double)K;
+      s_iv[j] = make_double4(lo, span, invK / span, ((double)j * invK - lo) / span);
+    }
+  }
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(full_bar(s), 1u);
@@ -449,7 +340,7 @@ __global__ void __launch_bounds__(kSoftThreads, 1) soft_fwd_kernel(const __grid_
   // come from the slots of intervals k and k + 1 (flags 0 and 1). Interval j in
   // 1..K-1, between lo = c_{j-1} and lo + S = c_j: with r = p K - j, the
   // reference's right-bin weight is u = (p - lo) / S = a r + b, a = 1 / (K S),
-  // b = (j / K - lo) / S (P.soft_ab, from the host), so sum u = a R1 + b n and
+  // b = (j / K - lo) / S (s_iv), so sum u = a R1 + b n and
   // sum u^2 = a^2 R2 + 2 a b R1 + b^2 n. Bin j gets the u share, W += sum u,
   // P += lo sum u + S sum u^2, G += the flag-1 slot's sum u; bin j - 1 the 1 - u
   // share, W += n - sum u, P += lo n + S sum u - (lo sum u + S sum u^2), G += the
@@ -459,7 +350,7 @@ __global__ void __launch_bounds__(kSoftThreads, 1) soft_fwd_kernel(const __grid_
   // when the epilogue is fused, runs the row's epilogue from registers.
   const int rows = P.B_total * CL;
   const int64_t stat_stride = (int64_t)rows * K;
-  const int64_t m = mstride * kSoftAccPad;
+  const int64_t m = mstride;
   unsigned long long* acc = P.iacc;
   const double ur = 1.0 / (double)kSoftRScale, uq = ur * 0.5, invK = 1.0 / (double)K;
   const bool failed = __ldcg(err) != 0u;  // a CTA's wait ran out: the sums are incomplete
@@ -478,7 +369,7 @@ __global__ void __launch_bounds__(kSoftThreads, 1) soft_fwd_kernel(const __grid_
       for (int o = 0; o < kSoftMoments; ++o)
 #pragma unroll
         for (int q = 0; q < 4; ++q)
-          mo[o][q] = (long long)__ldcg(acc + o * m + (row_slot + 2 * k + q) * kSoftAccPad);
+          mo[o][q] = (long long)__ldcg(acc + o * m + row_slot + 2 * k + q);
       double w = 0.0, pp = 0.0, gs = 0.0;
 #pragma unroll
       for (int side = 0; side < 2; ++side) {
@@ -530,7 +421,7 @@ __global__ void __launch_bounds__(kSoftThreads, 1) soft_fwd_kernel(const __grid_
 #pragma unroll
       for (int o = 0; o < kSoftMoments; ++o)
 #pragma unroll
-        for (int f = 0; f < 2; ++f) __stcg(acc + o * m + (row_slot + 2 * j + f) * kSoftAccPad, 0ull);
+        for (int f = 0; f < 2; ++f) __stcg(acc + o * m + row_slot + 2 * j + f, 0ull);
     if (P.do_epilogue) mine = ACE_FADD(mine, epilogue_row(P.epi, r, wv, pv, gv));
   }
   for (int i = tid; i < B; i += NT) P.pool_ctr[i] = 0u;

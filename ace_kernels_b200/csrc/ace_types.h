@@ -80,13 +80,12 @@ struct FwdParams {
   int B_total;
   double* accum;       // workspace: [NOUT, B_total, CL, slots] sums (self-cleaning)
   // soft_fwd_kernel only (the same workspace bytes as accum):
-  unsigned long long* iacc;  // [4, B_total, CL, K + 1, 2] integer moments (self-cleaning)
+  unsigned long long* iacc;  // [3, B_total, CL, K + 1, 2] integer moments (self-cleaning)
   unsigned* pool_ctr;  // [B] tile-claim counters, one per batch (self-cleaning)
   int64_t wt_batch;    // tiles (kSoftTileVoxels voxels) per batch
   int epoch;           // tiles a CTA adds between two folds (32-bit word range)
   int stages;          // shared-memory ring stages (<= kSoftMaxStages)
   int table_bytes;     // shared-memory bytes of the statistics table (128-aligned)
-  double2 soft_ab[kMaxBins + 1];  // interval j: u = a r + b (see soft_fwd_kernel)
   unsigned* counter;   // workspace: finished-CTA counter, then an error word (self-cleaning)
   float* hist_out;     // [3, B_total, CL, K] statistics (W, P, G)
   int do_epilogue;
@@ -108,6 +107,10 @@ struct BwdParams {
   const float* grad_out;  // scalar, or [B_total, CL] when grad_per_row
   int grad_per_row;
   int rec_copies;      // interleaved copies of the per-row records (power of two)
+  // grad_tma_kernel only:
+  int stages;          // shared-memory ring stages (<= kPipeMaxStages)
+  int stage_offset;    // shared-memory byte offset of the ring (128-aligned)
+  int64_t tiles_per_batch;  // tiles of kPipeTileVoxels voxels per batch
   BinTable tab;
 };
 

@@ -219,6 +219,34 @@ int ace_b200_bin_index_host(const float* p, int64_t n, int32_t num_bins, int32_t
 /* Message of the last failed call on this thread ("" if none). */
 const char* ace_b200_last_error(void);
 
+/*
+ * How the last successful forward, statistics or backward call on this thread
+ * was launched (thread-local, like ace_b200_last_error). No counterpart in the
+ * reference, whose launches are Triton's; tests use it to check which kernel and
+ * which work split a case takes.
+ *   kernel          ACE_B200_KERNEL_*
+ *   ctas            CTAs of the launch
+ *   crosses_batches 1 when a CTA may take voxels of more than one batch
+ *   stages          shared-memory ring stages (pipelined kernels), else 0
+ *   replicas        lane replicas of the statistics table (forward), else 0
+ *   tiles_per_batch tiles of one batch (kernel-specific tile size)
+ *   fused_epilogue  1 when the forward's last CTA ran the epilogue
+ */
+#define ACE_B200_KERNEL_HIST 0      /* hist_kernel: generic forward */
+#define ACE_B200_KERNEL_SOFT_PIPE 1 /* soft_fwd_kernel: pipelined soft forward */
+#define ACE_B200_KERNEL_GRAD 2      /* grad_kernel: generic backward */
+#define ACE_B200_KERNEL_GRAD_PIPE 3 /* grad_tma_kernel: pipelined backward */
+typedef struct ace_b200_plan {
+  int32_t kernel;
+  int32_t ctas;
+  int32_t crosses_batches;
+  int32_t stages;
+  int32_t replicas;
+  int32_t fused_epilogue;
+  int64_t tiles_per_batch;
+} ace_b200_plan;
+int ace_b200_last_plan(ace_b200_plan* out);
+
 /* Library version string. */
 const char* ace_b200_version(void);
 

@@ -1,8 +1,9 @@
 """Generate tests/golden/reference_fixtures.pt from the reference implementation.
 
-Imports kapitan05/ace-kernels from a local checkout (``--reference``, default
-``/root/reference``; read-only) with the monai stand-in in ``monai_shim/`` and
-records what its ``impl="reference"`` (the frozen upstream loss) returns:
+Imports kapitan05/ace-kernels from a local checkout (``--reference PATH`` or the
+``ACE_KERNELS_REFERENCE`` environment variable; read-only) with the monai
+stand-in in ``monai_shim/`` and records what its ``impl="reference"`` (the frozen
+upstream loss) returns:
 
 - ``cases``: the reference's 43 named correctness cases (``ace_kernels.cases.CASES``):
   config, input, target, loss and d(loss.sum())/d(input), evaluated here on the
@@ -18,12 +19,16 @@ records what its ``impl="reference"`` (the frozen upstream loss) returns:
 
 Run on purpose only (the fixtures pin the oracle):
 
-    python tests/golden/make_golden.py [--reference PATH]
+    python tests/golden/make_golden.py --reference PATH [--workloads NAME ...]
+
+``--workloads`` recomputes only the named workloads and keeps every other entry
+of the existing file (the 43 cases are then left as they are).
 """
 
 from __future__ import annotations
 
 import argparse
+import os
 import platform
 import sys
 import warnings
@@ -41,6 +46,8 @@ WORKLOAD_NAMES = [
     "c2_as_hard",
     "c4_soft_4x14x96c_f16",
     "c3_hard_32x21x512s_bf16",
+    "c5_hard_8x4x192c",
+    "c5_soft_8x4x192c",
 ]
 GRAD_SAMPLES = 4096
 
@@ -60,7 +67,12 @@ def _import_reference(ref: Path):  # type: ignore[no-untyped-def]
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", type=Path, default=Path("/root/reference"))
+    env = os.environ.get("ACE_KERNELS_REFERENCE")
+    ap.add_argument("--reference", type=Path, default=Path(env) if env else None,
+                    required=env is None,
+                    help="checkout of kapitan05/ace-kernels (or ACE_KERNELS_REFERENCE)")
+    ap.add_argument("--workloads", nargs="*", default=None,
+                    help="recompute only these workloads, keep the rest of the file")
     args = ap.parse_args()
     warnings.filterwarnings("ignore", category=UserWarning)
     torch.set_num_threads(max(1, torch.get_num_threads()))
@@ -70,6 +82,17 @@ def main() -> None:
     ref_golden = torch.load(
         args.reference / "tests" / "golden" / "reference_cases.pt", weights_only=True
     )["cases"]
+
+    if args.workloads is not None:
+        unknown = set(args.workloads) - set(WORKLOAD_NAMES)
+        if unknown:
+            raise SystemExit(f"unknown workloads: {sorted(unknown)}")
+        old = torch.load(OUT, weights_only=True)
+        workloads = dict(old["workloads"])
+        workloads.update(_workloads(args.workloads, ace_loss, hard_stats, soft_stats, prepare))
+        torch.save({"env": old["env"], "cases": old["cases"], "workloads": workloads}, OUT)
+        print(f"updated {OUT}: {sorted(args.workloads)}")
+        return
 
     cases = {}
     worst_loss = worst_grad = 0.0
@@ -97,10 +120,26 @@ def main() -> None:
     print(f"cases: {len(cases)}; vs the reference's golden file: loss {worst_loss:.2e}, "
           f"grad {worst_grad:.2e}")
 
+    workloads = _workloads(WORKLOAD_NAMES, ace_loss, hard_stats, soft_stats, prepare)
+
+    env = {
+        "torch": str(torch.__version__),
+        "python": platform.python_version(),
+        "platform": platform.platform(),
+        "reference_golden_max_loss_diff": worst_loss,
+        "reference_golden_max_grad_diff": worst_grad,
+    }
+    torch.save({"env": env, "cases": cases, "workloads": workloads}, OUT)
+    print(f"wrote {OUT} ({OUT.stat().st_size / 1e6:.2f} MB)")
+
+
+def _workloads(names, ace_loss, hard_stats, soft_stats, prepare):  # type: ignore[no-untyped-def]
+    """Reference loss, W/P/G and gradient checksums of the named workloads."""
     from ace_kernels import ACEConfig as RefConfig
+    from ace_kernels_b200 import workloads as wl
 
     workloads = {}
-    for name in WORKLOAD_NAMES:
+    for name in names:
         base = "c2_soft_2x3x128c" if name == "c2_as_hard" else name
         w = wl.WORKLOADS[base]
         cfg = RefConfig.model_validate(w.config.model_dump())
@@ -130,16 +169,7 @@ def main() -> None:
             "grad_vals": grad[idx].clone(),
         }
         print(f"{name}: loss {loss.item():.6f}")
-
-    env = {
-        "torch": str(torch.__version__),
-        "python": platform.python_version(),
-        "platform": platform.platform(),
-        "reference_golden_max_loss_diff": worst_loss,
-        "reference_golden_max_grad_diff": worst_grad,
-    }
-    torch.save({"env": env, "cases": cases, "workloads": workloads}, OUT)
-    print(f"wrote {OUT} ({OUT.stat().st_size / 1e6:.2f} MB)")
+    return workloads
 
 
 if __name__ == "__main__":

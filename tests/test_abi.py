@@ -131,3 +131,23 @@ def test_errors_are_reported() -> None:
     opts = _lib.Options(num_bins=20)
     rc = lib.ace_b200_forward(None, ctypes.byref(opts), None, _lib.EpilogueOut(), None, 0, None)
     assert rc == _lib.EINVAL
+
+
+def test_last_plan_before_any_launch() -> None:
+    """The launch record is thread-local: a thread that launched nothing reads
+    kernel -1."""
+    import threading
+
+    seen = []
+
+    def probe() -> None:
+        seen.append(_lib.last_plan().kernel)
+
+    t = threading.Thread(target=probe)
+    t.start()
+    t.join()
+    assert seen == [-1]
+    text = HEADER.read_text()
+    consts = dict(re.findall(r"#define (ACE_B200_KERNEL_\w+) (\d+)", text))
+    assert int(consts["ACE_B200_KERNEL_SOFT_PIPE"]) == _lib.KERNEL_SOFT_PIPE
+    assert int(consts["ACE_B200_KERNEL_GRAD_PIPE"]) == _lib.KERNEL_GRAD_PIPE

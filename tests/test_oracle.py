@@ -18,6 +18,10 @@ GOLDEN = golden()
 
 def test_fixtures_cover_all_reference_cases() -> None:
     assert len(GOLDEN["cases"]) == 43
+    # every benchmark configuration of BASELINE (c1-c5; c2 also as hard binning)
+    assert set(GOLDEN["workloads"]) == {
+        "c1_hard_2x3x64c", "c2_soft_2x3x128c", "c2_as_hard", "c3_hard_32x21x512s_bf16",
+        "c4_soft_4x14x96c_f16", "c5_hard_8x4x192c", "c5_soft_8x4x192c"}
     # the reference reproduced its own golden file when the fixtures were made
     assert GOLDEN["env"]["reference_golden_max_loss_diff"] < 1e-6
     assert GOLDEN["env"]["reference_golden_max_grad_diff"] < 1e-7
@@ -46,7 +50,8 @@ def test_oracle_matches_reference_workload(name: str) -> None:
     assert flat.double().square().sum().item() == pytest.approx(rec["grad_sq_sum"], rel=1e-6)
 
 
-@pytest.mark.parametrize("name", ["c1_hard_2x3x64c", "c2_soft_2x3x128c", "c2_as_hard"])
+@pytest.mark.parametrize("name", ["c1_hard_2x3x64c", "c2_soft_2x3x128c", "c2_as_hard",
+                                  "c5_hard_8x4x192c", "c5_soft_8x4x192c"])
 def test_oracle_stats_match_reference_binning(name: str) -> None:
     """W/P/G of the oracle (fp32 bins, float64 sums) vs the reference's
     binning.hard_stats / soft_stats (fp32 sums): hard counts bit-exact."""
@@ -58,14 +63,16 @@ def test_oracle_stats_match_reference_binning(name: str) -> None:
     # fp32 sums in the reference's order: bit-identical statistics
     W, P, G = oracle.bin_stats(p, t, cfg, dtype=torch.float32)
     assert torch.equal(W, rec["W"]) and torch.equal(G, rec["G"]) and torch.equal(P, rec["P"])
-    # float64 sums (the accuracy truth): the reference's sequential fp32 sums of
-    # ~3e5 values per bin are up to 1.4e-4 relative away from it (measured, c2
-    # soft P); hard counts stay exact
+    # float64 sums (the accuracy truth): the reference's sequential fp32 sums are
+    # measurably away from it, more so for longer slices (measured: 1.4e-4
+    # relative for c2's 2.1e6 voxels per slice; for c5's 7.1e6, 5.3e-4 hard and
+    # 3.3e-3 soft); hard counts stay exact
     W, P, G = oracle.bin_stats(p, t, cfg)
     if cfg.binning == "hard":
         assert torch.equal(W.float(), rec["W"]) and torch.equal(G.float(), rec["G"])
+    rtol = 5e-3 if x[0, 0].numel() > 4_000_000 else 3e-4
     for a, b in ((W, rec["W"]), (P, rec["P"]), (G, rec["G"])):
-        torch.testing.assert_close(a.float(), b, rtol=3e-4, atol=1e-3)
+        torch.testing.assert_close(a.float(), b, rtol=rtol, atol=1e-3)
 
 
 def test_linspace_tables_are_the_reference_tables() -> None:
