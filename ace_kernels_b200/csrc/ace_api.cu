@@ -701,8 +701,9 @@ int ace_b200_backward(const ace_b200_inputs* in, const ace_b200_options* opt,
     const size_t table_bytes = (size_t)(K + 1) * kTabCopies * sizeof(float2);
     int copies = soft ? 16 : 32;
     const int min_copies = soft ? 2 : 4;
+    // records: soft {F - D y, 2 D} for both class flags (16 bytes), hard g coef (4)
     auto fixed = [&](int c) {
-      return round_up((size_t)(soft ? 8 : 4) * c * in->B * CL * (K + 1) + table_bytes, 128);
+      return round_up((size_t)(soft ? 16 : 4) * c * in->B * CL * (K + 1) + table_bytes, 128);
     };
     while (copies > min_copies && fixed(copies) + 2 * stage_bytes > kSoftSmemBudget) copies /= 2;
     if (fixed(copies) + 2 * stage_bytes <= kSoftSmemBudget) {

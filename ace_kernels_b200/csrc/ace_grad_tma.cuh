@@ -6,11 +6,17 @@
 // v2_autograd.py:88-118): per value gp = F + D (2 p - y) from the per-(row,
 // interval) soft records, or g coef[bin] for hard binning, then the softmax
 // backward dx_c = p_c (gp_c - sum_c' p_c' gp_c'), with the forward's activation
-// recomputed (soft: the fast softmax; hard: the exact one, so the bins match the
-// forward's). The memory side is a producer thread streaming tiles (the C logit
+// recomputed. The memory side is a producer thread streaming tiles (the C logit
 // rows, and the labels for soft binning) into a shared-memory ring with bulk
 // copies; kPipeConsumerWarps consumer warps compute and store dx straight from
 // registers with streaming 16-byte stores.
+//
+// Soft binning recomputes exactly the forward's p (the fast softmax, saturated)
+// and takes the forward's interval, the rounded p K; its records are split by
+// class flag, {F - D y, 2 D} for y = 0 and 1, so gp = fma(2 D, p, F - D y) is one
+// FMA, and the fp32 arithmetic runs on voxel pairs (__ffma2_rn / __fmul2_rn /
+// __fadd2_rn). Hard binning recomputes the exact softmax and locates the exact
+// bin with the forward's code, so every value is in the forward's bin.
 //
 // Tile order: the tiles of all batches are taken round-robin by the CTAs
 // (tile k of the sequence by CTA k mod grid), the sequence running from the
@@ -41,10 +47,11 @@ __global__ void __launch_bounds__(kPipeThreads, 1) grad_tma_kernel(const __grid_
   const int K = P.tab.K, S = P.stages, B = P.g.B, copies = P.rec_copies;
   const int64_t N = P.g.N;
   const float Kf = (float)K;
-  // shared memory: records [B][CL][K + 1][copies] (float2 soft, float hard), the
-  // bin table [K + 1][kTabCopies] float2, then the stages (128-aligned)
+  // shared memory: records [B][CL][K + 1][copies] (hard: float) or
+  // [B][CL][K + 1][2][copies] (soft: float2, by class flag), the bin table
+  // [K + 1][kTabCopies] float2, then the stages (128-aligned)
   float* rec = reinterpret_cast<float*>(smem_raw);
-  const int rec_words = (SOFT ? 2 : 1) * B * CL * (K + 1) * copies;
+  const int rec_words = (SOFT ? 4 : 1) * B * CL * (K + 1) * copies;
   float2* lohi_t = reinterpret_cast<float2*>(rec + rec_words);
   const unsigned stage0 = smem_addr(smem_raw) + (unsigned)P.stage_offset;
   auto full_bar = [&](int s) { return smem_addr(&s_full[s]); };
@@ -123,33 +130,39 @@ __global__ void __launch_bounds__(kPipeThreads, 1) grad_tma_kernel(const __grid_
       const float g = P.jac[grow] * (P.grad_per_row ? P.grad_out[grow] : P.grad_out[0]);
       const float* cf = P.coef + grow * K;
       const float* dd = P.d + grow * K;
-      uint4 v;
       if constexpr (!SOFT) {
         const unsigned u = __float_as_uint(j < K ? g * cf[j] : 0.0f);
-        v = make_uint4(u, u, u, u);
+        const uint4 v = make_uint4(u, u, u, u);
+        uint4* dst = reinterpret_cast<uint4*>(rec + e * copies);
+        for (int q = 0; q < copies / 4; ++q) dst[q] = v;
       } else {
+        // {F - D y, 2 D} for y = 0, 1 (records [batch][row][j][flag][copies])
         const int l = max(j - 1, 0), r = min(j, K - 1);
         const float a = g * cf[l], bb = g * cf[r];
-        float2 rv = make_float2(a, 0.0f);
+        double F = a, D = 0.0;
         if (j > 0 && j < K) {
           const float2 mp = s_map[j];
           const double lo = mp.x, inv = (double)mp.y / (double)kFixScale;
-          const double dd_ = ((double)bb - (double)a) * inv;
-          const double e_ = inv * ((double)a * dd[l] - (double)bb * dd[r]);
-          rv = make_float2((float)((double)a - dd_ * lo + e_), (float)dd_);
+          D = ((double)bb - (double)a) * inv;
+          F = (double)a - D * lo + inv * ((double)a * dd[l] - (double)bb * dd[r]);
         }
-        v = make_uint4(__float_as_uint(rv.x), __float_as_uint(rv.y), __float_as_uint(rv.x),
-                       __float_as_uint(rv.y));
+        const unsigned d2 = __float_as_uint(2.0f * (float)D);
+        const unsigned f0 = __float_as_uint((float)F), f1 = __float_as_uint((float)(F - D));
+        const uint4 v0 = make_uint4(f0, d2, f0, d2), v1 = make_uint4(f1, d2, f1, d2);
+        uint4* dst = reinterpret_cast<uint4*>(rec + 4 * e * copies);
+        for (int q = 0; q < copies / 2; ++q) dst[q] = v0;
+        for (int q = copies / 2; q < copies; ++q) dst[q] = v1;
       }
-      uint4* dst = reinterpret_cast<uint4*>(rec + (SOFT ? 2 : 1) * e * copies);
-      for (int q = 0; q < (SOFT ? 2 : 1) * copies / 4; ++q) dst[q] = v;
     }
     consumer_sync();
-    const float* my_rec = rec + (SOFT ? 2 : 1) * (lane & (copies - 1));
     const float2* my_lohi = lohi_t + (lane & (kTabCopies - 1));
     auto entry = [&](int j) -> float2 { return my_lohi[j * kTabCopies]; };
     const int vo = (warp * 32 + lane) * VL;  // this lane's first voxel of a tile
     T* dxp = static_cast<T*>(P.dx);
+    // soft: shared byte address of the record (row rb + c, interval j, flag 0) of
+    // this lane's copy is bits(t) * RS + rbase + c * CS, t = magic + j
+    const unsigned RS = 2u * copies * 8u, CS = (unsigned)(K + 1) * RS;
+    const unsigned rec0 = smem_addr(rec) + (unsigned)((lane & (copies - 1)) * 8) - kFixMagicBits * RS;
     for (int i = 0;; ++i) {
       const int s = i % S;
       if (!mbar_wait(full_bar(s), (unsigned)(i / S) & 1u)) {
@@ -168,37 +181,80 @@ __global__ void __launch_bounds__(kPipeThreads, 1) grad_tma_kernel(const __grid_
       if (lane == 0) mbar_arrive(empty_bar(s));  // the stage may be refilled now
       if (vo >= m.z) continue;                    // past the batch's last voxel
       const int rb = m.y * CL - OFF;              // record row of channel c: rb + c
+      if constexpr (SOFT) {
+        const unsigned rbase = rec0 + (unsigned)rb * CS;
 #pragma unroll
-      for (int v = 0; v < VL; ++v) {
-        float p[C];
+        for (int v = 0; v < VL; v += 2) {
+          // the forward's softmax (soft_fwd_kernel), on the voxel pair v, v + 1
+          float2 xp[C], e[C], p[C];
 #pragma unroll
-        for (int c = 0; c < C; ++c) p[c] = xv[c][v];
-        ace_softmax_sel<SOFT, C>(p, C);
-        int j[C];
-        bool ok = true;
+          for (int c = 0; c < C; ++c) xp[c] = make_float2(xv[c][v], xv[c][v + 1]);
+          float2 mx = xp[0];
 #pragma unroll
-        for (int c = OFF; c < C; ++c) {
-          j[c] = ace_guess(p[c], Kf, K, SOFT);
-          ok &= ace_is_count(p[c], entry(j[c]));
-        }
-        if (!ok) {
+          for (int c = 1; c < C; ++c) mx = make_float2(fmaxf(mx.x, xp[c].x), fmaxf(mx.y, xp[c].y));
+          const float2 nmL = __fmul2_rn(mx, make_float2(-kLog2e, -kLog2e));
+          float2 sum;
 #pragma unroll
-          for (int c = OFF; c < C; ++c)
-            if (!ace_is_count(p[c], entry(j[c])))
-              j[c] = ace_fix_count(p[c], j[c], K, my_lohi, kTabCopies).i;
-        }
-        float gp[C], dot = 0.0f;
-#pragma unroll
-        for (int c = 0; c < C; ++c) {
-          gp[c] = 0.0f;
-          if (c >= OFF) {
-            const float y = (SOFT && lab[v] == c) ? 1.0f : 0.0f;
-            gp[c] = grad_p<SOFT>(my_rec, copies, rb + c, K, j[c], p[c], y);
+          for (int c = 0; c < C; ++c) {
+            const float2 arg = __ffma2_rn(xp[c], make_float2(kLog2e, kLog2e), nmL);
+            e[c] = make_float2(ace_exp2_approx(arg.x), ace_exp2_approx(arg.y));
+            sum = c == 0 ? e[0] : __fadd2_rn(sum, e[c]);
           }
-          dot += p[c] * gp[c];
-        }
+          const float2 y = make_float2(ace_rcp_approx(sum.x), ace_rcp_approx(sum.y));
+          float2 dot = make_float2(0.0f, 0.0f), gp[C];
 #pragma unroll
-        for (int c = 0; c < C; ++c) xv[c][v] = p[c] * (gp[c] - dot);
+          for (int c = 0; c < C; ++c) {
+            p[c] = make_float2(__saturatef(__fmul_rn(e[c].x, y.x)), __saturatef(__fmul_rn(e[c].y, y.y)));
+            gp[c] = make_float2(0.0f, 0.0f);
+            if (c < OFF) continue;
+            const float2 t = __ffma2_rn(p[c], make_float2(Kf, Kf), make_float2(kFixMagic, kFixMagic));
+            unsigned a0 = __float_as_uint(t.x) * RS + rbase + (unsigned)c * CS;
+            unsigned a1 = __float_as_uint(t.y) * RS + rbase + (unsigned)c * CS;
+            if (lab[v] == c) a0 += copies * 8u;
+            if (lab[v + 1] == c) a1 += copies * 8u;
+            float2 r0, r1;
+            asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(r0.x), "=f"(r0.y) : "r"(a0));
+            asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(r1.x), "=f"(r1.y) : "r"(a1));
+            gp[c] = make_float2(__fmaf_rn(r0.y, p[c].x, r0.x), __fmaf_rn(r1.y, p[c].y, r1.x));
+            dot = __ffma2_rn(p[c], gp[c], dot);
+          }
+#pragma unroll
+          for (int c = 0; c < C; ++c) {
+            const float2 dx = __fmul2_rn(p[c], __fadd2_rn(gp[c], make_float2(-dot.x, -dot.y)));
+            xv[c][v] = dx.x;
+            xv[c][v + 1] = dx.y;
+          }
+        }
+      } else {
+        const float* my_rec = rec + (lane & (copies - 1));
+#pragma unroll
+        for (int v = 0; v < VL; ++v) {
+          float p[C];
+#pragma unroll
+          for (int c = 0; c < C; ++c) p[c] = xv[c][v];
+          ace_softmax<C>(p, C);
+          int j[C];
+          bool ok = true;
+#pragma unroll
+          for (int c = OFF; c < C; ++c) {
+            j[c] = ace_guess(p[c], Kf, K, false);
+            ok &= ace_is_count(p[c], entry(j[c]));
+          }
+          if (!ok) {
+#pragma unroll
+            for (int c = OFF; c < C; ++c)
+              if (!ace_is_count(p[c], entry(j[c])))
+                j[c] = ace_fix_count(p[c], j[c], K, my_lohi, kTabCopies).i;
+          }
+          float gp[C], dot = 0.0f;
+#pragma unroll
+          for (int c = 0; c < C; ++c) {
+            gp[c] = c >= OFF ? grad_p<false>(my_rec, copies, rb + c, K, j[c], p[c], 0.0f) : 0.0f;
+            dot += p[c] * gp[c];
+          }
+#pragma unroll
+          for (int c = 0; c < C; ++c) xv[c][v] = p[c] * (gp[c] - dot);
+        }
       }
       const int64_t v0 = (int64_t)m.x * TV + vo;
       T* db = dxp + (int64_t)m.y * C * N + v0;

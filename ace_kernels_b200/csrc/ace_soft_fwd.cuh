@@ -284,35 +284,48 @@ __global__ void __launch_bounds__(kPipeThreads, 1) soft_fwd_kernel(const __grid_
       __syncwarp();
       if (lane == 0) mbar_arrive(empty_bar(s));  // the stage may be refilled now
       if (vo >= m.z) continue;                    // past the batch's last voxel
+      // Two voxels at a time: the fp32 arithmetic runs as packed pairs
+      // (__ffma2_rn / __fmul2_rn / __fadd2_rn, one instruction for both voxels,
+      // each element rounded as its scalar form), the rest per voxel.
 #pragma unroll
-      for (int v = 0; v < VL; ++v) {
+      for (int v = 0; v < VL; v += 2) {
         // softmax: exp(x - m) = 2^(x log2 e - m log2 e) (ace_softmax_fast)
-        float e[C];
-        float mx = xv[0][v];
+        float2 xp[C], e[C];
 #pragma unroll
-        for (int c = 1; c < C; ++c) mx = fmaxf(mx, xv[c][v]);
-        const float mL = __fmul_rn(mx, kLog2e);
-        float sum = 0.0f;
+        for (int c = 0; c < C; ++c) xp[c] = make_float2(xv[c][v], xv[c][v + 1]);
+        float2 mx = xp[0];
+#pragma unroll
+        for (int c = 1; c < C; ++c) mx = make_float2(fmaxf(mx.x, xp[c].x), fmaxf(mx.y, xp[c].y));
+        const float2 nmL = __fmul2_rn(mx, make_float2(-kLog2e, -kLog2e));
+        float2 sum;
 #pragma unroll
         for (int c = 0; c < C; ++c) {
-          e[c] = ace_exp_fast(xv[c][v], mL);
-          sum = __fadd_rn(sum, e[c]);
+          const float2 arg = __ffma2_rn(xp[c], make_float2(kLog2e, kLog2e), nmL);
+          e[c] = make_float2(ace_exp2_approx(arg.x), ace_exp2_approx(arg.y));
+          sum = c == 0 ? e[0] : __fadd2_rn(sum, e[c]);
         }
-        const float y = ace_rcp_approx(sum);
+        const float2 y = make_float2(ace_rcp_approx(sum.x), ace_rcp_approx(sum.y));
 #pragma unroll
         for (int c = OFF; c < C; ++c) {
           // p in [0, 1] (NaN -> 0); t = magic + j, j = round(p K) in [0, K]
-          const float p = __saturatef(__fmul_rn(e[c], y));
-          const float t = __fmaf_rn(p, Kf, kFixMagic);
+          const float2 p = make_float2(__saturatef(__fmul_rn(e[c].x, y.x)),
+                                       __saturatef(__fmul_rn(e[c].y, y.y)));
+          const float2 t = __ffma2_rn(p, make_float2(Kf, Kf), make_float2(kFixMagic, kFixMagic));
           // rs = (p K - j) 2^22, exact before its one rounding (|rs| <= 2^21)
-          const float rs = __fmaf_rn(p, KfS, __fmaf_rn(t, -kSoftRScale, kFixMagic * kSoftRScale));
+          const float2 mj = __ffma2_rn(t, make_float2(-kSoftRScale, -kSoftRScale),
+                                       make_float2(kFixMagic * kSoftRScale, kFixMagic * kSoftRScale));
+          const float2 rs = __ffma2_rn(p, make_float2(KfS, KfS), mj);
           // magic + round(rs); magic + round(r^2 2^23) = magic + round(rs^2 2^-21)
-          const unsigned rw = __float_as_uint(__fadd_rn(rs, kFixMagic));
-          const unsigned q =
-              __float_as_uint(__fmaf_rn(rs, __fmul_rn(rs, 1.0f / kFixScale), kFixMagic));
-          unsigned a = __float_as_uint(t) * A + base[c];
-          if (lab[v] == c) a += sb;
-          red_slot(a, 1u, rw, q);
+          const float2 rw = __fadd2_rn(rs, make_float2(kFixMagic, kFixMagic));
+          const float2 q = __ffma2_rn(
+              rs, __fmul2_rn(rs, make_float2(1.0f / kFixScale, 1.0f / kFixScale)),
+              make_float2(kFixMagic, kFixMagic));
+          unsigned a0 = __float_as_uint(t.x) * A + base[c];
+          unsigned a1 = __float_as_uint(t.y) * A + base[c];
+          if (lab[v] == c) a0 += sb;
+          if (lab[v + 1] == c) a1 += sb;
+          red_slot(a0, 1u, __float_as_uint(rw.x), __float_as_uint(q.x));
+          red_slot(a1, 1u, __float_as_uint(rw.y), __float_as_uint(q.y));
         }
       }
     }
