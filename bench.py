@@ -8,7 +8,9 @@ Workload: 2 x 3 x 128^3 fp32 logits, int64 labels, soft binning, K = 20 (the
 headline configuration), seeded synthetic inputs (``ace_kernels_b200.workloads``).
 With N GPUs every rank holds its own 2 x 3 x 128^3 shard of a 2N-sample batch
 (weak scaling); the per-bin statistics are all-reduced with NCCL before the
-epilogue and the local backward.
+epilogue and the local backward. ``--workload c5_soft_8x4x192c`` (or c5_hard)
+splits one 8-sample batch over the ranks instead (strong scaling, BASELINE's
+sharded configuration).
 
 One step = forward + backward of ``ace_loss(..., impl="b200_cuda")`` through
 ``torch.autograd.grad``, inputs resident in HBM, replayed from a CUDA graph; L2 is
@@ -19,8 +21,13 @@ then be charged to the step). ``value`` =
 voxels of all ranks / (max over ranks of the summed device time of K steps).
 ``e2e`` = the same call per step with the inputs copied from pinned host memory
 and the loss read back, inside the timed region. ``roofline`` = the dominant
-kernel timed alone (algorithmic bytes / CUDA-event time). ``cpu_baseline`` = the
-reference's CPU path (the oracle restatement) on the host cores.
+kernel timed alone (algorithmic bytes / CUDA-event time). ``floors`` = the
+calculator's bandwidth floor (ideal bytes at the measured peak) and launch floor
+(a CUDA graph of as many trivial kernels as the step launches, timed like the
+step). ``cpu_baseline`` = the reference's CPU path (the oracle restatement) on the
+host cores, over the whole workload. With N > 1, ``parity`` compares the sharded
+loss of every rank with rank 0's single-GPU loss over the gathered global batch,
+and ``phases_us`` splits an eager step into its launches.
 """
 
 from __future__ import annotations
@@ -67,19 +74,18 @@ def env_rank() -> tuple[int, int, int]:
 # ---------------------------------------------------------------------------
 # reference arm: the reference's CPU path (oracle restatement), host cores
 # ---------------------------------------------------------------------------
-def cpu_reference(w, cfg, seconds: float, max_steps: int, slab: int = 8) -> dict:  # type: ignore[no-untyped-def]
-    """Times fwd+bwd of the CPU restatement of the reference on a bounded sample
-    of the workload: the first ``slab`` planes of the last spatial axis of every
-    sample (same distributions; the CPU path's cost is linear in voxels)."""
+def cpu_reference(w, cfg, seconds: float, max_steps: int, warmup: int = 1) -> dict:  # type: ignore[no-untyped-def]
+    """Times fwd+bwd of the CPU restatement of the reference over the whole
+    workload: ``warmup`` untimed steps, then at least one and at most
+    ``max_steps`` timed steps, stopping once ``seconds`` have passed."""
     from ace_kernels_b200 import workloads as wl
     from oracle import ace_oracle as oracle
 
     torch.set_num_threads(os.cpu_count() or 1)
     x, y = wl.make(w)
-    x = x[..., :slab].contiguous().float()
-    y = y[..., :slab].contiguous()
-    voxels = x.shape[0] * x[0, 0].numel()
-    oracle.loss_and_grad(x, y, cfg)  # warm-up
+    x = x.float()
+    for _ in range(max(0, warmup)):
+        oracle.loss_and_grad(x, y, cfg)
     times = []
     t_end = time.perf_counter() + seconds
     while len(times) < max_steps and (not times or time.perf_counter() < t_end):
@@ -88,14 +94,15 @@ def cpu_reference(w, cfg, seconds: float, max_steps: int, slab: int = 8) -> dict
         times.append(time.perf_counter() - t0)
     per_step = sum(times) / len(times)
     return {
-        "value": voxels / per_step,
+        "value": w.voxels / per_step,
         "unit": UNIT,
         "cores": torch.get_num_threads(),
         "kind": "port",
-        "sample": (f"{len(times)} fwd+bwd steps of the CPU restatement of the reference "
-                   f"(per-(b,c) bucketize/scatter + autograd, fp32) on {voxels} voxels "
-                   f"({list(x.shape)}: the first {slab} planes of the workload)"),
+        "sample": (f"{len(times)} fwd+bwd steps (after {warmup} untimed) of the CPU restatement "
+                   f"of the reference (per-(b,c) bucketize/scatter + autograd, fp32) on the whole "
+                   f"workload, {list(x.shape)}"),
         "steps": len(times),
+        "warmup": warmup,
         "sec_per_step": per_step,
     }
 
@@ -107,19 +114,26 @@ def run_reference(args: argparse.Namespace) -> None:
     from ace_kernels_b200 import workloads as wl
 
     w = wl.WORKLOADS[args.workload]
-    res = cpu_reference(w, w.config, seconds=120.0, max_steps=max(1, args.steps))
+    res = cpu_reference(w, w.config, seconds=120.0, max_steps=max(1, args.steps),
+                        warmup=max(0, args.warmup))
     line = {
         "metric": METRIC, "value": res["value"], "unit": UNIT, "n_gpus": args.gpus,
-        "steps": res["steps"], "warmup": 1, "ms_per_step": res["sec_per_step"] * 1e3,
+        "steps": res["steps"], "warmup": res["warmup"], "ms_per_step": res["sec_per_step"] * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded generator, BASELINE distributions)",
-        "config": {"workload": args.workload, "sample": res["sample"]},
+        "config": workload_config(w, args.workload),
         "impl": "reference",
         "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def workload_config(w, name: str) -> dict:  # type: ignore[no-untyped-def]
+    """The ``config`` object of the JSON line (the same for both arms)."""
+    return {"workload": name, "shape": list(w.shape), "binning": w.config.binning,
+            "num_bins": w.config.num_bins, "dtype": str(w.dtype).replace("torch.", "")}
 
 
 # ---------------------------------------------------------------------------
@@ -259,8 +273,9 @@ def capture(fn, warmup: int = 3) -> torch.cuda.CUDAGraph:  # type: ignore[no-unt
 
 def run_ours(args: argparse.Namespace) -> None:
     from ace_kernels_b200 import ace_loss
+    from ace_kernels_b200 import calculator as calc
     from ace_kernels_b200 import workloads as wl
-    from ace_kernels_b200.distributed import sharded_ace_loss
+    from ace_kernels_b200.distributed import batch_shard, sharded_ace_loss
     from ace_kernels_b200.loss import kernel_args, run_backward, run_forward
 
     rank, world, local = env_rank()
@@ -272,22 +287,29 @@ def run_ours(args: argparse.Namespace) -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     w = wl.WORKLOADS[args.workload]
     cfg = w.config
-    # inputs resident in HBM: rank r holds samples 2r, 2r+1 of a 2N-sample batch
+    # Weak scaling (default): rank r holds its own copy of the workload's batch,
+    # samples r*B .. r*B+B-1 of an N*B-sample batch. Strong scaling (the c5
+    # workloads): the workload's batch is split over the ranks.
+    strong = args.workload.startswith("c5_") and world > 1
+    if strong:
+        b_offset, b_local = batch_shard(w.batch, rank, world)
+        b_total = w.batch
+        wr = w.with_batch(b_local)
+    else:
+        b_local, b_offset, b_total = w.batch, rank * w.batch, w.batch * world
+        wr = w
     if world == 1:
         x, y = wl.make(w, dev)
     else:
-        x, y = wl.make_on_device(w, dev, seed_offset=rank)
-    b_local = w.batch
-    b_total = b_local * world
-    voxels_rank = w.voxels
-    voxels_all = voxels_rank * world
+        x, y = wl.make_on_device(wr, dev, seed_offset=rank)
+    voxels_all = w.voxels if strong else w.voxels * world
     x.requires_grad_(True)
 
     def step() -> torch.Tensor:
         if world == 1:
             loss = ace_loss(x, y, cfg, impl="b200_cuda")
         else:
-            loss = sharded_ace_loss(x, y, cfg, b_offset=rank * b_local, b_total=b_total)
+            loss = sharded_ace_loss(x, y, cfg, b_offset=b_offset, b_total=b_total)
         (g,) = torch.autograd.grad(loss, x)
         return g
 
@@ -319,20 +341,16 @@ def run_ours(args: argparse.Namespace) -> None:
     with sampler:
         total_ms = time_events(run, flush, args.steps, align)
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-        t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms = float(t.item())
+    total_ms = max_over_ranks(total_ms, world, dev)
     ms_per_step = total_ms / args.steps
     value = voxels_all / (ms_per_step * 1e-3)
 
     # eager (no graph) for information
-    eager_ms = time_events(step, flush, min(args.steps, 100), align) / min(args.steps, 100)
-    if world > 1:
-        t = torch.tensor([eager_ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        eager_ms = float(t.item())
+    reps = min(args.steps, 100)
+    eager_ms = max_over_ranks(time_events(step, flush, reps, align) / reps, world, dev)
+
+    # ---- N > 1: where an eager step's time goes, launch by launch
+    phases = sharded_phases(x, y, cfg, b_offset, b_total, flush, align, world, dev) if world > 1 else None
 
     # ---- e2e through the public call with host buffers
     xh = x.detach().cpu().pin_memory()
@@ -348,7 +366,7 @@ def run_ours(args: argparse.Namespace) -> None:
         if world == 1:
             loss = ace_loss(xd, yd, cfg, impl="b200_cuda")
         else:
-            loss = sharded_ace_loss(xd, yd, cfg, b_offset=rank * b_local, b_total=b_total)
+            loss = sharded_ace_loss(xd, yd, cfg, b_offset=b_offset, b_total=b_total)
         torch.autograd.grad(loss, xd)
         loss_h.copy_(loss.detach(), non_blocking=True)
 
@@ -358,12 +376,11 @@ def run_ours(args: argparse.Namespace) -> None:
     e2e_reps = min(args.steps, 50)
     if world > 1:
         dist.barrier()
-    e2e_ms = time_events(e2e_step, flush, e2e_reps, align) / e2e_reps
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    e2e_ms = max_over_ranks(time_events(e2e_step, flush, e2e_reps, align) / e2e_reps, world, dev)
     h2d = xh.numel() * xh.element_size() + yh.numel() * yh.element_size()
+
+    # ---- N > 1: the sharded loss against a single-GPU loss of the whole batch
+    parity = sharded_parity(x, y, cfg, b_offset, b_total, world, dev) if world > 1 else None
 
     # ---- roofline: each kernel timed alone (graph-replayed, L2 flushed)
     kargs = kernel_args(x.detach(), y, cfg)
@@ -374,8 +391,8 @@ def run_ours(args: argparse.Namespace) -> None:
     reps = min(args.steps, 200)
     hist_ms = time_events(g_hist.replay, flush, reps) / reps
     grad_ms = time_events(g_grad.replay, flush, reps) / reps
-    in_b = w.input_bytes()
-    tgt_b = w.target_bytes()
+    in_b = wr.input_bytes()
+    tgt_b = wr.target_bytes()
     hist_bytes = in_b + tgt_b
     grad_bytes = in_b + in_b + (tgt_b if cfg.binning == "soft" else 0)
     peak, peak_src = measured_peaks()
@@ -385,7 +402,20 @@ def run_ours(args: argparse.Namespace) -> None:
     }
     dom = max(kernels, key=lambda k: kernels[k]["ms"])
     achieved = kernels[dom]["gbs"]
-    step_bytes = w.ideal_bytes()
+    step_bytes = calc.ideal_bytes(in_b, tgt_b, "fwd_bwd")  # per rank
+    # launches per step: ours (forward, backward; N > 1: statistics, epilogue,
+    # backward) and torch's fill of grad_output, plus NCCL's all-reduce at N > 1
+    ours_per_step = 2 if world == 1 else 3
+    graph_kernels = ours_per_step + 1 + (1 if world > 1 else 0)
+    launch_us = calc.measure_launch_us(graph_kernels, lambda: flush_l2(flush))
+    floors = {
+        "bandwidth_floor_us": calc.bandwidth_floor_ms(step_bytes, peak) * 1e3,
+        "launch_floor_us": launch_us,
+        "launch_floor_kernels": graph_kernels,
+        "launch_floor_method": "CUDA graph of that many 1-element kernels, L2 flushed before, events",
+        "reference_launch_floor_us": calc.launch_floor_ms(graph_kernels) * 1e3,
+        "ideal_bytes_per_rank": step_bytes,
+    }
     line = {
         "metric": METRIC,
         "value": value,
@@ -395,22 +425,22 @@ def run_ours(args: argparse.Namespace) -> None:
         "warmup": max(3, args.warmup),
         "ms_per_step": ms_per_step,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if strong else "weak",
         "vs_baseline": None,
-        "dtype": "f32",
-        "data": "synthetic (seeded generator: labels 0.90/0.08/0.02, logits N(0,1.5^2)+2 on the true class)",
-        "config": {
-            "workload": args.workload,
-            "shape_per_rank": list(w.shape),
+        "dtype": "f32" if w.dtype == torch.float32 else str(w.dtype).replace("torch.", ""),
+        "data": "synthetic (seeded generator: the workload's BASELINE class probabilities and logit distribution)",
+        "config": workload_config(w, args.workload),
+        "run": {
+            "shape_per_rank": list(wr.shape),
             "global_batch": b_total,
-            "binning": cfg.binning,
-            "num_bins": cfg.num_bins,
-            "parallelism": f"batch-sharded dp{world}" if world > 1 else "single GPU",
+            "parallelism": (f"batch-sharded dp{world}" + (" (one batch split)" if strong else ""))
+            if world > 1 else "single GPU",
             "mode": mode,
             "l2": "flushed before every step: 512 MiB written, then read back, outside the events",
         },
         "hbm_frac_of_ideal_bytes": (step_bytes * world / (ms_per_step * 1e-3) / 1e9) / (peak * world),
         "eager_ms_per_step": eager_ms,
+        "floors": floors,
         "roofline": {
             "bound": "hbm",
             "kernel": dom,
@@ -423,7 +453,7 @@ def run_ours(args: argparse.Namespace) -> None:
             "algorithmic_bytes_per_launch": kernels[dom]["bytes"],
         },
         "kernels": kernels,
-        "gpu_launches": args.steps * (2 if world == 1 else 3),
+        "gpu_launches": args.steps * ours_per_step,
         "clocks": sampler.summary(),
         "e2e": {
             "value": voxels_all / (e2e_ms * 1e-3),
@@ -433,6 +463,10 @@ def run_ours(args: argparse.Namespace) -> None:
             "ms_per_step": e2e_ms,
         },
     }
+    if phases is not None:
+        line["phases_us"] = phases
+    if parity is not None:
+        line["parity"] = parity
     if world > 1:
         del run, graph, g_hist, g_grad
         torch.cuda.synchronize()
@@ -441,10 +475,79 @@ def run_ours(args: argparse.Namespace) -> None:
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = {
-                k: v for k, v in cpu_reference(w, cfg, args.cpu_seconds, 50).items()
+                k: v for k, v in cpu_reference(w, cfg, args.cpu_seconds, 20).items()
                 if k in ("value", "unit", "cores", "kind", "sample")
             }
         print(json.dumps(line), flush=True)
+
+
+def max_over_ranks(v: float, world: int, dev: torch.device) -> float:
+    if world == 1:
+        return v
+    t = torch.tensor([v], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sharded_phases(x, y, cfg, b_offset, b_total, flush, align, world, dev, reps: int = 50) -> dict:  # type: ignore[no-untyped-def]
+    """Device microseconds of each launch of an eager sharded step (statistics,
+    NCCL all-reduce, epilogue, backward), max over ranks, L2 flushed first."""
+    from ace_kernels_b200.distributed import _cuda_epilogue, _cuda_hist
+    from ace_kernels_b200.loss import alloc_outputs, kernel_args, run_backward
+
+    args = kernel_args(x.detach(), y, cfg, b_offset=b_offset, b_total=b_total)
+    s = args.setup
+    grad1 = torch.ones((), device=dev)
+    names = ("hist", "allreduce", "epilogue", "backward")
+    acc = dict.fromkeys(names, 0.0)
+    for _ in range(reps):
+        out = alloc_outputs(dev, b_total, s.cl, s.num_bins)
+        flush_l2(flush)
+        align()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+        ev[0].record()
+        _cuda_hist(args, out)
+        ev[1].record()
+        dist.all_reduce(out.hist)
+        ev[2].record()
+        _cuda_epilogue(args, out)
+        ev[3].record()
+        run_backward(args, out.coef, out.d, out.jac, grad1)
+        ev[4].record()
+        torch.cuda.synchronize()
+        for i, n in enumerate(names):
+            acc[n] += ev[i].elapsed_time(ev[i + 1]) * 1e3
+    return {n: max_over_ranks(acc[n] / reps, world, dev) for n in names}
+
+
+def sharded_parity(x, y, cfg, b_offset, b_total, world, dev) -> dict:  # type: ignore[no-untyped-def]
+    """Every rank's sharded loss, and rank 0's single-GPU loss over the batch
+    gathered from all ranks (the unsharded call on one device)."""
+    from ace_kernels_b200 import ace_loss
+    from ace_kernels_b200.distributed import sharded_ace_loss
+
+    with torch.no_grad():
+        loss = sharded_ace_loss(x.detach(), y, cfg, b_offset=b_offset, b_total=b_total)
+    losses = [torch.zeros_like(loss) for _ in range(world)]
+    dist.all_gather(losses, loss)
+    counts = [torch.zeros(1, dtype=torch.int64, device=dev) for _ in range(world)]
+    dist.all_gather(counts, torch.tensor([x.shape[0]], device=dev))
+    shapes = [int(c.item()) for c in counts]
+    xs = [torch.empty((n, *x.shape[1:]), dtype=x.dtype, device=dev) for n in shapes]
+    ys = [torch.empty((n, *y.shape[1:]), dtype=y.dtype, device=dev) for n in shapes]
+    dist.all_gather(xs, x.detach().contiguous())
+    dist.all_gather(ys, y.contiguous())
+    vals = [float(v.item()) for v in losses]
+    out = {"loss_equal_across_ranks": len(set(vals)) == 1, "loss": vals[0]}
+    if dist.get_rank() == 0:
+        with torch.no_grad():
+            ref = float(ace_loss(torch.cat(xs), torch.cat(ys), cfg, impl="b200_cuda").item())
+        out["single_gpu_loss"] = ref
+        out["max_rel_vs_single_gpu"] = max(abs(v - ref) / abs(ref) for v in vals)
+        out["ok"] = out["loss_equal_across_ranks"] and out["max_rel_vs_single_gpu"] <= 1e-5
+    del xs, ys
+    torch.cuda.synchronize()
+    return out
 
 
 def main() -> None:
