@@ -1,128 +1,126 @@
-"""Loss modules with the upstream ``HardL1ACELoss`` / ``SoftL1ACELoss`` signature.
+"""Loss modules with the constructor of the upstream ``HardL1ACELoss`` /
+``SoftL1ACELoss`` (cai4cai's Average-Calibration-Losses, which kapitan05/ace-kernels
+re-exports in ``src/ace_kernels/module.py``): the same parameters in the same
+order with the same defaults, plus a keyword-only ``impl``.
 
-The reference ships these drop-in modules in ``src/ace_kernels/module.py:1-178``:
-the upstream constructor (argument names, order, defaults and validation),
-``forward(input, target)``, and a keyword-only ``impl`` chosen per device by
-``resolve_impl`` (``module.py:90-94``). Here ``impl="auto"`` resolves to
-``b200_cuda``, the sm_100a implementation registered by this package.
+``impl="auto"`` picks the implementation from the input's device, as the
+reference's modules do (``module.py:90-94`` there): ``b200_cuda`` on a CUDA device
+of compute capability 10.x (B200, sm_100a). This package has nothing for other
+devices, so ``auto`` raises ``ValueError`` there; name another registered
+implementation with ``impl=...`` instead.
 
     from ace_kernels_b200.module import SoftL1ACELoss
     loss_fn = SoftL1ACELoss(to_onehot_y=True, softmax=True)
     loss = loss_fn(logits, labels)  # CUDA tensors on a B200
-
-There is no CPU implementation behind ``auto``: CPU tensors raise the
-registry's ``ValueError``, like any call of ``b200_cuda`` on an unsupported
-device.
 """
 
 from __future__ import annotations
 
+import functools
 from collections.abc import Callable, Sequence
 from enum import Enum
 from typing import Any
 
 import torch
-from torch.nn.modules.loss import _Loss
+from torch import nn
 
 from ace_kernels_b200.config import ACEConfig, Activation, Binning
-from ace_kernels_b200.registry import get_impl
+from ace_kernels_b200.registry import DEFAULT
 
-AUTO_IMPL = "b200_cuda"
-REDUCTIONS = ("none", "mean", "sum")
+SM100_IMPL = "b200_cuda"
+_REDUCTIONS = frozenset({"none", "mean", "sum"})
 
 Weight = Sequence[float] | float | int | torch.Tensor | None
 
 
-def _reduction(reduction: Any) -> str:
-    """``"none"`` / ``"mean"`` / ``"sum"``, or an enum member with that value (the
-    upstream classes take monai's ``LossReduction``); anything else raises
-    ``ValueError``, as ``LossReduction(value)`` does there."""
+@functools.lru_cache(maxsize=16)
+def _is_sm100(index: int) -> bool:
+    return torch.cuda.get_device_capability(index)[0] == 10
+
+
+def auto_impl(device: torch.device) -> str:
+    """The implementation ``impl="auto"`` takes for tensors on ``device``."""
+    if device.type == "cuda":
+        index = device.index if device.index is not None else torch.cuda.current_device()
+        if _is_sm100(index):
+            return SM100_IMPL
+    raise ValueError(
+        f"impl='auto' has no implementation for {device}: this package's b200_cuda needs a "
+        "CUDA device of compute capability 10.x; pass impl=<a registered name> instead"
+    )
+
+
+def _plain_reduction(reduction: Any) -> str:
+    """A reduction given as a string or as an enum whose value is one (monai's
+    ``LossReduction``, which the upstream modules accept)."""
     value = reduction.value if isinstance(reduction, Enum) else reduction
-    if value not in REDUCTIONS:
-        raise ValueError(f"{reduction!r} is not a valid LossReduction")
+    if value not in _REDUCTIONS:
+        raise ValueError(f"reduction must be one of {sorted(_REDUCTIONS)}, got {reduction!r}")
     return str(value)
 
 
-def _weight(weight: Weight) -> tuple[float, ...] | float | None:
+def _plain_weight(weight: Weight) -> tuple[float, ...] | float | None:
+    """The class weights as ACEConfig stores them: None, one float, or a tuple."""
     if weight is None:
         return None
     if isinstance(weight, torch.Tensor):
-        values = [float(w) for w in weight.flatten().tolist()]
-        return values[0] if weight.dim() == 0 else tuple(values)
-    if isinstance(weight, int | float):
+        flat = [float(v) for v in weight.detach().flatten().cpu().tolist()]
+        return flat[0] if weight.dim() == 0 else tuple(flat)
+    if isinstance(weight, (int, float)):
         return float(weight)
-    return tuple(float(w) for w in weight)
+    return tuple(float(v) for v in weight)
 
 
-class _ACELoss(_Loss):
+def _activation(sigmoid: bool, softmax: bool, other_act: Any) -> Activation:
+    if other_act is not None and not callable(other_act):
+        raise TypeError(f"other_act has to be a callable or None, not {type(other_act).__name__}")
+    chosen = [name for name, on in (("sigmoid", sigmoid), ("softmax", softmax),
+                                    ("other_act", other_act is not None)) if on]
+    if len(chosen) > 1:
+        raise ValueError(f"at most one activation may be set, got {' and '.join(chosen)}")
+    # a callable other_act is applied before the loss, which then sees probabilities
+    return "sigmoid" if sigmoid else "softmax" if softmax else "none"
+
+
+class _CalibrationLoss(nn.Module):
+    """Shared body of the two modules: an ACEConfig built from the upstream
+    arguments, and dispatch through the registry."""
+
     binning: Binning
 
-    def __init__(
-        self,
-        *,
-        num_bins: int,
-        include_background: bool,
-        to_onehot_y: bool,
-        sigmoid: bool,
-        softmax: bool,
-        other_act: Callable[[torch.Tensor], torch.Tensor] | None,
-        reduction: Any,
-        weight: Weight,
-        empty_weight: float,
-        right: bool,
-        ignore_empty_classes: bool,
-        impl: str,
-    ) -> None:
-        red = _reduction(reduction)
-        super().__init__(reduction=red)
-        if other_act is not None and not callable(other_act):
-            raise TypeError(f"other_act must be None or callable but is {type(other_act).__name__}.")
-        if int(sigmoid) + int(softmax) + int(other_act is not None) > 1:
-            raise ValueError(
-                "Incompatible values: more than 1 of [sigmoid=True, softmax=True, "
-                "other_act is not None]."
-            )
-        activation: Activation = "sigmoid" if sigmoid else "softmax" if softmax else "none"
+    def __init__(self, num_bins: int, include_background: bool, to_onehot_y: bool,
+                 sigmoid: bool, softmax: bool, other_act: Callable[[torch.Tensor], torch.Tensor] | None,
+                 reduction: Any, weight: Weight, empty_weight: float, right: bool,
+                 ignore_empty_classes: bool, impl: str) -> None:
+        super().__init__()
+        self.reduction = _plain_reduction(reduction)
         self.other_act = other_act
-        self.impl = impl
         self.config = ACEConfig(
-            binning=self.binning,
-            num_bins=num_bins,
-            activation=activation,
-            to_onehot_y=to_onehot_y,
-            include_background=include_background,
-            ignore_empty_classes=ignore_empty_classes,
-            reduction=red,
-            weight=_weight(weight),
-            right=right,
+            binning=self.binning, num_bins=num_bins,
+            activation=_activation(sigmoid, softmax, other_act), to_onehot_y=to_onehot_y,
+            include_background=include_background, ignore_empty_classes=ignore_empty_classes,
+            reduction=self.reduction, weight=_plain_weight(weight), right=right,
             empty_weight=empty_weight,
         )
         if impl != "auto":
-            get_impl(impl)  # an unknown name fails here (KeyError)
+            DEFAULT.lookup(impl)  # an unknown name fails at construction (KeyError)
+        self.impl = impl
 
     def resolve_impl(self, device: torch.device) -> str:
-        """Implementation used for inputs on ``device``: the forced name, else
-        ``b200_cuda`` (which rejects non-CUDA devices when called)."""
-        return self.impl if self.impl != "auto" else AUTO_IMPL
+        """The implementation that runs inputs on ``device``."""
+        return auto_impl(device) if self.impl == "auto" else self.impl
 
     def forward(self, input: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
-        """``input``: logits ``[B, C, *spatial]`` (probabilities when no activation);
-        ``target``: one-hot ``[B, C, ...]``, or class indices ``[B, 1, ...]`` with
-        ``to_onehot_y``."""
+        """``input``: ``[B, C, *spatial]`` logits (probabilities without an
+        activation); ``target``: ``[B, C, ...]`` targets, or ``[B, 1, ...]`` class
+        indices with ``to_onehot_y``."""
         if self.other_act is not None:
             input = self.other_act(input)
-        spec = get_impl(self.resolve_impl(input.device))
-        if not spec.supports(self.config.binning, input.device.type):
-            raise ValueError(
-                f"{spec.name!r} does not support binning={self.config.binning!r} "
-                f"on device={input.device.type!r}"
-            )
-        loss: torch.Tensor = spec.fn(input, target, self.config)
-        return loss
+        return DEFAULT.dispatch(self.resolve_impl(input.device), input, target, self.config)
 
 
-class HardL1ACELoss(_ACELoss):
-    """Hard-binned L1 average calibration error (mL1-ACE); upstream signature."""
+class HardL1ACELoss(_CalibrationLoss):
+    """mL1-ACE with hard binning (each probability counts in one bin)."""
 
     binning: Binning = "hard"
 
@@ -141,24 +139,14 @@ class HardL1ACELoss(_ACELoss):
         *,
         impl: str = "auto",
     ) -> None:
-        super().__init__(
-            num_bins=num_bins,
-            include_background=include_background,
-            to_onehot_y=to_onehot_y,
-            sigmoid=sigmoid,
-            softmax=softmax,
-            other_act=other_act,
-            reduction=reduction,
-            weight=weight,
-            empty_weight=0.01,  # not used by hard binning
-            right=right,
-            ignore_empty_classes=ignore_empty_classes,
-            impl=impl,
-        )
+        # hard binning has no empty_weight; ACEConfig keeps its default
+        super().__init__(num_bins, include_background, to_onehot_y, sigmoid, softmax, other_act,
+                         reduction, weight, 0.01, right, ignore_empty_classes, impl)
 
 
-class SoftL1ACELoss(_ACELoss):
-    """Soft-binned L1 average calibration error (mL1-ACE); upstream signature."""
+class SoftL1ACELoss(_CalibrationLoss):
+    """mL1-ACE with soft binning (each probability shared by its two nearest bin
+    centres, linearly)."""
 
     binning: Binning = "soft"
 
@@ -178,17 +166,5 @@ class SoftL1ACELoss(_ACELoss):
         *,
         impl: str = "auto",
     ) -> None:
-        super().__init__(
-            num_bins=num_bins,
-            include_background=include_background,
-            to_onehot_y=to_onehot_y,
-            sigmoid=sigmoid,
-            softmax=softmax,
-            other_act=other_act,
-            reduction=reduction,
-            weight=weight,
-            empty_weight=empty_weight,
-            right=right,
-            ignore_empty_classes=ignore_empty_classes,
-            impl=impl,
-        )
+        super().__init__(num_bins, include_background, to_onehot_y, sigmoid, softmax, other_act,
+                         reduction, weight, empty_weight, right, ignore_empty_classes, impl)

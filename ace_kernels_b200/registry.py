@@ -1,21 +1,19 @@
-"""Registry of mL1-ACE implementations: the reference's plugin API
-(kapitan05/ace-kernels ``src/ace_kernels/registry.py:14-100``) with the same names,
-argument meaning and errors, so code written against ``ace_kernels.registry``
-runs unchanged with ``impl="b200_cuda"``:
+"""Implementation registry with the plugin API of kapitan05/ace-kernels.
 
-- ``register(name, *, description, binnings, devices, slow)``: decorator; a
-  duplicate name raises ``ValueError``;
-- ``get_impl(name)``: unknown name raises ``KeyError``;
-- ``available_impls(binning, device)``;
-- ``ace_loss(input, target, config=None, impl=...)``: an unsupported binning or
-  device raises ``ValueError``.
-
-When the reference package itself is importable, ``ace_kernels_b200.plugin``
-registers ``b200_cuda`` into its registry as well.
+Code written against ``ace_kernels.registry`` (``src/ace_kernels/registry.py``
+there) keeps working here: the same five names exist with the same arguments,
+and the same error types are raised (``ValueError`` for a name taken twice or an
+unsupported binning/device, ``KeyError`` for an unknown name). Entries live in a
+:class:`Registry`; the module-level functions act on the package's default one,
+where ``ace_kernels_b200`` registers ``b200_cuda`` at import. (When the reference
+package is importable, ``ace_kernels_b200.plugin`` also enters ``b200_cuda`` in
+the reference's own registry.)
 """
 
-from collections.abc import Callable
-from dataclasses import dataclass
+from __future__ import annotations
+
+from collections.abc import Callable, Iterator
+from dataclasses import dataclass, field
 
 import torch
 
@@ -29,7 +27,9 @@ ALL_DEVICES: frozenset[str] = frozenset({"cpu", "cuda"})
 
 @dataclass(frozen=True)
 class ImplSpec:
-    """A registered implementation and the settings it supports."""
+    """One loss implementation: its callable ``fn(input, target, config)`` and
+    the binnings and device types it accepts (``slow``: excluded from heavy test
+    and benchmark sweeps)."""
 
     name: str
     fn: ACEFn
@@ -42,7 +42,47 @@ class ImplSpec:
         return binning in self.binnings and device in self.devices
 
 
-_REGISTRY: dict[str, ImplSpec] = {}
+@dataclass
+class Registry:
+    """Name -> :class:`ImplSpec` table with registration, lookup and dispatch."""
+
+    entries: dict[str, ImplSpec] = field(default_factory=dict)
+
+    def add(self, spec: ImplSpec) -> None:
+        if spec.name in self.entries:
+            raise ValueError(f"an implementation named {spec.name!r} exists already")
+        self.entries[spec.name] = spec
+
+    def lookup(self, name: str) -> ImplSpec:
+        spec = self.entries.get(name)
+        if spec is None:
+            known = ", ".join(sorted(self.entries)) or "none"
+            raise KeyError(f"no implementation named {name!r} (registered: {known})")
+        return spec
+
+    def select(self, binning: Binning | None, device: str | None) -> list[ImplSpec]:
+        return [s for s in self if (binning is None or binning in s.binnings)
+                and (device is None or device in s.devices)]
+
+    def dispatch(self, name: str, input: torch.Tensor, target: torch.Tensor,
+                 config: ACEConfig) -> torch.Tensor:
+        spec = self.lookup(name)
+        device = input.device.type
+        if not spec.supports(config.binning, device):
+            raise ValueError(
+                f"implementation {name!r} cannot run {config.binning} binning on a "
+                f"{device} tensor (it takes binnings {sorted(spec.binnings)} on "
+                f"devices {sorted(spec.devices)})"
+            )
+        return spec.fn(input, target, config)
+
+    def __iter__(self) -> Iterator[ImplSpec]:
+        return iter(self.entries.values())
+
+
+DEFAULT = Registry()
+# the default registry's table (tests substitute entries through it)
+_REGISTRY = DEFAULT.entries
 
 
 def register(
@@ -53,36 +93,24 @@ def register(
     devices: frozenset[str] = ALL_DEVICES,
     slow: bool = False,
 ) -> Callable[[ACEFn], ACEFn]:
-    """Decorator adding an implementation to the registry under ``name``."""
+    """Class-free decorator form of :meth:`Registry.add` on the default registry;
+    returns the function unchanged."""
 
-    def decorator(fn: ACEFn) -> ACEFn:
-        if name in _REGISTRY:
-            raise ValueError(f"implementation {name!r} already registered")
-        _REGISTRY[name] = ImplSpec(name, fn, binnings, devices, description, slow)
+    def enter(fn: ACEFn) -> ACEFn:
+        DEFAULT.add(ImplSpec(name, fn, frozenset(binnings), frozenset(devices), description, slow))
         return fn
 
-    return decorator
+    return enter
 
 
 def get_impl(name: str) -> ImplSpec:
-    try:
-        return _REGISTRY[name]
-    except KeyError:
-        raise KeyError(
-            f"unknown implementation {name!r}; available: {sorted(_REGISTRY)}"
-        ) from None
+    return DEFAULT.lookup(name)
 
 
-def available_impls(
-    binning: Binning | None = None, device: str | None = None
-) -> list[ImplSpec]:
-    """Registered implementations, optionally filtered by binning and device."""
-    return [
-        spec
-        for spec in _REGISTRY.values()
-        if (binning is None or binning in spec.binnings)
-        and (device is None or device in spec.devices)
-    ]
+def available_impls(binning: Binning | None = None, device: str | None = None) -> list[ImplSpec]:
+    """Implementations of the default registry accepting ``binning`` and
+    ``device`` (either filter may be left out)."""
+    return DEFAULT.select(binning, device)
 
 
 def ace_loss(
@@ -91,20 +119,9 @@ def ace_loss(
     config: ACEConfig | None = None,
     impl: str = "b200_cuda",
 ) -> torch.Tensor:
-    """Compute the mL1-ACE loss with the chosen implementation.
-
-    Args:
-        input: logits or probabilities, shape ``[B, C, *spatial]``.
-        target: one-hot ``[B, C, *spatial]``, or labels ``[B, 1, *spatial]``
-            when ``config.to_onehot_y`` is set.
-        config: loss options; defaults to ``ACEConfig()``.
-        impl: registered implementation name.
-    """
-    config = config if config is not None else ACEConfig()
-    spec = get_impl(impl)
-    if not spec.supports(config.binning, input.device.type):
-        raise ValueError(
-            f"{impl!r} does not support binning={config.binning!r} "
-            f"on device={input.device.type!r}"
-        )
-    return spec.fn(input, target, config)
+    """mL1-ACE of ``input`` (``[B, C, *spatial]`` logits, or probabilities when
+    the config's activation is "none") against ``target`` (``[B, C, ...]``
+    targets, or ``[B, 1, ...]`` class indices with ``to_onehot_y``), computed by
+    the implementation registered as ``impl``; ``config`` defaults to
+    ``ACEConfig()``."""
+    return DEFAULT.dispatch(impl, input, target, config if config is not None else ACEConfig())

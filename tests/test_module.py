@@ -46,9 +46,9 @@ def test_same_signature(cls: type, upstream: list) -> None:
 
 
 def test_validation_errors() -> None:
-    with pytest.raises(ValueError, match="Incompatible values"):
+    with pytest.raises(ValueError, match="at most one activation"):
         HardL1ACELoss(sigmoid=True, softmax=True)
-    with pytest.raises(ValueError, match="Incompatible values"):
+    with pytest.raises(ValueError, match="at most one activation"):
         SoftL1ACELoss(softmax=True, other_act=torch.sigmoid)
     with pytest.raises(TypeError, match="other_act"):
         SoftL1ACELoss(other_act=3)
@@ -71,15 +71,21 @@ def test_config_from_arguments() -> None:
     h = HardL1ACELoss(sigmoid=True, weight=2)
     assert (h.config.binning, h.config.activation, h.config.weight) == ("hard", "sigmoid", 2.0)
     assert HardL1ACELoss().config.activation == "none"
-    assert h.resolve_impl(torch.device("cuda")) == "b200_cuda"
     assert HardL1ACELoss(impl="b200_cuda").resolve_impl(torch.device("cpu")) == "b200_cuda"
+
+
+def test_auto_has_no_cpu_implementation() -> None:
+    with pytest.raises(ValueError, match="compute capability 10"):
+        HardL1ACELoss().resolve_impl(torch.device("cpu"))
 
 
 def test_cpu_inputs_have_no_fallback() -> None:
     x = torch.randn(1, 2, 4, 4)
     y = torch.randint(0, 2, (1, 1, 4, 4))
-    with pytest.raises(ValueError, match="device='cpu'"):
+    with pytest.raises(ValueError, match="impl='auto' has no implementation for cpu"):
         SoftL1ACELoss(to_onehot_y=True, softmax=True)(x, y)
+    with pytest.raises(ValueError, match="cannot run soft binning on a cpu tensor"):
+        SoftL1ACELoss(to_onehot_y=True, softmax=True, impl="b200_cuda")(x, y)
 
 
 def _kwargs(cfg: dict) -> dict:
@@ -121,6 +127,13 @@ def test_module_matches_reference_case(name: str) -> None:
         assert torch.isfinite(grad).all()
         return
     torch.testing.assert_close(grad.cpu(), rec["grad"], rtol=CUDA_GRAD_RTOL, atol=CUDA_GRAD_ATOL)
+
+
+@pytest.mark.gpu
+def test_auto_takes_b200_cuda_on_sm100() -> None:
+    assert torch.cuda.get_device_capability(0)[0] == 10
+    assert HardL1ACELoss().resolve_impl(torch.device("cuda")) == "b200_cuda"
+    assert SoftL1ACELoss().resolve_impl(torch.device("cuda", 0)) == "b200_cuda"
 
 
 @pytest.mark.gpu
