@@ -64,7 +64,8 @@ class Inputs(Structure):
     ]
 
 
-KERNEL_HIST, KERNEL_SOFT_PIPE, KERNEL_GRAD, KERNEL_GRAD_PIPE = 0, 1, 2, 3
+KERNEL_HIST, KERNEL_SOFT_PIPE, KERNEL_GRAD, KERNEL_GRAD_PIPE, KERNEL_MC_PIPE, KERNEL_MC_GRAD = (
+    0, 1, 2, 3, 4, 5)
 
 
 class Plan(Structure):

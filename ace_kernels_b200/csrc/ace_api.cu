@@ -249,6 +249,7 @@ Variant choose_variant(const ace_b200_inputs* in, const ace_b200_options* opt, c
   v.soft = opt->soft != 0;
   v.labels = in->target_kind == ACE_B200_TARGET_LABELS;
   v.split = false;
+  v.mc = false;
   const int es = elem_size(in->x_dtype);
   const int vmax = 16 / es;
   int V;
@@ -406,6 +407,73 @@ bool soft_fwd_setup(const ace_b200_inputs* in, const ace_b200_options* opt, cons
   return true;
 }
 
+// mc_fwd_kernel: int64 labels and a softmax over kMcMinChannels to
+// kMcMaxChannels channels, soft or hard binning, rows of whole 16-byte vectors
+// and 16-byte aligned logits and labels (the bulk copies move 16-byte multiples). Shared memory: the table (hard: [K][C][R][3] words;
+// soft: [K + 1][C][2][R][3]), the bin-edge table (hard), then three or four
+// stages of a 1024-voxel tile. R lane replicas (a power of two up to 32, at
+// least 4 hard / 8 soft), the most that fit beside three stages, else two; the
+// epoch follows from R (the kernel's word ranges). Returns false when the case
+// does not fit (hist_kernel then takes it).
+constexpr size_t kMcSmemBudget = 218 * 1024;
+
+bool mc_fwd_setup(const ace_b200_inputs* in, const ace_b200_options* opt, Variant& v,
+                  FwdParams& p, const Workspace& w, int dev, bool want_epilogue, int& smem,
+                  dim3& grid) {
+  const int K = opt->num_bins, C = (int)in->C;
+  const bool soft = opt->soft != 0;
+  const int es = elem_size(in->x_dtype);
+  if (!v.softmax || !v.labels || C > kMcMaxChannels || C < kMcMinChannels) return false;
+  if (in->N % (16 / es) != 0 || !aligned(in->x, 16) || !aligned(in->target, 16)) return false;
+  const size_t stage_bytes = (size_t)kMcTileVoxels * (C * es + 8);
+  const size_t slot_bytes = (size_t)(soft ? (K + 1) * 2 : K) * C * 3 * 4;  // one replica
+  const size_t lohi_bytes = soft ? 0 : (size_t)(K + 1) * kTabCopies * sizeof(float2);
+  auto table = [&](int r) { return round_up(slot_bytes * r, 128); };
+  auto need = [&](int r, int st) { return round_up(table(r) + lohi_bytes, 128) + st * stage_bytes; };
+  const int r_min = soft ? 8 : 4;
+  int R = 0, stages = 0;
+  for (int st = 3; st >= 2 && R == 0; --st)
+    for (int r = 32; r >= r_min; r >>= 1)
+      if (need(r, st) <= kMcSmemBudget) {
+        R = r;
+        stages = st;
+        break;
+      }
+  if (R == 0) return false;
+  if (stages == 3 && need(R, 4) <= kMcSmemBudget) stages = 4;
+  const int64_t tiles = (in->N + kMcTileVoxels - 1) / kMcTileVoxels;
+  int64_t ctas = (int64_t)sm_count(dev);  // one CTA per SM
+  if (ctas > in->B * tiles) ctas = in->B * tiles;
+  if (ctas < 1) ctas = 1;
+  v.mc = true;
+  v.CM = C <= 8 ? 8 : C <= 16 ? 16 : 24;
+  smem = (int)need(R, stages);
+  p.iacc = reinterpret_cast<unsigned long long*>(w.accum);
+  p.pool_ctr = w.pool;
+  p.wt_batch = tiles;
+  // word ranges (mc_fwd_kernel): soft R - 1 tiles, and at most kMcAggEpoch with the
+  // interval-0 aggregates (CM <= 16); hard 2R - 1
+  p.epoch = soft ? (v.CM <= 16 && R - 1 > kMcAggEpoch ? kMcAggEpoch : R - 1) : 2 * R - 1;
+  p.stages = stages;
+  p.table_bytes = (int)table(R);
+  p.stage_offset = (int)round_up(table(R) + lohi_bytes, 128);
+  p.R = R;
+  p.flush_tiles = 0;
+  p.g.N = in->N;
+  p.g.B = (int)in->B;
+  p.g.C = C;
+  p.g.CL = C - opt->offset;
+  p.g.offset = opt->offset;
+  p.g.chunks = (int)ctas;
+  p.g.tiles = tiles;
+  p.g.tiles_per_chunk = 0;
+  p.g.chunks_per_batch = 0;
+  const int64_t rows = in->b_total * p.g.CL;
+  p.do_epilogue = want_epilogue && rows <= 8 * kEpiRowsPerCta;
+  grid = dim3((unsigned)ctas, 1u);
+  return true;
+}
+
 int hist_impl(const ace_b200_inputs* in, const ace_b200_options* opt, float* hist,
               const ace_b200_epilogue_out* out, void* workspace, size_t ws_bytes, void* stream) {
   int CL = 0;
@@ -457,6 +525,22 @@ int hist_impl(const ace_b200_inputs* in, const ace_b200_options* opt, float* his
     // CTAs start spread over the batches and move on to others' tiles when theirs
     // run out, so any launch with more than one batch may cross batches
     set_plan(ACE_B200_KERNEL_SOFT_PIPE, soft_grid.x, in->B > 1, p.stages, p.R, p.do_epilogue,
+             p.wt_batch);
+    if (out && !p.do_epilogue) {
+      e = launch_epilogue(hist, p.epi, w.epi_counter, w.epi_partial, s);
+      if (e != cudaSuccess) return cuda_fail(e, "epilogue kernel launch");
+    }
+    return ACE_B200_OK;
+  }
+
+  // Labels and a softmax over many channels: mc_fwd_kernel, with the same tables
+  // as hist_kernel (build_table above).
+  int mc_smem = 0;
+  dim3 mc_grid;
+  if (mc_fwd_setup(in, opt, v, p, w, dev, out != nullptr, mc_smem, mc_grid)) {
+    e = launch_hist_any(p, v, mc_grid, mc_smem, in->x_dtype, s, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "many-channel histogram kernel launch");
+    set_plan(ACE_B200_KERNEL_MC_PIPE, mc_grid.x, in->B > 1, p.stages, p.R, p.do_epilogue,
              p.wt_batch);
     if (out && !p.do_epilogue) {
       e = launch_epilogue(hist, p.epi, w.epi_counter, w.epi_partial, s);
@@ -732,6 +816,57 @@ int ace_b200_backward(const ace_b200_inputs* in, const ace_b200_options* opt,
       return ACE_B200_OK;
     }
     v.split = false;
+  }
+
+  // mc_grad_kernel: softmax over kMcMinChannels..kMcMaxChannels channels, soft
+  // binning with labels or hard binning, rows of whole 16-byte vectors, 16-byte
+  // aligned logits, labels and dx. Shared memory: the records of all local
+  // batches in `copies` interleaved copies (the most that fit beside three
+  // stages, else two), the bin table (hard), then the ring of 1024-voxel tiles.
+  if (v.softmax && (!soft || v.labels) && in->C >= kMcMinChannels && in->C <= kMcMaxChannels &&
+      in->N % (16 / elem_size(in->x_dtype)) == 0 && aligned(in->x, 16) && aligned(dx, 16) &&
+      (!soft || aligned(in->target, 16))) {
+    const size_t stage_bytes =
+        (size_t)kMcTileVoxels * (in->C * elem_size(in->x_dtype) + (soft ? 8 : 0));
+    const size_t table_bytes = soft ? 0 : (size_t)(K + 1) * kTabCopies * sizeof(float2);
+    auto fixed = [&](int c) {
+      return round_up((size_t)(soft ? 16 : 4) * c * in->B * CL * (K + 1) + table_bytes, 128);
+    };
+    int copies = 0, stages = 0;
+    for (int st = 3; st >= 2 && copies == 0; --st)
+      for (int c = soft ? 16 : 32; c >= (soft ? 2 : 1); c /= 2)  // soft: 16-byte record pairs
+        if (fixed(c) + st * stage_bytes <= kMcSmemBudget) {
+          copies = c;
+          stages = st;
+          break;
+        }
+    if (copies > 0) {
+      if (stages == 3 && fixed(copies) + 4 * stage_bytes <= kMcSmemBudget) stages = 4;
+      const int64_t tiles = (in->N + kMcTileVoxels - 1) / kMcTileVoxels;
+      int64_t ctas = sm_count(dev);
+      if (ctas > tiles * in->B) ctas = tiles * in->B;
+      if (ctas < 1) ctas = 1;
+      v.mc = true;
+      v.split = false;
+      v.CM = in->C <= 8 ? 8 : in->C <= 16 ? 16 : 24;
+      p.rec_copies = copies;
+      p.stages = stages;
+      p.stage_offset = (int)fixed(copies);
+      p.tiles_per_batch = tiles;
+      p.g.N = in->N;
+      p.g.B = (int)in->B;
+      p.g.C = (int)in->C;
+      p.g.CL = CL;
+      p.g.offset = opt->offset;
+      const int smem = (int)(fixed(copies) + stages * stage_bytes);
+      const dim3 grid((unsigned)ctas, 1u);
+      if (in->x_dtype == ACE_B200_F32) e = launch_grad<float>(p, v, grid, smem, s, dev);
+      else if (in->x_dtype == ACE_B200_BF16) e = launch_grad<__nv_bfloat16>(p, v, grid, smem, s, dev);
+      else e = launch_grad<__half>(p, v, grid, smem, s, dev);
+      if (e != cudaSuccess) return cuda_fail(e, "gradient kernel launch");
+      set_plan(ACE_B200_KERNEL_MC_GRAD, ctas, in->B > 1, stages, 0, false, tiles);
+      return ACE_B200_OK;
+    }
   }
 
   // grad_kernel. Record copies: as many as fit in 96 KB (two CTAs per SM keep

@@ -30,6 +30,107 @@
 
 namespace ace {
 
+// The producer thread of a backward pipeline (grad_tma_kernel, mc_grad_kernel):
+// the tiles of all batches round-robin over the CTAs (tile k of the sequence by
+// CTA k mod grid), the sequence running from the batches' last tiles to their
+// first, the batches interleaved (k -> batch k % B, tile tpb - 1 - k / B). Each
+// tile's C logit rows (TV * sizeof(T) bytes apart) and, when `lab` is given, its
+// int64 labels (after the rows) go into stage i % S of the ring, with s_meta[s] =
+// {tile, batch, voxels, 0}; the last stage carries the end marker (tile -1). A
+// wait that runs out sets s_abort; the producer then waits (bounded) for its
+// copies still in flight.
+template <typename T, int TV>
+__device__ __forceinline__ void produce_round_robin(const T* x, const int64_t* lab, int C,
+                                                    int64_t N, int B, int64_t tpb,
+                                                    unsigned stage0, unsigned SB, int S,
+                                                    unsigned long long* s_full,
+                                                    unsigned long long* s_empty, int4* s_meta,
+                                                    volatile int* s_abort) {
+  constexpr unsigned XB = TV * sizeof(T);
+  const int64_t total = tpb * B;
+  int issued = 0;
+  int64_t k = blockIdx.x;
+  for (int i = 0;; ++i, k += gridDim.x) {
+    const int s = i % S;
+    const unsigned use = (unsigned)(i / S);
+    if (use > 0 && !mbar_wait(smem_addr(&s_empty[s]), (use - 1) & 1u)) {
+      *s_abort = 1;
+      break;
+    }
+    if (*s_abort) break;
+    const unsigned full = smem_addr(&s_full[s]);
+    if (k >= total) {  // the end marker (no copies)
+      s_meta[s] = make_int4(-1, 0, 0, 0);
+      mbar_arrive(full);
+      break;
+    }
+    const int tb = (int)(k % B);
+    const int64_t tile = tpb - 1 - k / B;
+    const int64_t v0 = tile * TV;
+    const int cnt = (int)min((int64_t)TV, N - v0);
+    s_meta[s] = make_int4((int)tile, tb, cnt, 0);
+    const unsigned xb = (unsigned)cnt * (unsigned)sizeof(T);
+    mbar_arrive_tx(full, (unsigned)C * xb + (lab ? (unsigned)cnt * 8u : 0u));
+    const unsigned dst = stage0 + (unsigned)s * SB;
+    const T* gx = x + (int64_t)tb * C * N + v0;
+    for (int c = 0; c < C; ++c) bulk_load(dst + c * XB, gx + (int64_t)c * N, xb, full);
+    if (lab) bulk_load(dst + C * XB, lab + (int64_t)tb * N + v0, (unsigned)cnt * 8u, full);
+    issued = i + 1;
+  }
+  // after an abort, no copy may still be in flight when the CTA leaves
+  if (*s_abort)
+    for (int i = issued - S > 0 ? issued - S : 0; i < issued; ++i)
+      mbar_wait(smem_addr(&s_full[i % S]), (unsigned)(i / S) & 1u);
+}
+
+// The per-(batch, row, interval or bin) records of the pipelined backwards, built
+// by the consumer threads into shared memory from coef, d, jac and the upstream
+// gradient g (after the dependency wait): hard, [B][CL][K + 1][copies] floats
+// g coef[k] (0 for the count K, no bin); soft, [B][CL][K + 1][2][copies] float2
+// {F - D y, 2 D} for the class flags y = 0, 1 of interval j (see grad_kernel: the
+// soft gradient is F + D (2 p - y) inside an interval). One thread per record
+// writes all its copies with 16-byte stores (copies * record bytes is a multiple
+// of 16), or 4-byte stores when a hard record has fewer than four copies.
+template <bool SOFT>
+__device__ __forceinline__ void build_records(const BwdParams& P, float* rec, int CL,
+                                              const float2* s_map) {
+  const int K = P.tab.K, B = P.g.B, copies = P.rec_copies;
+  for (int e = threadIdx.x; e < B * CL * (K + 1); e += kPipeConsumerWarps * 32) {
+    const int bro = e / (K + 1), j = e - bro * (K + 1);  // bro = b * CL + row
+    const int b = bro / CL, row = bro - b * CL;
+    const int64_t grow = (int64_t)(P.b_offset + b) * CL + row;
+    const float g = P.jac[grow] * (P.grad_per_row ? P.grad_out[grow] : P.grad_out[0]);
+    const float* cf = P.coef + grow * K;
+    const float* dd = P.d + grow * K;
+    if constexpr (!SOFT) {
+      const unsigned u = __float_as_uint(j < K ? g * cf[j] : 0.0f);
+      if (copies >= 4) {
+        const uint4 v = make_uint4(u, u, u, u);
+        uint4* dst = reinterpret_cast<uint4*>(rec + e * copies);
+        for (int q = 0; q < copies / 4; ++q) dst[q] = v;
+      } else {
+        for (int q = 0; q < copies; ++q) rec[e * copies + q] = __uint_as_float(u);
+      }
+    } else {
+      const int l = max(j - 1, 0), r = min(j, K - 1);
+      const float a = g * cf[l], bb = g * cf[r];
+      double F = a, D = 0.0;
+      if (j > 0 && j < K) {
+        const float2 mp = s_map[j];
+        const double lo = mp.x, inv = (double)mp.y / (double)kFixScale;
+        D = ((double)bb - (double)a) * inv;
+        F = (double)a - D * lo + inv * ((double)a * dd[l] - (double)bb * dd[r]);
+      }
+      const unsigned d2 = __float_as_uint(2.0f * (float)D);
+      const unsigned f0 = __float_as_uint((float)F), f1 = __float_as_uint((float)(F - D));
+      const uint4 v0 = make_uint4(f0, d2, f0, d2), v1 = make_uint4(f1, d2, f1, d2);
+      uint4* dst = reinterpret_cast<uint4*>(rec + 4 * e * copies);
+      for (int q = 0; q < copies / 2; ++q) dst[q] = v0;
+      for (int q = copies / 2; q < copies; ++q) dst[q] = v1;
+    }
+  }
+}
+
 template <typename T, int C, int OFF, bool SOFT>
 __global__ void __launch_bounds__(kPipeThreads, 1) grad_tma_kernel(const __grid_constant__ BwdParams P) {
   constexpr int NCW = kPipeConsumerWarps, NT = kPipeThreads;
@@ -71,89 +172,21 @@ __global__ void __launch_bounds__(kPipeThreads, 1) grad_tma_kernel(const __grid_
   }
   __syncthreads();
 
-  // Tile sequence: k -> batch k % B, tile tpb - 1 - k / B of that batch.
   const int64_t tpb = P.tiles_per_batch;
-  const int64_t total = tpb * B;
 
   if (warp == NCW) {
     // ---------------- producer (one thread) ----------------
     // The logits and labels are inputs of the forward too, never written by the
     // kernel this one depends on: the copies may start before that kernel ends.
-    if (lane == 0) {
-      const T* x = static_cast<const T*>(P.x);
-      const int64_t* lab = static_cast<const int64_t*>(P.target);
-      int issued = 0;
-      int64_t k = blockIdx.x;
-      for (int i = 0;; ++i, k += gridDim.x) {
-        const int s = i % S;
-        const unsigned use = (unsigned)(i / S);
-        if (use > 0 && !mbar_wait(empty_bar(s), (use - 1) & 1u)) {
-          s_abort = 1;
-          break;
-        }
-        if (s_abort) break;
-        if (k >= total) {  // the end marker (no copies)
-          s_meta[s] = make_int4(-1, 0, 0, 0);
-          mbar_arrive(full_bar(s));
-          break;
-        }
-        const int tb = (int)(k % B);
-        const int64_t tile = tpb - 1 - k / B;
-        const int64_t v0 = tile * TV;
-        const int cnt = (int)min((int64_t)TV, N - v0);
-        s_meta[s] = make_int4((int)tile, tb, cnt, 0);
-        const unsigned xb = (unsigned)cnt * (unsigned)sizeof(T);
-        mbar_arrive_tx(full_bar(s), C * xb + (SOFT ? (unsigned)cnt * 8u : 0u));
-        const unsigned dst = stage0 + (unsigned)s * SB;
-        const T* gx = x + (int64_t)tb * C * N + v0;
-#pragma unroll
-        for (int c = 0; c < C; ++c) bulk_load(dst + c * XB, gx + (int64_t)c * N, xb, full_bar(s));
-        if constexpr (SOFT)
-          bulk_load(dst + C * XB, lab + (int64_t)tb * N + v0, (unsigned)cnt * 8u, full_bar(s));
-        issued = i + 1;
-      }
-      // after an abort, no copy may still be in flight when the CTA leaves
-      if (s_abort)
-        for (int i = issued - S > 0 ? issued - S : 0; i < issued; ++i)
-          mbar_wait(full_bar(i % S), (unsigned)(i / S) & 1u);
-    }
+    if (lane == 0)
+      produce_round_robin<T, TV>(static_cast<const T*>(P.x),
+                                 SOFT ? static_cast<const int64_t*>(P.target) : nullptr, C, N, B,
+                                 tpb, stage0, SB, S, s_full, s_empty, s_meta, &s_abort);
   } else {
     // ---------------- consumers ----------------
     // coef, d and jac come from the previous kernel: records only after it
     ace_grid_dependency_wait();
-    // One consumer thread per (batch, row, j) record; it writes all the record's
-    // copies (16-byte stores: copies * record bytes is a multiple of 16).
-    for (int e = tid; e < B * CL * (K + 1); e += NCW * 32) {
-      const int bro = e / (K + 1), j = e - bro * (K + 1);  // bro = b * CL + row
-      const int b = bro / CL, row = bro - b * CL;
-      const int64_t grow = (int64_t)(P.b_offset + b) * CL + row;
-      const float g = P.jac[grow] * (P.grad_per_row ? P.grad_out[grow] : P.grad_out[0]);
-      const float* cf = P.coef + grow * K;
-      const float* dd = P.d + grow * K;
-      if constexpr (!SOFT) {
-        const unsigned u = __float_as_uint(j < K ? g * cf[j] : 0.0f);
-        const uint4 v = make_uint4(u, u, u, u);
-        uint4* dst = reinterpret_cast<uint4*>(rec + e * copies);
-        for (int q = 0; q < copies / 4; ++q) dst[q] = v;
-      } else {
-        // {F - D y, 2 D} for y = 0, 1 (records [batch][row][j][flag][copies])
-        const int l = max(j - 1, 0), r = min(j, K - 1);
-        const float a = g * cf[l], bb = g * cf[r];
-        double F = a, D = 0.0;
-        if (j > 0 && j < K) {
-          const float2 mp = s_map[j];
-          const double lo = mp.x, inv = (double)mp.y / (double)kFixScale;
-          D = ((double)bb - (double)a) * inv;
-          F = (double)a - D * lo + inv * ((double)a * dd[l] - (double)bb * dd[r]);
-        }
-        const unsigned d2 = __float_as_uint(2.0f * (float)D);
-        const unsigned f0 = __float_as_uint((float)F), f1 = __float_as_uint((float)(F - D));
-        const uint4 v0 = make_uint4(f0, d2, f0, d2), v1 = make_uint4(f1, d2, f1, d2);
-        uint4* dst = reinterpret_cast<uint4*>(rec + 4 * e * copies);
-        for (int q = 0; q < copies / 2; ++q) dst[q] = v0;
-        for (int q = copies / 2; q < copies; ++q) dst[q] = v1;
-      }
-    }
+    build_records<SOFT>(P, rec, CL, s_map);
     consumer_sync();
     const float2* my_lohi = lohi_t + (lane & (kTabCopies - 1));
     auto entry = [&](int j) -> float2 { return my_lohi[j * kTabCopies]; };

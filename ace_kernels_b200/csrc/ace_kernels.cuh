@@ -19,6 +19,7 @@ struct Variant {
   bool soft;    // soft binning
   bool labels;  // int64 labels (else dense fp32 targets)
   bool split;   // forward only: soft_fwd_kernel (softmax, CM <= 4, soft, labels)
+  bool mc;      // mc_fwd_kernel / mc_grad_kernel (softmax over many channels)
   int offset;   // soft_fwd_kernel: 1 when the background channel is dropped
 };
 
@@ -759,6 +760,7 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constan
 
 #include "ace_tma.cuh"       // pipeline primitives
 #include "ace_soft_fwd.cuh"  // soft_fwd_kernel (uses the helpers above)
+#include "ace_mc_fwd.cuh"    // mc_fwd_kernel (uses soft_fwd_kernel's pipeline)
 
 namespace ace {
 
@@ -1030,6 +1032,7 @@ __global__ void __launch_bounds__(kThreads) grad_kernel(const __grid_constant__ 
 }  // namespace ace
 
 #include "ace_grad_tma.cuh"  // grad_tma_kernel (uses grad_p above)
+#include "ace_mc_grad.cuh"   // mc_grad_kernel (grad_tma_kernel's pipeline, mc_fwd_kernel's math)
 
 namespace ace {
 
@@ -1133,11 +1136,17 @@ ACE_LAUNCHER(HistLauncher, (hist_kernel<T, V, CM, SM, SOFT, LAB>), kHistThreads,
 template <typename T, int C, int OFF>
 ACE_LAUNCHER(SoftFwdLauncher, (soft_fwd_kernel<T, C, OFF>), kPipeThreads, FwdParams);
 
+template <typename T, int CM, bool SOFT>
+ACE_LAUNCHER(McFwdLauncher, (mc_fwd_kernel<T, CM, SOFT>), kPipeThreads, FwdParams);
+
 template <typename T, int V, int CM, bool SM, bool SOFT, bool LAB>
 ACE_LAUNCHER(GradLauncher, (grad_kernel<T, V, CM, SM, SOFT, LAB>), kThreads, BwdParams);
 
 template <typename T, int C, int OFF, bool SOFT>
 ACE_LAUNCHER(GradTmaLauncher, (grad_tma_kernel<T, C, OFF, SOFT>), kPipeThreads, BwdParams);
+
+template <typename T, int CM, bool SOFT>
+ACE_LAUNCHER(McGradLauncher, (mc_grad_kernel<T, CM, SOFT>), kPipeThreads, BwdParams);
 
 #undef ACE_LAUNCHER
 
@@ -1201,11 +1210,29 @@ ACE_LAUNCHER(GradTmaLauncher, (grad_tma_kernel<T, C, OFF, SOFT>), kPipeThreads, 
     }                                                                                     \
   } while (0)
 
+// The many-channel forward for labels: channel capacities 8, 16 and 24.
+#define ACE_MC_FWD_CASES(F, T, ...)                                                      \
+  do {                                                                                   \
+    if (v.mc) {                                                                          \
+      if (v.soft) {                                                                      \
+        if (v.CM == 8) return McFwdLauncher<T, 8, true>::F(__VA_ARGS__);                 \
+        if (v.CM == 16) return McFwdLauncher<T, 16, true>::F(__VA_ARGS__);              \
+        if (v.CM == 24) return McFwdLauncher<T, 24, true>::F(__VA_ARGS__);              \
+      } else {                                                                           \
+        if (v.CM == 8) return McFwdLauncher<T, 8, false>::F(__VA_ARGS__);                \
+        if (v.CM == 16) return McFwdLauncher<T, 16, false>::F(__VA_ARGS__);             \
+        if (v.CM == 24) return McFwdLauncher<T, 24, false>::F(__VA_ARGS__);             \
+      }                                                                                  \
+    }                                                                                    \
+  } while (0)
+
 template <typename T>
 cudaError_t launch_hist(const FwdParams& p, const Variant& v, dim3 grid, int smem,
                         cudaStream_t s, int dev) {
   ACE_SOFT_FWD_CASES(run, T, p, grid, smem, s, dev);
   if (v.split) return cudaErrorInvalidValue;
+  ACE_MC_FWD_CASES(run, T, p, grid, smem, s, dev);
+  if (v.mc) return cudaErrorInvalidValue;
   ACE_FOR_SOFT_LABELS(ACE_VARIANT_CASES(HistLauncher, run, T, p, grid, smem, s, dev));
   return cudaErrorInvalidValue;
 }
@@ -1234,10 +1261,29 @@ cudaError_t launch_hist(const FwdParams& p, const Variant& v, dim3 grid, int sme
     }                                                                                    \
   } while (0)
 
+// The many-channel backward: channel capacities 8, 16 and 24, soft binning with
+// labels or hard binning.
+#define ACE_MC_GRAD_CASES(F, T, ...)                                                     \
+  do {                                                                                   \
+    if (v.mc) {                                                                          \
+      if (v.soft) {                                                                      \
+        if (v.CM == 8) return McGradLauncher<T, 8, true>::F(__VA_ARGS__);                \
+        if (v.CM == 16) return McGradLauncher<T, 16, true>::F(__VA_ARGS__);             \
+        if (v.CM == 24) return McGradLauncher<T, 24, true>::F(__VA_ARGS__);             \
+      } else {                                                                           \
+        if (v.CM == 8) return McGradLauncher<T, 8, false>::F(__VA_ARGS__);               \
+        if (v.CM == 16) return McGradLauncher<T, 16, false>::F(__VA_ARGS__);            \
+        if (v.CM == 24) return McGradLauncher<T, 24, false>::F(__VA_ARGS__);            \
+      }                                                                                  \
+      return cudaErrorInvalidValue;                                                      \
+    }                                                                                    \
+  } while (0)
+
 template <typename T>
 cudaError_t launch_grad(const BwdParams& p, const Variant& v, dim3 grid, int smem,
                         cudaStream_t s, int dev) {
   ACE_GRAD_TMA_CASES(run, T, p, grid, smem, s, dev);
+  ACE_MC_GRAD_CASES(run, T, p, grid, smem, s, dev);
   ACE_FOR_SOFT_LABELS(ACE_VARIANT_CASES(GradLauncher, run, T, p, grid, smem, s, dev));
   return cudaErrorInvalidValue;
 }
@@ -1246,6 +1292,8 @@ template <typename T>
 int hist_occupancy(const Variant& v, int smem, int dev) {
   ACE_SOFT_FWD_CASES(occupancy, T, smem, dev);
   if (v.split) return 1;
+  ACE_MC_FWD_CASES(occupancy, T, smem, dev);
+  if (v.mc) return 1;
   ACE_FOR_SOFT_LABELS(ACE_VARIANT_CASES(HistLauncher, occupancy, T, smem, dev));
   return 1;
 }

@@ -69,9 +69,9 @@ __device__ __forceinline__ void red_slot(unsigned a, unsigned n, unsigned r, uns
 // channel. acc layout: [3][rows][K + 1][2] (moment
 // stride `ms`), rows = b_total * CL; `row0` is the global row of loss channel 0
 // of the batch folded. `clear`: zero the table afterwards.
-template <int C, int OFF>
-__device__ __forceinline__ void fold_soft(unsigned* hist, int K, int R, unsigned long long* acc,
-                                          int64_t ms, int64_t row0, bool clear) {
+__device__ __forceinline__ void fold_soft(unsigned* hist, int C, int OFF, int K, int R,
+                                          unsigned long long* acc, int64_t ms, int64_t row0,
+                                          bool clear) {
   constexpr int NW = kSoftNW, NCT = kPipeConsumerWarps * 32;
   const int slots = (K + 1) * C * 2;
   const int gsh = R >= 4 ? 2 : (R == 2 ? 1 : 0);
@@ -120,250 +120,59 @@ __device__ __forceinline__ void fold_soft(unsigned* hist, int K, int R, unsigned
   }
 }
 
-template <typename T, int C, int OFF>
-__global__ void __launch_bounds__(kPipeThreads, 1) soft_fwd_kernel(const __grid_constant__ FwdParams P) {
-  constexpr int NCW = kPipeConsumerWarps, NT = kPipeThreads, NW = kSoftNW;
-  constexpr int TV = kPipeTileVoxels, VL = kPipeLaneVoxels;
-  constexpr unsigned XB = TV * sizeof(T);  // bytes of one logit row of a stage
-  constexpr unsigned SB = C * XB + TV * 8;  // bytes of a stage (rows, then labels)
-  static_assert(VL == 4, "lds_logits / lds_labels load four voxels");
-  extern __shared__ __align__(128) unsigned char smem_raw[];
-  __shared__ __align__(8) unsigned long long s_full[kPipeMaxStages], s_empty[kPipeMaxStages];
-  __shared__ int4 s_meta[kPipeMaxStages];  // {tile, batch, voxels, 0}; tile < 0: no more tiles
-  __shared__ volatile int s_abort;
+// Ticket of a CTA that has finished its tiles (all threads): true in the last
+// CTA to finish. The ticket is a release (this CTA's sums, ordered before it by
+// the barrier) and an acquire (the other CTAs' sums, for the last CTA).
+__device__ __forceinline__ bool last_cta_ticket(unsigned* counter) {
   __shared__ bool s_last;
-  // per interval j: {lo, span, a, b} of the last CTA's reconstruction, staged
-  // once here (indexing the parameters by a lane's own j would serialise the
-  // lanes of a warp on the constant bank)
-  __shared__ double4 s_iv[kMaxBins + 1];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  constexpr int CL = C - OFF;
-  const int K = P.tab.K, R = P.R, S = P.stages;
-  const int64_t N = P.g.N;
-  unsigned* hist = reinterpret_cast<unsigned*>(smem_raw);
-  const int table_words = (K + 1) * C * 2 * R * NW;
-  const unsigned stage0 = smem_addr(smem_raw) + (unsigned)P.table_bytes;
-  auto full_bar = [&](int s) { return smem_addr(&s_full[s]); };
-  auto empty_bar = [&](int s) { return smem_addr(&s_empty[s]); };
-  {
-    uint4* h4 = reinterpret_cast<uint4*>(hist);
-    for (int i = tid; i < table_words / 4; i += NT) h4[i] = make_uint4(0u, 0u, 0u, 0u);
-    for (int i = (table_words & ~3) + tid; i < table_words; i += NT) hist[i] = 0u;
-  }
-  for (int j = warp; j <= K; j += NT / 32) {
-    if (lane == 0) {
-      const double lo = P.tab.lohi[j].x, span = (double)P.tab.lohi[j].y - lo;
-      const double invK = 1.0 / (double)K;
-      s_iv[j] = make_double4(lo, span, invK / span, ((double)j * invK - lo) / span);
-    }
-  }
-  if (tid == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(full_bar(s), 1u);
-      mbar_init(empty_bar(s), (unsigned)NCW);
-    }
-    s_abort = 0;
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-  }
-  // programmatic dependent launch: global memory only after the previous grid
-  ace_grid_dependency_wait();
   __syncthreads();
-
-  unsigned* err = P.counter + 1;  // the workspace's error word
-  auto abort_cta = [&]() {
-    s_abort = 1;
-    atomicExch(err, 1u);
-  };
-  const int64_t mstride = (int64_t)P.B_total * CL * (K + 1) * 2;
-  const int B = P.g.B;
-  const int64_t tpb = P.wt_batch;  // tiles per batch
-
-  if (warp == NCW) {
-    // ---------------- producer (one thread) ----------------
-    if (lane == 0) {
-      const T* x = static_cast<const T*>(P.x);
-      const int64_t* lab = static_cast<const int64_t*>(P.target);
-      unsigned* ctr = P.pool_ctr;
-      int b = (int)((int64_t)blockIdx.x * B / gridDim.x);
-      unsigned pend = atomicAdd(ctr + b, 1u);  // claimed one tile ahead
-      int pend_b = b;
-      int issued = 0;
-      for (int i = 0;; ++i) {
-        const int s = i % S;
-        const unsigned use = (unsigned)(i / S);
-        int64_t tile = pend;
-        int tb = pend_b;
-        if (tile >= tpb) {  // this batch is done: take a tile of another one
-          tile = -1;
-          for (int k = 1; k < B; ++k) {
-            const int bb = (pend_b + k) % B;
-            const unsigned t2 = atomicAdd(ctr + bb, 1u);
-            if ((int64_t)t2 < tpb) {
-              tile = t2;
-              tb = bb;
-              break;
-            }
-          }
-        }
-        if (tile >= 0) {
-          pend = atomicAdd(ctr + tb, 1u);
-          pend_b = tb;
-        }
-        // the stage's previous tile must have been read
-        if (use > 0 && !mbar_wait(empty_bar(s), (use - 1) & 1u)) {
-          abort_cta();
-          break;
-        }
-        if (s_abort) break;
-        if (tile < 0) {  // no tiles left: the end marker (no copies)
-          s_meta[s] = make_int4(-1, 0, 0, 0);
-          mbar_arrive(full_bar(s));
-          break;
-        }
-        const int64_t v0 = tile * TV;
-        const int cnt = (int)min((int64_t)TV, N - v0);
-        s_meta[s] = make_int4((int)tile, tb, cnt, 0);
-        const unsigned xb = (unsigned)cnt * (unsigned)sizeof(T), lb = (unsigned)cnt * 8u;
-        mbar_arrive_tx(full_bar(s), C * xb + lb);
-        const unsigned dst = stage0 + (unsigned)s * SB;
-        const T* gx = x + (int64_t)tb * C * N + v0;
-#pragma unroll
-        for (int c = 0; c < C; ++c) bulk_load(dst + c * XB, gx + (int64_t)c * N, xb, full_bar(s));
-        bulk_load(dst + C * XB, lab + (int64_t)tb * N + v0, lb, full_bar(s));
-        issued = i + 1;
-      }
-      // After an abort no copy may still be in flight when the CTA leaves: wait
-      // (bounded) for the last fill of every stage. (Otherwise the consumers
-      // have consumed every fill before the CTA's final barrier.)
-      if (s_abort)
-        for (int i = issued - S > 0 ? issued - S : 0; i < issued; ++i)
-          mbar_wait(full_bar(i % S), (unsigned)(i / S) & 1u);
-    }
-  } else {
-    // ---------------- consumers ----------------
-    // Shared byte address of row c, flag 0, of the interval whose rounding
-    // pattern is t (bits(t) - magic = j): bits(t) * A + base[c] (mod 2^32).
-    const unsigned sb = (unsigned)(R * NW * 4);  // bytes of one slot (all replicas)
-    const unsigned A = 2u * C * sb;               // bytes of one interval
-    unsigned base[C];
-    {
-      const unsigned t0 =
-          smem_addr(hist) + (unsigned)((lane & (R - 1)) * NW * 4) - kFixMagicBits * A;
-#pragma unroll
-      for (int c = 0; c < C; ++c) base[c] = t0 + (unsigned)c * 2u * sb;
-    }
-    const float Kf = (float)K, KfS = (float)K * kSoftRScale;
-    const int vo = (warp * 32 + lane) * VL;  // this lane's first voxel of a tile
-    int cur_b = -1, since = 0;
-    for (int i = 0;; ++i) {
-      const int s = i % S;
-      if (!mbar_wait(full_bar(s), (unsigned)(i / S) & 1u)) {
-        abort_cta();
-        break;
-      }
-      const int4 m = s_meta[s];
-      if (m.x < 0 || s_abort) break;
-      if (m.y != cur_b || since == P.epoch) {
-        // a new batch, or the 32-bit words' range: fold the table first
-        if (cur_b >= 0) {
-          consumer_sync();
-          fold_soft<C, OFF>(hist, K, R, P.iacc, mstride, (int64_t)(P.b_offset + cur_b) * CL, true);
-          consumer_sync();
-        }
-        cur_b = m.y;
-        since = 0;
-      }
-      ++since;
-      const unsigned st = stage0 + (unsigned)s * SB;
-      float xv[C][4];
-      int lab[4];
-#pragma unroll
-      for (int c = 0; c < C; ++c) lds_logits<T>(st + c * XB + vo * (unsigned)sizeof(T), xv[c]);
-      lds_labels(st + C * XB + vo * 8u, lab);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(empty_bar(s));  // the stage may be refilled now
-      if (vo >= m.z) continue;                    // past the batch's last voxel
-      // Two voxels at a time: the fp32 arithmetic runs as packed pairs
-      // (__ffma2_rn / __fmul2_rn / __fadd2_rn, one instruction for both voxels,
-      // each element rounded as its scalar form), the rest per voxel.
-#pragma unroll
-      for (int v = 0; v < VL; v += 2) {
-        // softmax: exp(x - m) = 2^(x log2 e - m log2 e) (ace_softmax_fast)
-        float2 xp[C], e[C];
-#pragma unroll
-        for (int c = 0; c < C; ++c) xp[c] = make_float2(xv[c][v], xv[c][v + 1]);
-        float2 mx = xp[0];
-#pragma unroll
-        for (int c = 1; c < C; ++c) mx = make_float2(fmaxf(mx.x, xp[c].x), fmaxf(mx.y, xp[c].y));
-        const float2 nmL = __fmul2_rn(mx, make_float2(-kLog2e, -kLog2e));
-        float2 sum;
-#pragma unroll
-        for (int c = 0; c < C; ++c) {
-          const float2 arg = __ffma2_rn(xp[c], make_float2(kLog2e, kLog2e), nmL);
-          e[c] = make_float2(ace_exp2_approx(arg.x), ace_exp2_approx(arg.y));
-          sum = c == 0 ? e[0] : __fadd2_rn(sum, e[c]);
-        }
-        const float2 y = make_float2(ace_rcp_approx(sum.x), ace_rcp_approx(sum.y));
-#pragma unroll
-        for (int c = OFF; c < C; ++c) {
-          // p in [0, 1] (NaN -> 0); t = magic + j, j = round(p K) in [0, K]
-          const float2 p = make_float2(__saturatef(__fmul_rn(e[c].x, y.x)),
-                                       __saturatef(__fmul_rn(e[c].y, y.y)));
-          const float2 t = __ffma2_rn(p, make_float2(Kf, Kf), make_float2(kFixMagic, kFixMagic));
-          // rs = (p K - j) 2^22, exact before its one rounding (|rs| <= 2^21)
-          const float2 mj = __ffma2_rn(t, make_float2(-kSoftRScale, -kSoftRScale),
-                                       make_float2(kFixMagic * kSoftRScale, kFixMagic * kSoftRScale));
-          const float2 rs = __ffma2_rn(p, make_float2(KfS, KfS), mj);
-          // magic + round(rs); magic + round(r^2 2^23) = magic + round(rs^2 2^-21)
-          const float2 rw = __fadd2_rn(rs, make_float2(kFixMagic, kFixMagic));
-          const float2 q = __ffma2_rn(
-              rs, __fmul2_rn(rs, make_float2(1.0f / kFixScale, 1.0f / kFixScale)),
-              make_float2(kFixMagic, kFixMagic));
-          unsigned a0 = __float_as_uint(t.x) * A + base[c];
-          unsigned a1 = __float_as_uint(t.y) * A + base[c];
-          if (lab[v] == c) a0 += sb;
-          if (lab[v + 1] == c) a1 += sb;
-          red_slot(a0, 1u, __float_as_uint(rw.x), __float_as_uint(q.x));
-          red_slot(a1, 1u, __float_as_uint(rw.y), __float_as_uint(q.y));
-        }
-      }
-    }
-    consumer_sync();
-    if (cur_b >= 0)
-      fold_soft<C, OFF>(hist, K, R, P.iacc, mstride, (int64_t)(P.b_offset + cur_b) * CL, false);
-  }
-
-  ace_launch_dependents();  // a dependent launch may begin its own setup now
-  __syncthreads();
-  if (tid == 0) {
-    // The ticket is a release (this CTA's sums, ordered before it by the
-    // barrier) and an acquire (the other CTAs' sums, for the last CTA).
+  if (threadIdx.x == 0) {
     unsigned done;
     asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
                  : "=r"(done)
-                 : "l"(P.counter)
+                 : "l"(counter)
                  : "memory");
     s_last = (done == gridDim.x - 1);
   }
   __syncthreads();
-  if (!s_last) return;
+  return s_last;
+}
 
-  // Last CTA, one warp per row r: lane l takes bins k = l + 32 q. W, P, G of bin k
-  // come from the slots of intervals k and k + 1 (flags 0 and 1). Interval j in
-  // 1..K-1, between lo = c_{j-1} and lo + S = c_j: with r = p K - j, the
-  // reference's right-bin weight is u = (p - lo) / S = a r + b, a = 1 / (K S),
-  // b = (j / K - lo) / S (s_iv), so sum u = a R1 + b n and
-  // sum u^2 = a^2 R2 + 2 a b R1 + b^2 n. Bin j gets the u share, W += sum u,
-  // P += lo sum u + S sum u^2, G += the flag-1 slot's sum u; bin j - 1 the 1 - u
-  // share, W += n - sum u, P += lo n + S sum u - (lo sum u + S sum u^2), G += the
-  // flag-1 n - sum u. The end intervals (j = 0, K) give all of n,
-  // sum p = (R1 + j n) / K and the flag-1 n to bins 0 and K - 1, as the
-  // reference's two scatters. The warp then zeroes the row's accumulators and,
-  // when the epilogue is fused, runs the row's epilogue from registers.
-  const int rows = P.B_total * CL;
+// Interval constants of soft_finish, per interval j: {lo, span, a, b} (one warp
+// lane per interval: indexing the parameters by a lane's own j would serialise
+// the lanes of a warp on the constant bank).
+__device__ __forceinline__ void stage_soft_intervals(const BinTable& tab, double4* s_iv) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, K = tab.K;
+  for (int j = warp; j <= K; j += blockDim.x / 32) {
+    if (lane == 0) {
+      const double lo = tab.lohi[j].x, span = (double)tab.lohi[j].y - lo;
+      const double invK = 1.0 / (double)K;
+      s_iv[j] = make_double4(lo, span, invK / span, ((double)j * invK - lo) / span);
+    }
+  }
+}
+
+// The last CTA of soft_fwd_kernel and mc_fwd_kernel (soft binning; all threads of
+// the CTA), one warp per row r: lane l takes bins k = l + 32 q. W, P, G of bin k
+// come from the slots of intervals k and k + 1 (flags 0 and 1). Interval j in
+// 1..K-1, between lo = c_{j-1} and lo + S = c_j: with r = p K - j, the
+// reference's right-bin weight is u = (p - lo) / S = a r + b, a = 1 / (K S),
+// b = (j / K - lo) / S (s_iv), so sum u = a R1 + b n and
+// sum u^2 = a^2 R2 + 2 a b R1 + b^2 n. Bin j gets the u share, W += sum u,
+// P += lo sum u + S sum u^2, G += the flag-1 slot's sum u; bin j - 1 the 1 - u
+// share, W += n - sum u, P += lo n + S sum u - (lo sum u + S sum u^2), G += the
+// flag-1 n - sum u. The end intervals (j = 0, K) give all of n,
+// sum p = (R1 + j n) / K and the flag-1 n to bins 0 and K - 1, as the
+// reference's two scatters. The warp then zeroes the row's accumulators and,
+// when the epilogue is fused, runs the row's epilogue from registers.
+__device__ __forceinline__ void soft_finish(const FwdParams& P, const double4* s_iv) {
+  constexpr int NT = kPipeThreads;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int K = P.tab.K;
+  const int rows = P.B_total * P.g.CL;
+  const int64_t m = (int64_t)rows * (K + 1) * 2;  // moment stride of the workspace sums
+  unsigned* err = P.counter + 1;
   const int64_t stat_stride = (int64_t)rows * K;
-  const int64_t m = mstride;
   unsigned long long* acc = P.iacc;
   const double ur = 1.0 / (double)kSoftRScale, uq = ur * 0.5, invK = 1.0 / (double)K;
   const bool failed = __ldcg(err) != 0u;  // a CTA's wait ran out: the sums are incomplete
@@ -437,13 +246,166 @@ __global__ void __launch_bounds__(kPipeThreads, 1) soft_fwd_kernel(const __grid_
         for (int f = 0; f < 2; ++f) __stcg(acc + o * m + row_slot + 2 * j + f, 0ull);
     if (P.do_epilogue) mine = ACE_FADD(mine, epilogue_row(P.epi, r, wv, pv, gv));
   }
-  for (int i = tid; i < B; i += NT) P.pool_ctr[i] = 0u;
+  for (int i = tid; i < P.g.B; i += NT) P.pool_ctr[i] = 0u;
   if (P.do_epilogue) write_loss_if0(P.epi, cta_sum_in_warp_order(mine));
   __syncthreads();
   if (tid == 0) {
     *err = 0u;
     *P.counter = 0u;
   }
+}
+
+template <typename T, int C, int OFF>
+__global__ void __launch_bounds__(kPipeThreads, 1) soft_fwd_kernel(const __grid_constant__ FwdParams P) {
+  constexpr int NCW = kPipeConsumerWarps, NT = kPipeThreads, NW = kSoftNW;
+  constexpr int TV = kPipeTileVoxels, VL = kPipeLaneVoxels;
+  constexpr unsigned XB = TV * sizeof(T);  // bytes of one logit row of a stage
+  constexpr unsigned SB = C * XB + TV * 8;  // bytes of a stage (rows, then labels)
+  static_assert(VL == 4, "lds_logits / lds_labels load four voxels");
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  __shared__ __align__(8) unsigned long long s_full[kPipeMaxStages], s_empty[kPipeMaxStages];
+  __shared__ int4 s_meta[kPipeMaxStages];  // {tile, batch, voxels, 0}; tile < 0: no more tiles
+  __shared__ volatile int s_abort;
+  __shared__ double4 s_iv[kMaxBins + 1];  // soft_finish's interval constants
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int CL = C - OFF;
+  const int K = P.tab.K, R = P.R, S = P.stages;
+  const int64_t N = P.g.N;
+  unsigned* hist = reinterpret_cast<unsigned*>(smem_raw);
+  const int table_words = (K + 1) * C * 2 * R * NW;
+  const unsigned stage0 = smem_addr(smem_raw) + (unsigned)P.table_bytes;
+  auto full_bar = [&](int s) { return smem_addr(&s_full[s]); };
+  auto empty_bar = [&](int s) { return smem_addr(&s_empty[s]); };
+  {
+    uint4* h4 = reinterpret_cast<uint4*>(hist);
+    for (int i = tid; i < table_words / 4; i += NT) h4[i] = make_uint4(0u, 0u, 0u, 0u);
+    for (int i = (table_words & ~3) + tid; i < table_words; i += NT) hist[i] = 0u;
+  }
+  stage_soft_intervals(P.tab, s_iv);
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full_bar(s), 1u);
+      mbar_init(empty_bar(s), (unsigned)NCW);
+    }
+    s_abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  // programmatic dependent launch: global memory only after the previous grid
+  ace_grid_dependency_wait();
+  __syncthreads();
+
+  unsigned* err = P.counter + 1;  // the workspace's error word
+  auto abort_cta = [&]() {
+    s_abort = 1;
+    atomicExch(err, 1u);
+  };
+  const int64_t mstride = (int64_t)P.B_total * CL * (K + 1) * 2;
+  const int B = P.g.B;
+  const int64_t tpb = P.wt_batch;  // tiles per batch
+
+  if (warp == NCW) {
+    // ---------------- producer (one thread) ----------------
+    if (lane == 0)
+      produce_claimed<T, TV>(static_cast<const T*>(P.x), static_cast<const int64_t*>(P.target), C,
+                             N, B, tpb, P.pool_ctr, stage0, SB, S, s_full, s_empty, s_meta,
+                             &s_abort, err);
+  } else {
+    // ---------------- consumers ----------------
+    // Shared byte address of row c, flag 0, of the interval whose rounding
+    // pattern is t (bits(t) - magic = j): bits(t) * A + base[c] (mod 2^32).
+    const unsigned sb = (unsigned)(R * NW * 4);  // bytes of one slot (all replicas)
+    const unsigned A = 2u * C * sb;               // bytes of one interval
+    unsigned base[C];
+    {
+      const unsigned t0 =
+          smem_addr(hist) + (unsigned)((lane & (R - 1)) * NW * 4) - kFixMagicBits * A;
+#pragma unroll
+      for (int c = 0; c < C; ++c) base[c] = t0 + (unsigned)c * 2u * sb;
+    }
+    const float Kf = (float)K, KfS = (float)K * kSoftRScale;
+    const int vo = (warp * 32 + lane) * VL;  // this lane's first voxel of a tile
+    int cur_b = -1, since = 0;
+    for (int i = 0;; ++i) {
+      const int s = i % S;
+      if (!mbar_wait(full_bar(s), (unsigned)(i / S) & 1u)) {
+        abort_cta();
+        break;
+      }
+      const int4 m = s_meta[s];
+      if (m.x < 0 || s_abort) break;
+      if (m.y != cur_b || since == P.epoch) {
+        // a new batch, or the 32-bit words' range: fold the table first
+        if (cur_b >= 0) {
+          consumer_sync();
+          fold_soft(hist, C, OFF, K, R, P.iacc, mstride, (int64_t)(P.b_offset + cur_b) * CL, true);
+          consumer_sync();
+        }
+        cur_b = m.y;
+        since = 0;
+      }
+      ++since;
+      const unsigned st = stage0 + (unsigned)s * SB;
+      float xv[C][4];
+      int lab[4];
+#pragma unroll
+      for (int c = 0; c < C; ++c) lds_logits<T>(st + c * XB + vo * (unsigned)sizeof(T), xv[c]);
+      lds_labels(st + C * XB + vo * 8u, lab);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty_bar(s));  // the stage may be refilled now
+      if (vo >= m.z) continue;                    // past the batch's last voxel
+      // Two voxels at a time: the fp32 arithmetic runs as packed pairs
+      // (__ffma2_rn / __fmul2_rn / __fadd2_rn, one instruction for both voxels,
+      // each element rounded as its scalar form), the rest per voxel.
+#pragma unroll
+      for (int v = 0; v < VL; v += 2) {
+        // softmax: exp(x - m) = 2^(x log2 e - m log2 e) (ace_softmax_fast)
+        float2 xp[C], e[C];
+#pragma unroll
+        for (int c = 0; c < C; ++c) xp[c] = make_float2(xv[c][v], xv[c][v + 1]);
+        float2 mx = xp[0];
+#pragma unroll
+        for (int c = 1; c < C; ++c) mx = make_float2(fmaxf(mx.x, xp[c].x), fmaxf(mx.y, xp[c].y));
+        const float2 nmL = __fmul2_rn(mx, make_float2(-kLog2e, -kLog2e));
+        float2 sum;
+#pragma unroll
+        for (int c = 0; c < C; ++c) {
+          const float2 arg = __ffma2_rn(xp[c], make_float2(kLog2e, kLog2e), nmL);
+          e[c] = make_float2(ace_exp2_approx(arg.x), ace_exp2_approx(arg.y));
+          sum = c == 0 ? e[0] : __fadd2_rn(sum, e[c]);
+        }
+        const float2 y = make_float2(ace_rcp_approx(sum.x), ace_rcp_approx(sum.y));
+#pragma unroll
+        for (int c = OFF; c < C; ++c) {
+          // p in [0, 1] (NaN -> 0); t = magic + j, j = round(p K) in [0, K]
+          const float2 p = make_float2(__saturatef(__fmul_rn(e[c].x, y.x)),
+                                       __saturatef(__fmul_rn(e[c].y, y.y)));
+          const float2 t = __ffma2_rn(p, make_float2(Kf, Kf), make_float2(kFixMagic, kFixMagic));
+          // rs = (p K - j) 2^22, exact before its one rounding (|rs| <= 2^21)
+          const float2 mj = __ffma2_rn(t, make_float2(-kSoftRScale, -kSoftRScale),
+                                       make_float2(kFixMagic * kSoftRScale, kFixMagic * kSoftRScale));
+          const float2 rs = __ffma2_rn(p, make_float2(KfS, KfS), mj);
+          // magic + round(rs); magic + round(r^2 2^23) = magic + round(rs^2 2^-21)
+          const float2 rw = __fadd2_rn(rs, make_float2(kFixMagic, kFixMagic));
+          const float2 q = __ffma2_rn(
+              rs, __fmul2_rn(rs, make_float2(1.0f / kFixScale, 1.0f / kFixScale)),
+              make_float2(kFixMagic, kFixMagic));
+          unsigned a0 = __float_as_uint(t.x) * A + base[c];
+          unsigned a1 = __float_as_uint(t.y) * A + base[c];
+          if (lab[v] == c) a0 += sb;
+          if (lab[v + 1] == c) a1 += sb;
+          red_slot(a0, 1u, __float_as_uint(rw.x), __float_as_uint(q.x));
+          red_slot(a1, 1u, __float_as_uint(rw.y), __float_as_uint(q.y));
+        }
+      }
+    }
+    consumer_sync();
+    if (cur_b >= 0)
+      fold_soft(hist, C, OFF, K, R, P.iacc, mstride, (int64_t)(P.b_offset + cur_b) * CL, false);
+  }
+
+  ace_launch_dependents();  // a dependent launch may begin its own setup now
+  if (last_cta_ticket(P.counter)) soft_finish(P, s_iv);
 }
 
 }  // namespace ace

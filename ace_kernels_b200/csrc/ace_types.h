@@ -79,13 +79,16 @@ struct FwdParams {
   int b_offset;        // first statistics row of this launch
   int B_total;
   double* accum;       // workspace: [NOUT, B_total, CL, slots] sums (self-cleaning)
-  // soft_fwd_kernel only (the same workspace bytes as accum):
-  unsigned long long* iacc;  // [3, B_total, CL, K + 1, 2] integer moments (self-cleaning)
+  // the pipelined kernels (soft_fwd_kernel, mc_fwd_kernel) only (the same
+  // workspace bytes as accum):
+  unsigned long long* iacc;  // integer sums (self-cleaning): soft [3, B_total, CL, K + 1, 2],
+                             // mc_fwd_kernel hard [3, B_total, CL, K]
   unsigned* pool_ctr;  // [B] tile-claim counters, one per batch (self-cleaning)
-  int64_t wt_batch;    // tiles (kSoftTileVoxels voxels) per batch
+  int64_t wt_batch;    // tiles per batch
   int epoch;           // tiles a CTA adds between two folds (32-bit word range)
-  int stages;          // shared-memory ring stages (<= kSoftMaxStages)
+  int stages;          // shared-memory ring stages (<= kPipeMaxStages)
   int table_bytes;     // shared-memory bytes of the statistics table (128-aligned)
+  int stage_offset;    // shared-memory byte offset of the ring (128-aligned)
   unsigned* counter;   // workspace: finished-CTA counter, then an error word (self-cleaning)
   float* hist_out;     // [3, B_total, CL, K] statistics (W, P, G)
   int do_epilogue;

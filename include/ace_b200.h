@@ -236,6 +236,8 @@ const char* ace_b200_last_error(void);
 #define ACE_B200_KERNEL_SOFT_PIPE 1 /* soft_fwd_kernel: pipelined soft forward */
 #define ACE_B200_KERNEL_GRAD 2      /* grad_kernel: generic backward */
 #define ACE_B200_KERNEL_GRAD_PIPE 3 /* grad_tma_kernel: pipelined backward */
+#define ACE_B200_KERNEL_MC_PIPE 4   /* mc_fwd_kernel: pipelined many-channel forward */
+#define ACE_B200_KERNEL_MC_GRAD 5   /* mc_grad_kernel: pipelined many-channel backward */
 typedef struct ace_b200_plan {
   int32_t kernel;
   int32_t ctas;

@@ -6,9 +6,10 @@ the oracle.
   starts its CTAs spread over the batches and lets a CTA whose batch is done take
   another batch's tiles (a fold of its table in between). Batch counts that do not
   divide the CTAs, and batches of very different lengths in tiles, make CTAs move.
-- The generic forward (``hist_kernel``) splits the tiles of all batches flat when
-  per-batch chunks would leave SMs idle; a CTA's run then crosses a batch
-  boundary. The shapes below include one that takes the flat split.
+- The generic forward (``hist_kernel``, here with dense targets) splits the
+  tiles of all batches flat when per-batch chunks would leave SMs idle; a CTA's
+  run then crosses a batch boundary. The shapes below include one that takes the
+  flat split.
 - The pipelined backward takes softmax cases with at most four channels.
 """
 
@@ -103,11 +104,12 @@ def _flat_shapes() -> list[tuple[int, int, tuple[int, ...]]]:
 
 def test_hard_forward_takes_a_flat_split_and_matches() -> None:
     """hist_kernel's flat split (CTA runs that cross batches) is taken for one of
-    these shapes, whatever the occupancy; all of them are bit-exact in W and G."""
-    cfg = to_config({"binning": "hard", "to_onehot_y": True})
+    these shapes, whatever the occupancy; all of them are bit-exact in W and G.
+    (Dense one-hot targets: with labels, hard binning runs mc_fwd_kernel.)"""
+    cfg = to_config({"binning": "hard"})
     crossed = []
     for i, (b, c, spatial) in enumerate(_flat_shapes()):
-        x, y = make(Spec(b, c, spatial, seed=20 + i), 20, "cuda")
+        x, y = make(Spec(b, c, spatial, seed=20 + i, labels_as_index=False), 20, "cuda")
         plan = _check_stats(x, y, cfg)
         assert plan.kernel == _lib.KERNEL_HIST
         crossed.append((plan.ctas, plan.crosses_batches))
@@ -120,10 +122,13 @@ def test_backward_kernel_choice() -> None:
     for binning in ("hard", "soft"):
         cfg = to_config({"binning": binning, "to_onehot_y": True})
         assert backward_plan(x, y, cfg).kernel == _lib.KERNEL_GRAD_PIPE
-    # more than four channels, or sigmoid with dense soft targets: the generic kernel
+    # 5..24 channels: the many-channel pipeline; more, or sigmoid with dense soft
+    # targets: the generic kernel
     x8, y8 = make(Spec(2, 8, (16, 16, 16), seed=3), 20, "cuda")
     cfg8 = to_config({"binning": "soft", "to_onehot_y": True})
-    assert backward_plan(x8, y8, cfg8).kernel == _lib.KERNEL_GRAD
+    assert backward_plan(x8, y8, cfg8).kernel == _lib.KERNEL_MC_GRAD
+    x30, y30 = make(Spec(2, 30, (16, 16, 16), seed=3), 20, "cuda")
+    assert backward_plan(x30, y30, cfg8).kernel == _lib.KERNEL_GRAD
     xs, ys = make(Spec(2, 1, (16, 16, 16), seed=3, labels_as_index=False), 20, "cuda")
     cfgs = to_config({"binning": "soft", "activation": "sigmoid"})
     assert backward_plan(xs, ys, cfgs).kernel == _lib.KERNEL_GRAD
