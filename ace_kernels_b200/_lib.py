@@ -90,6 +90,18 @@ class EpilogueOut(Structure):
     ]
 
 
+MAX_PEERS = 8
+IPC_HANDLE_BYTES = 64
+
+
+class Exchange(Structure):
+    _fields_ = [
+        ("world", c_int32),
+        ("rank", c_int32),
+        ("mailbox", c_void_p * MAX_PEERS),
+    ]
+
+
 # (name, restype, argtypes) of every exported symbol.
 SIGNATURES: list[tuple[str, object, list[object]]] = [
     ("ace_b200_workspace_bytes", c_size_t, [c_int64, c_int64, c_int32]),
@@ -129,6 +141,18 @@ SIGNATURES: list[tuple[str, object, list[object]]] = [
             c_void_p,
         ],
     ),
+    (
+        "ace_b200_forward_exchange",
+        c_int,
+        [POINTER(Inputs), POINTER(Options), c_void_p, EpilogueOut, c_void_p, c_size_t,
+         POINTER(Exchange), c_void_p],
+    ),
+    ("ace_b200_mailbox_bytes", c_size_t, [c_int64, c_int64, c_int32, c_int32]),
+    ("ace_b200_mailbox_alloc", c_int, [c_size_t, POINTER(c_void_p)]),
+    ("ace_b200_mailbox_free", c_int, [c_void_p]),
+    ("ace_b200_ipc_handle", c_int, [c_void_p, c_void_p]),
+    ("ace_b200_ipc_open", c_int, [c_void_p, POINTER(c_void_p)]),
+    ("ace_b200_ipc_close", c_int, [c_void_p]),
     ("ace_b200_probs", c_int, [POINTER(Inputs), c_int32, c_void_p, c_void_p]),
     ("ace_b200_bin_table", c_int, [c_int32, c_int32, POINTER(c_float)]),
     (

@@ -474,8 +474,13 @@ bool mc_fwd_setup(const ace_b200_inputs* in, const ace_b200_options* opt, Varian
   return true;
 }
 
+size_t mailbox_slot_bytes(int64_t b_total, int64_t cl, int K) {
+  return round_up(16 + (size_t)12 * b_total * cl * K, 16);
+}
+
 int hist_impl(const ace_b200_inputs* in, const ace_b200_options* opt, float* hist,
-              const ace_b200_epilogue_out* out, void* workspace, size_t ws_bytes, void* stream) {
+              const ace_b200_epilogue_out* out, void* workspace, size_t ws_bytes, void* stream,
+              const ace_b200_exchange* xchg = nullptr) {
   int CL = 0;
   int rc = check_common(in, opt, CL);
   if (rc) return rc;
@@ -509,6 +514,21 @@ int hist_impl(const ace_b200_inputs* in, const ace_b200_options* opt, float* his
   p.hist_out = hist;
   build_table(K, soft, opt->right != 0, p.tab);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  p.xchg.world = 1;
+  const bool multi = xchg && xchg->world > 1;
+  if (multi) {
+    if (!out) return fail(ACE_B200_EINVAL, "the exchange needs the epilogue outputs");
+    if (xchg->world > kMaxPeers || xchg->rank < 0 || xchg->rank >= xchg->world)
+      return fail(ACE_B200_EINVAL, "bad exchange world=%d rank=%d", xchg->world, xchg->rank);
+    p.xchg.world = xchg->world;
+    p.xchg.rank = xchg->rank;
+    p.xchg.slot_bytes = (int64_t)mailbox_slot_bytes(in->b_total, CL, K);
+    for (int r = 0; r < xchg->world; ++r) {
+      if (!xchg->mailbox[r] || !aligned(xchg->mailbox[r], 16))
+        return fail(ACE_B200_EINVAL, "mailbox %d is null or misaligned", r);
+      p.xchg.mailbox[r] = static_cast<unsigned char*>(xchg->mailbox[r]);
+    }
+  }
 
   // Soft binning with labels and a softmax over <= 4 channels: soft_fwd_kernel.
   // Its interval distances use the true centres: `right` only decides ties of p
@@ -518,6 +538,8 @@ int hist_impl(const ace_b200_inputs* in, const ace_b200_options* opt, float* his
   int soft_smem = 0;
   dim3 soft_grid;
   if (v.split) v.split = soft_fwd_setup(in, opt, v, p, w, dev, out != nullptr, soft_smem, soft_grid);
+  if (v.split && multi && !p.do_epilogue)
+    return fail(ACE_B200_EUNSUPPORTED, "the exchange needs the epilogue in the forward (<= 256 rows)");
   if (v.split) {
     build_table(K, true, false, p.tab);
     e = launch_hist_any(p, v, soft_grid, soft_smem, in->x_dtype, s, dev);
@@ -538,6 +560,8 @@ int hist_impl(const ace_b200_inputs* in, const ace_b200_options* opt, float* his
   int mc_smem = 0;
   dim3 mc_grid;
   if (mc_fwd_setup(in, opt, v, p, w, dev, out != nullptr, mc_smem, mc_grid)) {
+    if (multi && !p.do_epilogue)
+      return fail(ACE_B200_EUNSUPPORTED, "the exchange needs the epilogue in the forward (<= 256 rows)");
     e = launch_hist_any(p, v, mc_grid, mc_smem, in->x_dtype, s, dev);
     if (e != cudaSuccess) return cuda_fail(e, "many-channel histogram kernel launch");
     set_plan(ACE_B200_KERNEL_MC_PIPE, mc_grid.x, in->B > 1, p.stages, p.R, p.do_epilogue,
@@ -548,6 +572,11 @@ int hist_impl(const ace_b200_inputs* in, const ace_b200_options* opt, float* his
     }
     return ACE_B200_OK;
   }
+
+  if (multi)
+    return fail(ACE_B200_EUNSUPPORTED,
+                "the exchange runs in the pipelined forwards only (labels and a softmax; soft "
+                "binning, or %d..%d channels)", kMcMinChannels, kMcMaxChannels);
 
   // hist_kernel. Shared-memory table: `entries` words per lane replica. A 32-bit
   // word of a replica takes at most (threads / R) * V additions per tile and must
@@ -692,6 +721,60 @@ int ace_b200_forward(const ace_b200_inputs* in, const ace_b200_options* opt, flo
                      ace_b200_epilogue_out out, void* workspace, size_t workspace_bytes,
                      void* stream) {
   return hist_impl(in, opt, hist, &out, workspace, workspace_bytes, stream);
+}
+
+size_t ace_b200_mailbox_bytes(int64_t b_total, int64_t cl, int32_t num_bins, int32_t world) {
+  if (b_total < 1 || cl < 1 || num_bins < 1 || world < 1) return 0;
+  return (size_t)kXchgHeaderBytes + 2 * (size_t)world * mailbox_slot_bytes(b_total, cl, num_bins);
+}
+
+int ace_b200_mailbox_alloc(size_t bytes, void** ptr_out) {
+  if (!ptr_out || bytes == 0) return fail(ACE_B200_EINVAL, "null pointer or zero bytes");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc of the mailbox");
+  e = cudaMemset(p, 0, bytes);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "cudaMemset of the mailbox");
+  }
+  *ptr_out = p;
+  return ACE_B200_OK;
+}
+
+int ace_b200_mailbox_free(void* ptr) {
+  cudaError_t e = cudaFree(ptr);
+  return e == cudaSuccess ? ACE_B200_OK : cuda_fail(e, "cudaFree of the mailbox");
+}
+
+int ace_b200_ipc_handle(void* ptr, void* handle_out) {
+  static_assert(sizeof(cudaIpcMemHandle_t) == ACE_B200_IPC_HANDLE_BYTES, "IPC handle size");
+  if (!ptr || !handle_out) return fail(ACE_B200_EINVAL, "null pointer");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, ptr);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+  memcpy(handle_out, &h, sizeof(h));
+  return ACE_B200_OK;
+}
+
+int ace_b200_ipc_open(const void* handle, void** ptr_out) {
+  if (!handle || !ptr_out) return fail(ACE_B200_EINVAL, "null pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(ptr_out, h, cudaIpcMemLazyEnablePeerAccess);
+  return e == cudaSuccess ? ACE_B200_OK : cuda_fail(e, "cudaIpcOpenMemHandle");
+}
+
+int ace_b200_ipc_close(void* ptr) {
+  cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  return e == cudaSuccess ? ACE_B200_OK : cuda_fail(e, "cudaIpcCloseMemHandle");
+}
+
+int ace_b200_forward_exchange(const ace_b200_inputs* in, const ace_b200_options* opt, float* hist,
+                              ace_b200_epilogue_out out, void* workspace, size_t workspace_bytes,
+                              const ace_b200_exchange* xchg, void* stream) {
+  if (!xchg) return fail(ACE_B200_EINVAL, "null exchange");
+  return hist_impl(in, opt, hist, &out, workspace, workspace_bytes, stream, xchg);
 }
 
 int ace_b200_forward_static(const ace_b200_inputs* in, const ace_b200_options* opt, float* hist,

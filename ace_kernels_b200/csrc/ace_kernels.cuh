@@ -759,6 +759,7 @@ __global__ void __launch_bounds__(kHistThreads) hist_kernel(const __grid_constan
 }  // namespace ace
 
 #include "ace_tma.cuh"       // pipeline primitives
+#include "ace_xchg.cuh"      // statistics exchange between ranks (multi-rank forwards)
 #include "ace_soft_fwd.cuh"  // soft_fwd_kernel (uses the helpers above)
 #include "ace_mc_fwd.cuh"    // mc_fwd_kernel (uses soft_fwd_kernel's pipeline)
 

@@ -167,8 +167,9 @@ __device__ __forceinline__ void hard_finish(const FwdParams& P) {
       P.hist_out[m + e] = pv[qq];
       P.hist_out[2 * m + e] = gv[qq];
     }
-    if (P.do_epilogue) mine = ACE_FADD(mine, epilogue_row(P.epi, r, wv, pv, gv));
+    if (P.do_epilogue && P.xchg.world == 1) mine = ACE_FADD(mine, epilogue_row(P.epi, r, wv, pv, gv));
   }
+  if (P.xchg.world > 1) mine = exchange_and_epilogue(P);
   for (int i = tid; i < P.g.B; i += NT) P.pool_ctr[i] = 0u;
   if (P.do_epilogue) write_loss_if0(P.epi, cta_sum_in_warp_order(mine));
   __syncthreads();

@@ -68,6 +68,15 @@ struct EpiParams {
   float* loss;         // [1]
 };
 
+// Statistics exchange between ranks inside the forward (ace_b200_forward_exchange).
+constexpr int kMaxPeers = ACE_B200_MAX_PEERS;
+struct XchgParams {
+  int world;                         // 1: no exchange
+  int rank;
+  int64_t slot_bytes;                // bytes of one rank's slot in a mailbox
+  unsigned char* mailbox[kMaxPeers];  // every rank's mailbox, mapped in this process
+};
+
 struct FwdParams {
   const void* x;       // [B, C, N] logits / probabilities (fp32, bf16, fp16)
   const void* target;  // [B, N] int64 labels or [B, C, N] fp32 dense targets
@@ -94,6 +103,7 @@ struct FwdParams {
   int do_epilogue;
   BinTable tab;
   EpiParams epi;
+  XchgParams xchg;
 };
 
 struct BwdParams {

@@ -6,10 +6,15 @@ index of its first sample, ``b_total`` = global batch) or, with ``b_offset=0`` a
 
 1. the fused histogram kernel writes this rank's partial W/P/G into a full
    ``[3, b_total, C', K]`` fp32 buffer (zeros in rows it does not hold);
-2. one NCCL all-reduce (sum) of that buffer over NVLink: the only exchange
-   (7.7 KB for an 8 x 4-channel batch at K = 20);
+2. the ranks' buffers are summed: inside the forward kernel when it is one of
+   the pipelined kernels (``ace_b200_forward_exchange``: the last CTA of each
+   rank stores its rows into every rank's mailbox over NVLink, waits for the
+   others' and adds them in rank order, mailboxes mapped through CUDA IPC by
+   ``PeerExchange``), else by one NCCL all-reduce over NVLink (7.7 KB for an
+   8 x 4-channel batch at K = 20);
 3. every rank runs the same epilogue on the global statistics (the "mean"
-   divides by the global b_total * C'), so all ranks hold the same loss;
+   divides by the global b_total * C'), so all ranks hold the same loss: in the
+   same kernel after the in-kernel exchange, else as a second launch;
 4. the backward is local: each rank's gradient for its own voxels, using the
    global ``coef`` / ``d`` / ``jac`` rows of its samples.
 
@@ -71,18 +76,93 @@ def _cuda_backward(args: KernelArgs, out: Any, grad: torch.Tensor) -> torch.Tens
     return run_backward(args, coef, d, jac, grad)
 
 
+class PeerExchange:
+    """The mailboxes of the in-kernel exchange for one process group and one
+    statistics shape: this rank's (``ace_b200_mailbox_alloc``) and every other
+    rank's, mapped from the CUDA IPC handles gathered over the group. Made by
+    every rank together (the gather is a collective), once per shape."""
+
+    def __init__(self, device: torch.device, group: Any, b_total: int, cl: int, k: int) -> None:
+        lib = _lib.load()
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > _lib.MAX_PEERS:
+            raise ValueError(f"the in-kernel exchange takes at most {_lib.MAX_PEERS} ranks")
+        nbytes = lib.ace_b200_mailbox_bytes(b_total, cl, k, self.world)
+        own = ctypes.c_void_p()
+        handle = (ctypes.c_char * _lib.IPC_HANDLE_BYTES)()
+        with torch.cuda.device(device):
+            _lib.check(lib.ace_b200_mailbox_alloc(nbytes, ctypes.byref(own)), "ace_b200_mailbox_alloc")
+            _lib.check(lib.ace_b200_ipc_handle(own, handle), "ace_b200_ipc_handle")
+        handles: list[Any] = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.struct = _lib.Exchange(world=self.world, rank=self.rank)
+        self.mapped: list[int] = []
+        with torch.cuda.device(device):
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    self.struct.mailbox[r] = own.value
+                    continue
+                ptr = ctypes.c_void_p()
+                buf = ctypes.create_string_buffer(h, _lib.IPC_HANDLE_BYTES)
+                _lib.check(lib.ace_b200_ipc_open(buf, ctypes.byref(ptr)), "ace_b200_ipc_open")
+                self.struct.mailbox[r] = ptr.value
+                self.mapped.append(int(ptr.value))
+
+
+_exchanges: dict[tuple[Any, ...], PeerExchange] = {}
+# Whether the last sharded forward of this process combined the ranks in-kernel
+# (diagnostic: tests and the benchmark report which path ran).
+last_forward_exchanged = False
+
+
+def _cuda_exchange_for(args: KernelArgs, group: Any) -> PeerExchange:
+    s = args.setup
+    device = args.x.device
+    key = (device.index, id(group), int(args.inputs.b_total), s.cl, s.num_bins)
+    ex = _exchanges.get(key)
+    if ex is None:
+        ex = PeerExchange(device, group, int(args.inputs.b_total), s.cl, s.num_bins)
+        _exchanges[key] = ex
+    return ex
+
+
+def _cuda_forward_exchange(args: KernelArgs, out: ForwardOut, ex: PeerExchange) -> bool:
+    """The forward with the in-kernel exchange; False (nothing launched) when the
+    case has no pipelined forward, for the all-reduce path to take."""
+    lib = _lib.load()
+    s = args.setup
+    b_total = int(args.inputs.b_total)
+    ws = workspace(args.x.device, lib.ace_b200_workspace_bytes(b_total, s.cl, s.num_bins))
+    rc = lib.ace_b200_forward_exchange(
+        ctypes.byref(args.inputs), ctypes.byref(s.options), out.hist.data_ptr(),
+        epilogue_struct(out), ws.data_ptr(), ws.numel(), ctypes.byref(ex.struct),
+        torch.cuda.current_stream(args.x.device).cuda_stream,
+    )
+    if rc == _lib.EUNSUPPORTED:
+        return False
+    _lib.check(rc, "ace_b200_forward_exchange")
+    return True
+
+
 @dataclass
 class Steps:
-    """The device steps of one sharded call (CUDA by default)."""
+    """The device steps of one sharded call (CUDA by default). ``exchange`` /
+    ``forward_exchange``: the in-kernel exchange (None: always the all-reduce
+    path, as for CPU stand-ins)."""
 
     hist: Callable[[KernelArgs, ForwardOut], None] = _cuda_hist
     epilogue: Callable[[KernelArgs, ForwardOut], None] = _cuda_epilogue
     backward: Callable[[KernelArgs, Any, torch.Tensor], torch.Tensor] = _cuda_backward
     args: Callable[..., KernelArgs] = kernel_args
     alloc: Callable[..., ForwardOut] = alloc_outputs
+    exchange: Callable[[KernelArgs, Any], Any] | None = None
+    forward_exchange: Callable[[KernelArgs, ForwardOut, Any], bool] | None = None
 
 
-CUDA_STEPS = Steps()
+CUDA_STEPS = Steps(exchange=_cuda_exchange_for, forward_exchange=_cuda_forward_exchange)
+# the all-reduce path on CUDA (for comparisons)
+CUDA_ALLREDUCE_STEPS = Steps()
 
 
 class ShardedACELoss(torch.autograd.Function):
@@ -100,10 +180,17 @@ class ShardedACELoss(torch.autograd.Function):
         args = steps.args(input, target, config, b_offset=b_offset, b_total=b_total)
         s = args.setup
         out = steps.alloc(input.device, b_total, s.cl, s.num_bins)
-        steps.hist(args, out)
-        if dist.is_initialized() and dist.get_world_size(group) > 1:
-            dist.all_reduce(out.hist, op=dist.ReduceOp.SUM, group=group)
-        steps.epilogue(args, out)
+        multi = dist.is_initialized() and dist.get_world_size(group) > 1
+        fused = False
+        if multi and steps.exchange is not None and steps.forward_exchange is not None:
+            fused = steps.forward_exchange(args, out, steps.exchange(args, group))
+        global last_forward_exchanged
+        last_forward_exchanged = fused
+        if not fused:
+            steps.hist(args, out)
+            if multi:
+                dist.all_reduce(out.hist, op=dist.ReduceOp.SUM, group=group)
+            steps.epilogue(args, out)
         ctx.config, ctx.b_offset, ctx.b_total, ctx.steps = config, b_offset, b_total, steps
         ctx.save_for_backward(input, target, out.coef, out.d, out.jac)
         if s.reduction == "none":

@@ -7,8 +7,10 @@
 Workload: 2 x 3 x 128^3 fp32 logits, int64 labels, soft binning, K = 20 (the
 headline configuration), seeded synthetic inputs (``ace_kernels_b200.workloads``).
 With N GPUs every rank holds its own 2 x 3 x 128^3 shard of a 2N-sample batch
-(weak scaling); the per-bin statistics are all-reduced with NCCL before the
-epilogue and the local backward. ``--workload c5_soft_8x4x192c`` (or c5_hard)
+(weak scaling); the ranks' per-bin statistics are combined inside the forward
+kernel (peer stores over NVLink, then the epilogue in the same launch) where the
+forward is a pipelined kernel, else all-reduced with NCCL between the
+statistics and the epilogue launches, before the local backward. ``--workload c5_soft_8x4x192c`` (or c5_hard)
 splits one 8-sample batch over the ranks instead (strong scaling, BASELINE's
 sharded configuration).
 
@@ -27,7 +29,8 @@ calculator's bandwidth floor (ideal bytes at the measured peak) and launch floor
 step). ``cpu_baseline`` = the reference's CPU path (the oracle restatement) on the
 host cores, over the whole workload. With N > 1, ``parity`` compares the sharded
 loss of every rank with rank 0's single-GPU loss over the gathered global batch,
-and ``phases_us`` splits an eager step into its launches.
+and ``phases_us`` splits an eager step into its launches, for both ways of
+combining the ranks.
 """
 
 from __future__ import annotations
@@ -324,6 +327,9 @@ def run_ours(args: argparse.Namespace) -> None:
     for _ in range(max(3, args.warmup)):
         step()
     torch.cuda.synchronize()
+    from ace_kernels_b200 import distributed as dd
+
+    in_kernel = world > 1 and dd.last_forward_exchanged
     # One CUDA graph per step (with N > 1 it holds the NCCL all-reduce; every
     # reference to it is dropped before the process group is destroyed)
     graph = None if args.eager else capture(step)
@@ -403,10 +409,12 @@ def run_ours(args: argparse.Namespace) -> None:
     dom = max(kernels, key=lambda k: kernels[k]["ms"])
     achieved = kernels[dom]["gbs"]
     step_bytes = calc.ideal_bytes(in_b, tgt_b, "fwd_bwd")  # per rank
-    # launches per step: ours (forward, backward; N > 1: statistics, epilogue,
-    # backward) and torch's fill of grad_output, plus NCCL's all-reduce at N > 1
-    ours_per_step = 2 if world == 1 else 3
-    graph_kernels = ours_per_step + 1 + (1 if world > 1 else 0)
+    # launches per step: ours (forward, backward; N > 1 with the all-reduce path:
+    # statistics, epilogue, backward) and torch's fill of grad_output, plus NCCL's
+    # all-reduce on that path
+    allreduce_path = world > 1 and not in_kernel
+    ours_per_step = 3 if allreduce_path else 2
+    graph_kernels = ours_per_step + 1 + (1 if allreduce_path else 0)
     launch_us = calc.measure_launch_us(graph_kernels, lambda: flush_l2(flush))
     floors = {
         "bandwidth_floor_us": calc.bandwidth_floor_ms(step_bytes, peak) * 1e3,
@@ -437,6 +445,8 @@ def run_ours(args: argparse.Namespace) -> None:
             if world > 1 else "single GPU",
             "mode": mode,
             "l2": "flushed before every step: 512 MiB written, then read back, outside the events",
+            "ranks_combined": ("in the forward kernel (peer stores over NVLink)" if in_kernel
+                               else "NCCL all-reduce between two launches") if world > 1 else None,
         },
         "hbm_frac_of_ideal_bytes": (step_bytes * world / (ms_per_step * 1e-3) / 1e9) / (peak * world),
         "eager_ms_per_step": eager_ms,
@@ -490,9 +500,11 @@ def max_over_ranks(v: float, world: int, dev: torch.device) -> float:
 
 
 def sharded_phases(x, y, cfg, b_offset, b_total, flush, align, world, dev, reps: int = 50) -> dict:  # type: ignore[no-untyped-def]
-    """Device microseconds of each launch of an eager sharded step (statistics,
-    NCCL all-reduce, epilogue, backward), max over ranks, L2 flushed first."""
-    from ace_kernels_b200.distributed import _cuda_epilogue, _cuda_hist
+    """Device microseconds of each launch of an eager sharded step, max over
+    ranks, L2 flushed first: the all-reduce path (statistics, NCCL all-reduce,
+    epilogue, backward) and, where it applies, the in-kernel exchange (one
+    forward launch with the exchange and the epilogue, backward)."""
+    from ace_kernels_b200 import distributed as dd
     from ace_kernels_b200.loss import alloc_outputs, kernel_args, run_backward
 
     args = kernel_args(x.detach(), y, cfg, b_offset=b_offset, b_total=b_total)
@@ -506,18 +518,38 @@ def sharded_phases(x, y, cfg, b_offset, b_total, flush, align, world, dev, reps:
         align()
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
         ev[0].record()
-        _cuda_hist(args, out)
+        dd._cuda_hist(args, out)
         ev[1].record()
         dist.all_reduce(out.hist)
         ev[2].record()
-        _cuda_epilogue(args, out)
+        dd._cuda_epilogue(args, out)
         ev[3].record()
         run_backward(args, out.coef, out.d, out.jac, grad1)
         ev[4].record()
         torch.cuda.synchronize()
         for i, n in enumerate(names):
             acc[n] += ev[i].elapsed_time(ev[i + 1]) * 1e3
-    return {n: max_over_ranks(acc[n] / reps, world, dev) for n in names}
+    phases = {"allreduce_path": {n: max_over_ranks(acc[n] / reps, world, dev) for n in names}}
+    ex = dd._cuda_exchange_for(args, None)
+    out = alloc_outputs(dev, b_total, s.cl, s.num_bins)
+    if dd._cuda_forward_exchange(args, out, ex):  # the same decision on every rank
+        fwd = bwd = 0.0
+        for _ in range(reps):
+            out = alloc_outputs(dev, b_total, s.cl, s.num_bins)
+            flush_l2(flush)
+            align()
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            ev[0].record()
+            dd._cuda_forward_exchange(args, out, ex)
+            ev[1].record()
+            run_backward(args, out.coef, out.d, out.jac, grad1)
+            ev[2].record()
+            torch.cuda.synchronize()
+            fwd += ev[0].elapsed_time(ev[1]) * 1e3
+            bwd += ev[1].elapsed_time(ev[2]) * 1e3
+        phases["in_kernel_path"] = {"forward_with_exchange": max_over_ranks(fwd / reps, world, dev),
+                                    "backward": max_over_ranks(bwd / reps, world, dev)}
+    return phases
 
 
 def sharded_parity(x, y, cfg, b_offset, b_total, world, dev) -> dict:  # type: ignore[no-untyped-def]

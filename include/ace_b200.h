@@ -150,7 +150,7 @@ int ace_b200_forward(const ace_b200_inputs* in, const ace_b200_options* opt, flo
  * of its own, or one whose allocator may not run inside its step loop. This
  * call allocates nothing and calls no allocating function.
  *   - Limit: ace_b200_workspace_bytes(b_total, C - offset, num_bins) must not
- *     exceed ACE_B200_STATIC_SCRATCH_BYTES (about b_total * (C - offset) <= 1000
+ *     exceed ACE_B200_STATIC_SCRATCH_BYTES (about b_total * (C - offset) <= 780
  *     rows at K = 20); larger calls fail with ACE_B200_EUNSUPPORTED.
  *   - Setup: the first call on each device looks the array up and clears it on
  *     `stream`; it must not run under stream capture (it then fails with
@@ -162,6 +162,56 @@ int ace_b200_forward(const ace_b200_inputs* in, const ace_b200_options* opt, flo
 #define ACE_B200_STATIC_SCRATCH_BYTES 1048576 /* 1 MiB */
 int ace_b200_forward_static(const ace_b200_inputs* in, const ace_b200_options* opt, float* hist,
                             ace_b200_epilogue_out out, void* stream);
+
+/*
+ * Ranks that hold shards of one batch (one process per GPU) can combine their
+ * statistics inside the forward kernel itself instead of an all-reduce between
+ * ace_b200_hist and ace_b200_epilogue. No counterpart in the reference (which
+ * runs on one device); it replaces that NCCL all-reduce and the separate
+ * epilogue launch.
+ *
+ * Each rank allocates one mailbox (ace_b200_mailbox_alloc, zero-filled), hands
+ * its IPC handle (ace_b200_ipc_handle) to the others, and maps theirs
+ * (ace_b200_ipc_open). The forward's last CTA then writes this rank's rows of W,
+ * P, G into every rank's mailbox with plain stores over NVLink, raises a flag per
+ * rank, waits (at most about 2 s) for every rank's flag, adds the ranks' rows in
+ * rank order, and runs the epilogue on the global statistics: every rank ends
+ * with the same loss, coef, d and jac. A wait that runs out writes a NaN loss.
+ * All ranks must make the same sequence of these calls (the mailbox counts
+ * them); the kernels of different ranks must run on different GPUs.
+ *   world, rank  ranks (1..ACE_B200_MAX_PEERS) and this rank's index
+ *   mailbox[r]   rank r's mailbox as mapped in this process (own one at [rank])
+ * A rank's rows are samples b_offset .. b_offset + B - 1 (batch shards), or all
+ * b_total samples of a spatial shard (b_offset 0, B = b_total). Cases whose
+ * forward is not one of the pipelined kernels (soft binning with labels and a
+ * softmax; or a softmax over 5 to 24 channels with labels) return
+ * ACE_B200_EUNSUPPORTED before launching anything.
+ */
+#define ACE_B200_MAX_PEERS 8
+typedef struct ace_b200_exchange {
+  int32_t world;
+  int32_t rank;
+  void* mailbox[ACE_B200_MAX_PEERS];
+} ace_b200_exchange;
+
+/* Bytes of one mailbox for the statistics of b_total * cl rows, num_bins bins
+ * and `world` ranks. */
+size_t ace_b200_mailbox_bytes(int64_t b_total, int64_t cl, int32_t num_bins, int32_t world);
+/* A zero-filled device allocation of `bytes` (cudaMalloc), and its release. */
+int ace_b200_mailbox_alloc(size_t bytes, void** ptr_out);
+int ace_b200_mailbox_free(void* ptr);
+/* The CUDA IPC handle of a mailbox (ACE_B200_IPC_HANDLE_BYTES bytes), and the
+ * mapping of another process's mailbox from its handle (and its unmapping). */
+#define ACE_B200_IPC_HANDLE_BYTES 64
+int ace_b200_ipc_handle(void* ptr, void* handle_out);
+int ace_b200_ipc_open(const void* handle, void** ptr_out);
+int ace_b200_ipc_close(void* ptr);
+
+/* ace_b200_forward with the statistics of all ranks combined in the kernel. */
+int ace_b200_forward_exchange(const ace_b200_inputs* in, const ace_b200_options* opt, float* hist,
+                              ace_b200_epilogue_out out, void* workspace,
+                              size_t workspace_bytes, const ace_b200_exchange* xchg,
+                              void* stream);
 
 /*
  * Statistics only (the first half of ace_b200_forward), for callers that reduce

@@ -41,6 +41,20 @@ def test_header_constants_match_binding() -> None:
     assert int(consts["ACE_B200_ACT_SIGMOID"]) == _lib.ACT_SIGMOID
     assert int(consts["ACE_B200_TARGET_DENSE"]) == _lib.TARGET_DENSE
     assert int(consts["ACE_B200_REDUCTION_NONE"]) == _lib.REDUCTION_NONE
+    assert int(consts["ACE_B200_MAX_PEERS"]) == _lib.MAX_PEERS
+    assert int(consts["ACE_B200_IPC_HANDLE_BYTES"]) == _lib.IPC_HANDLE_BYTES
+    assert int(consts["ACE_B200_KERNEL_MC_PIPE"]) == _lib.KERNEL_MC_PIPE
+    assert int(consts["ACE_B200_KERNEL_MC_GRAD"]) == _lib.KERNEL_MC_GRAD
+
+
+def test_mailbox_bytes() -> None:
+    """Header, then two parities of one slot per rank: {b_offset, B} and the
+    rank's W, P, G (up to all b_total rows)."""
+    lib = _lib.load()
+    slot = 16 + 12 * 8 * 4 * 20
+    assert lib.ace_b200_mailbox_bytes(8, 4, 20, 2) == 256 + 2 * 2 * slot
+    assert lib.ace_b200_mailbox_bytes(0, 4, 20, 2) == 0
+    assert lib.ace_b200_mailbox_bytes(8, 4, 20, 0) == 0
 
 
 def table(k: int, soft: bool) -> torch.Tensor:
