@@ -99,6 +99,8 @@ class Exchange(Structure):
         ("world", c_int32),
         ("rank", c_int32),
         ("mailbox", c_void_p * MAX_PEERS),
+        ("first", c_int32 * MAX_PEERS),
+        ("count", c_int32 * MAX_PEERS),
     ]
 
 

@@ -474,8 +474,9 @@ bool mc_fwd_setup(const ace_b200_inputs* in, const ace_b200_options* opt, Varian
   return true;
 }
 
+// One source rank's slot: its rows (at most all b_total * cl) of 3 K tagged 64-bit words.
 size_t mailbox_slot_bytes(int64_t b_total, int64_t cl, int K) {
-  return round_up(16 + (size_t)12 * b_total * cl * K, 16);
+  return round_up((size_t)24 * b_total * cl * K, 16);
 }
 
 int hist_impl(const ace_b200_inputs* in, const ace_b200_options* opt, float* hist,
@@ -526,8 +527,16 @@ int hist_impl(const ace_b200_inputs* in, const ace_b200_options* opt, float* his
     for (int r = 0; r < xchg->world; ++r) {
       if (!xchg->mailbox[r] || !aligned(xchg->mailbox[r], 16))
         return fail(ACE_B200_EINVAL, "mailbox %d is null or misaligned", r);
+      if (xchg->first[r] < 0 || xchg->count[r] < 1 ||
+          (int64_t)xchg->first[r] + xchg->count[r] > in->b_total)
+        return fail(ACE_B200_EINVAL, "rank %d's samples %d + %d are outside b_total=%lld", r,
+                    xchg->first[r], xchg->count[r], (long long)in->b_total);
       p.xchg.mailbox[r] = static_cast<unsigned char*>(xchg->mailbox[r]);
+      p.xchg.first[r] = xchg->first[r];
+      p.xchg.count[r] = xchg->count[r];
     }
+    if (xchg->first[xchg->rank] != in->b_offset || xchg->count[xchg->rank] != in->B)
+      return fail(ACE_B200_EINVAL, "this rank's first/count differ from its b_offset/B");
   }
 
   // Soft binning with labels and a softmax over <= 4 channels: soft_fwd_kernel.

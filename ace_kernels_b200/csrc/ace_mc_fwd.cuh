@@ -146,6 +146,8 @@ __device__ __forceinline__ void hard_finish(const FwdParams& P) {
   const bool failed = __ldcg(err) != 0u;  // a CTA's wait ran out: the sums are incomplete
   const float nan = __int_as_float(0x7fc00000);
   const double ur = 1.0 / (double)kMcRScale, invK = 1.0 / (double)K;
+  const bool xg = P.xchg.world > 1;  // ranks combined here (xchg_send_row, xchg_finish)
+  const unsigned long long epoch = xg ? xchg_epoch(P.xchg) : 0ull;
   float mine = 0.0f;
   for (int r = warp; r < rows; r += NT / 32) {
     float wv[4], pv[4], gv[4];
@@ -167,9 +169,10 @@ __device__ __forceinline__ void hard_finish(const FwdParams& P) {
       P.hist_out[m + e] = pv[qq];
       P.hist_out[2 * m + e] = gv[qq];
     }
-    if (P.do_epilogue && P.xchg.world == 1) mine = ACE_FADD(mine, epilogue_row(P.epi, r, wv, pv, gv));
+    if (xg) xchg_send_row(P, epoch, r, wv, pv, gv);
+    else if (P.do_epilogue) mine = ACE_FADD(mine, epilogue_row(P.epi, r, wv, pv, gv));
   }
-  if (P.xchg.world > 1) mine = exchange_and_epilogue(P);
+  if (xg) mine = xchg_finish(P, epoch);
   for (int i = tid; i < P.g.B; i += NT) P.pool_ctr[i] = 0u;
   if (P.do_epilogue) write_loss_if0(P.epi, cta_sum_in_warp_order(mine));
   __syncthreads();

@@ -152,36 +152,6 @@ __device__ __forceinline__ void stage_soft_intervals(const BinTable& tab, double
   }
 }
 
-// Multi-rank forwards (ace_b200_forward_exchange), all threads of the last CTA
-// after hist_out holds this rank's W, P, G: the ranks' statistics combined
-// (exchange_stats), then the epilogue of every row from hist_out, one warp per
-// row in the order of the single-rank path (a failed exchange gives NaN rows).
-// Returns this thread's share of the loss (cta_sum_in_warp_order adds them).
-__device__ __forceinline__ float exchange_and_epilogue(const FwdParams& P) {
-  const bool ok = exchange_stats(P);
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x / 32;
-  const int K = P.tab.K, rows = P.B_total * P.g.CL;
-  const int64_t m = (int64_t)rows * K;
-  const float nan = __int_as_float(0x7fc00000);
-  float mine = 0.0f;
-  if (!P.do_epilogue) return mine;
-  for (int r = warp; r < rows; r += nw) {
-    float wv[4], pv[4], gv[4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int k = lane + 32 * q;
-      wv[q] = pv[q] = gv[q] = 0.0f;
-      if (k >= K) continue;
-      const int64_t e = (int64_t)r * K + k;
-      wv[q] = ok ? __ldcg(P.hist_out + e) : nan;
-      pv[q] = ok ? __ldcg(P.hist_out + m + e) : nan;
-      gv[q] = ok ? __ldcg(P.hist_out + 2 * m + e) : nan;
-    }
-    mine = ACE_FADD(mine, epilogue_row(P.epi, r, wv, pv, gv));
-  }
-  return mine;
-}
-
 // The last CTA of soft_fwd_kernel and mc_fwd_kernel (soft binning; all threads of
 // the CTA), one warp per row r: lane l takes bins k = l + 32 q. W, P, G of bin k
 // come from the slots of intervals k and k + 1 (flags 0 and 1). Interval j in
@@ -202,6 +172,8 @@ __device__ __forceinline__ void soft_finish(const FwdParams& P, const double4* s
   const int rows = P.B_total * P.g.CL;
   const int64_t m = (int64_t)rows * (K + 1) * 2;  // moment stride of the workspace sums
   unsigned* err = P.counter + 1;
+  const bool xg = P.xchg.world > 1;  // ranks combined here (xchg_send_row, xchg_finish)
+  const unsigned long long epoch = xg ? xchg_epoch(P.xchg) : 0ull;
   const int64_t stat_stride = (int64_t)rows * K;
   unsigned long long* acc = P.iacc;
   const double ur = 1.0 / (double)kSoftRScale, uq = ur * 0.5, invK = 1.0 / (double)K;
@@ -274,9 +246,10 @@ __device__ __forceinline__ void soft_finish(const FwdParams& P, const double4* s
       for (int o = 0; o < kSoftMoments; ++o)
 #pragma unroll
         for (int f = 0; f < 2; ++f) __stcg(acc + o * m + row_slot + 2 * j + f, 0ull);
-    if (P.do_epilogue && P.xchg.world == 1) mine = ACE_FADD(mine, epilogue_row(P.epi, r, wv, pv, gv));
+    if (xg) xchg_send_row(P, epoch, r, wv, pv, gv);
+    else if (P.do_epilogue) mine = ACE_FADD(mine, epilogue_row(P.epi, r, wv, pv, gv));
   }
-  if (P.xchg.world > 1) mine = exchange_and_epilogue(P);
+  if (xg) mine = xchg_finish(P, epoch);
   for (int i = tid; i < P.g.B; i += NT) P.pool_ctr[i] = 0u;
   if (P.do_epilogue) write_loss_if0(P.epi, cta_sum_in_warp_order(mine));
   __syncthreads();

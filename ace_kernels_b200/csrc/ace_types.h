@@ -71,10 +71,12 @@ struct EpiParams {
 // Statistics exchange between ranks inside the forward (ace_b200_forward_exchange).
 constexpr int kMaxPeers = ACE_B200_MAX_PEERS;
 struct XchgParams {
-  int world;                         // 1: no exchange
+  int world;                          // 1: no exchange
   int rank;
-  int64_t slot_bytes;                // bytes of one rank's slot in a mailbox
+  int64_t slot_bytes;                 // bytes of one rank's slot in a mailbox
   unsigned char* mailbox[kMaxPeers];  // every rank's mailbox, mapped in this process
+  int first[kMaxPeers];               // each rank's first sample (b_offset)
+  int count[kMaxPeers];               // and its number of samples (B)
 };
 
 struct FwdParams {

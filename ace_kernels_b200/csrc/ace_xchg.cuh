@@ -1,116 +1,130 @@
 // Exchange of the forward's statistics between ranks inside the forward kernel
 // (ace_b200_forward_exchange), on B200 (sm_100a) GPUs joined by NVLink. Run by the
-// last CTA of a pipelined forward (soft_finish, hard_finish) once it has written
-// this rank's W, P, G to hist_out; replaces an all-reduce of hist_out between two
-// launches and the separate epilogue launch after it.
+// last CTA of a pipelined forward (soft_finish, hard_finish) as it reconstructs
+// this rank's W, P, G; replaces an all-reduce between two launches and the
+// separate epilogue launch after it.
 //
-// Mailbox of a rank (XchgParams: every rank's mailbox is mapped in every process
-// through CUDA IPC; plain loads and stores, no multicast):
-//   [0, 8)        calls completed so far (the epoch counter; read and written by
-//                 its own rank only)
-//   [64, 192)     flags[2][kMaxPeers]: epoch of the data in slot (parity, source)
-//   [256, ...)    slots[2][world]: {b_offset, B} (two int32, 16 bytes), then W, P, G
-//                 of the source's rows, [3][B][CL][K] fp32
+// Low-latency protocol: every value crosses NVLink as one 64-bit store of {its
+// bits, the call's tag}, so a receiver that reads a word carrying the current tag
+// has the value: no fence, no separate flag, one one-way trip. The sender stores
+// a row's values from registers as soon as it has reconstructed them; the
+// receiver polls the words of the rows other ranks hold (plain loads of its own
+// memory, with a bound on the wait).
+//
+// Mailbox of a rank (every rank's mailbox is mapped in every process through
+// CUDA IPC; plain loads and stores, no multicast):
+//   [0, 8)       calls completed so far (the epoch counter; its own rank only)
+//   [256, ...)   slots[2][world]: the source rank's rows, [3][rows][K] words
+//                {value bits, tag}, tag = the low 32 bits of the call number
 // Call e (e = epoch counter + 1) uses parity e & 1: a rank writes call e's slot in
 // a peer only after finishing call e - 1, which needed that peer's call e - 1
-// data, written after the peer finished call e - 2 (its last read of parity
-// e & 1); so two parities never overlap.
+// data, sent after the peer finished call e - 2 (its last read of parity e & 1);
+// so two parities never overlap. A fresh mailbox is zero-filled and call numbers
+// start at 1, so a stale word never carries the current tag.
 #pragma once
 
 namespace ace {
 
 constexpr int kXchgHeaderBytes = 256;
-constexpr int kXchgFlagsOffset = 64;
 constexpr unsigned long long kXchgWaitNs = 2000000000ull;  // bound of the wait (2 s)
 
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
-  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+// This call's number (the last CTA, any thread; the load overlaps the
+// reconstruction's own loads).
+__device__ __forceinline__ unsigned long long xchg_epoch(const XchgParams& X) {
+  return *reinterpret_cast<volatile unsigned long long*>(X.mailbox[X.rank]) + 1ull;
 }
 
-__device__ __forceinline__ unsigned long long* xchg_flag(unsigned char* box, int parity, int src) {
-  return reinterpret_cast<unsigned long long*>(box + kXchgFlagsOffset) + parity * kMaxPeers + src;
-}
-__device__ __forceinline__ float* xchg_slot(const XchgParams& X, unsigned char* box, int parity,
-                                            int src) {
-  return reinterpret_cast<float*>(box + kXchgHeaderBytes +
-                                  ((int64_t)parity * X.world + src) * X.slot_bytes);
+// Word of (stat s, row r, bin k) of source `src` in `box`, parity `par`; rows are
+// counted from the source's first loss row.
+__device__ __forceinline__ unsigned long long* xchg_word(const XchgParams& X, unsigned char* box,
+                                                         int par, int src, int s, int r, int k,
+                                                         int CL, int K) {
+  const int64_t rows = (int64_t)X.count[src] * CL;
+  return reinterpret_cast<unsigned long long*>(box + kXchgHeaderBytes +
+                                               ((int64_t)par * X.world + src) * X.slot_bytes) +
+         ((int64_t)s * rows + (r - (int64_t)X.first[src] * CL)) * K + k;
 }
 
-// All threads of the last CTA, after hist_out ([3][B_total * CL][K]) holds this
-// rank's sums: sends this rank's rows to every rank, waits for every rank's rows,
-// and overwrites hist_out with the rank-ordered sums (a sample's rows come from
-// the ranks whose {b_offset, B} covers it). False if a wait ran out.
-__device__ __forceinline__ bool exchange_stats(const FwdParams& P) {
+// One warp: row r's W, P, G (lane l holds bins l + 32 q) to every rank, if this
+// rank holds the row.
+__device__ __forceinline__ void xchg_send_row(const FwdParams& P, unsigned long long epoch, int r,
+                                              const float (&w)[4], const float (&p)[4],
+                                              const float (&g)[4]) {
   const XchgParams& X = P.xchg;
-  const int tid = threadIdx.x, nt = blockDim.x;
-  const int K = P.tab.K, CL = P.g.CL;
-  const int64_t row_vals = (int64_t)CL * K;              // values of one sample, one stat
-  const int64_t m = (int64_t)P.B_total * row_vals;       // one stat, all samples
-  unsigned char* own = X.mailbox[X.rank];
-  __shared__ unsigned long long s_epoch;
-  __shared__ int s_fail;
-  __syncthreads();  // hist_out written by every warp
-  if (tid == 0) {
-    s_epoch = *reinterpret_cast<volatile unsigned long long*>(own) + 1ull;
-    s_fail = 0;
-  }
-  __syncthreads();
-  const unsigned long long epoch = s_epoch;
+  const int CL = P.g.CL, K = P.tab.K, lane = threadIdx.x & 31;
+  if (r < X.first[X.rank] * CL || r >= (X.first[X.rank] + X.count[X.rank]) * CL) return;
   const int par = (int)(epoch & 1ull);
-  // this rank's rows into its slot of every mailbox
-  const int64_t first = (int64_t)P.b_offset * row_vals, cnt = (int64_t)P.g.B * row_vals;
-  for (int p = 0; p < X.world; ++p) {
-    float* slot = xchg_slot(X, X.mailbox[p], par, X.rank);
-    if (tid == 0) {
-      reinterpret_cast<int*>(slot)[0] = P.b_offset;
-      reinterpret_cast<int*>(slot)[1] = P.g.B;
-    }
-    for (int64_t i = tid; i < 3 * cnt; i += nt) {
-      const int64_t st = i / cnt, j = i - st * cnt;
-      slot[4 + i] = __ldcg(P.hist_out + st * m + first + j);
+  const unsigned long long tag = (epoch & 0xffffffffull) << 32;
+  for (int dst = 0; dst < X.world; ++dst) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int k = lane + 32 * q;
+      if (k >= K) continue;
+      const float v[3] = {w[q], p[q], g[q]};
+#pragma unroll
+      for (int s = 0; s < 3; ++s) {
+        unsigned long long* a = xchg_word(X, X.mailbox[dst], par, X.rank, s, r, k, CL, K);
+        const unsigned long long word = tag | __float_as_uint(v[s]);
+        asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(a), "l"(word) : "memory");
+      }
     }
   }
-  __syncthreads();
-  if (tid < X.world) {
-    // every store above, ordered before the flag by the barrier and this fence
-    asm volatile("fence.acq_rel.sys;" ::: "memory");
-    st_release_sys(xchg_flag(X.mailbox[tid], par, X.rank), epoch);
-    // then wait for rank tid's data in this rank's mailbox
-    const unsigned long long* f = xchg_flag(own, par, tid);
-    if (ld_acquire_sys(f) != epoch) {
-      const unsigned long long t0 = ace_now_ns();
-      while (ld_acquire_sys(f) != epoch) {
-        if (ace_now_ns() - t0 > kXchgWaitNs) {
-          atomicExch(&s_fail, 1);
-          break;
+}
+
+// All threads of the last CTA, after every row was sent: per row (one warp, the
+// single-rank path's order) the values of the ranks holding the row, added in
+// rank order, into hist_out and (do_epilogue) the row's epilogue. A wait that
+// runs out makes the row NaN. Returns this thread's share of the loss; advances
+// the epoch counter.
+__device__ __forceinline__ float xchg_finish(const FwdParams& P, unsigned long long epoch) {
+  const XchgParams& X = P.xchg;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x / 32;
+  const int CL = P.g.CL, K = P.tab.K, rows = P.B_total * CL;
+  const int64_t m = (int64_t)rows * K;
+  const int par = (int)(epoch & 1ull);
+  const unsigned tag = (unsigned)(epoch & 0xffffffffull);
+  unsigned char* own = X.mailbox[X.rank];
+  const float nan = __int_as_float(0x7fc00000);
+  const unsigned long long t0 = ace_now_ns();
+  float mine = 0.0f;
+  for (int r = warp; r < rows; r += nw) {
+    const int b = r / CL;
+    float v[3][4];
+    bool ok = true;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int k = lane + 32 * q;
+#pragma unroll
+      for (int s = 0; s < 3; ++s) v[s][q] = 0.0f;
+      if (k >= K) continue;
+      for (int src = 0; src < X.world; ++src) {
+        if (b < X.first[src] || b >= X.first[src] + X.count[src]) continue;
+#pragma unroll
+        for (int s = 0; s < 3; ++s) {
+          const unsigned long long* a = xchg_word(X, own, par, src, s, r, k, CL, K);
+          unsigned long long word;
+          asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(word) : "l"(a) : "memory");
+          while ((unsigned)(word >> 32) != tag) {
+            if (ace_now_ns() - t0 > kXchgWaitNs) {
+              ok = false;
+              break;
+            }
+            asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(word) : "l"(a) : "memory");
+          }
+          v[s][q] = ACE_FADD(v[s][q], __uint_as_float((unsigned)word));
         }
       }
+      if (!ok) v[0][q] = v[1][q] = v[2][q] = nan;
+      const int64_t e = (int64_t)r * K + k;
+      P.hist_out[e] = v[0][q];
+      P.hist_out[m + e] = v[1][q];
+      P.hist_out[2 * m + e] = v[2][q];
     }
+    if (P.do_epilogue) mine = ACE_FADD(mine, epilogue_row(P.epi, r, v[0], v[1], v[2]));
   }
   __syncthreads();
-  const bool ok = s_fail == 0;
-  if (ok) {
-    for (int64_t e = tid; e < 3 * m; e += nt) {
-      const int64_t st = e / m, j = e - st * m;
-      const int b = (int)(j / row_vals);
-      float acc = 0.0f;
-      for (int r = 0; r < X.world; ++r) {
-        const float* slot = xchg_slot(X, own, par, r);
-        const int ob = __ldcv(reinterpret_cast<const int*>(slot)), nb = __ldcv(reinterpret_cast<const int*>(slot) + 1);
-        if (b >= ob && b < ob + nb)
-          acc = ACE_FADD(acc, __ldcv(slot + 4 + st * nb * row_vals + (j - (int64_t)ob * row_vals)));
-      }
-      P.hist_out[e] = acc;
-    }
-  }
-  __syncthreads();
-  if (tid == 0) *reinterpret_cast<volatile unsigned long long*>(own) = epoch;
-  return ok;
+  if (threadIdx.x == 0) *reinterpret_cast<volatile unsigned long long*>(own) = epoch;
+  return mine;
 }
 
 }  // namespace ace

@@ -77,12 +77,14 @@ def _cuda_backward(args: KernelArgs, out: Any, grad: torch.Tensor) -> torch.Tens
 
 
 class PeerExchange:
-    """The mailboxes of the in-kernel exchange for one process group and one
-    statistics shape: this rank's (``ace_b200_mailbox_alloc``) and every other
-    rank's, mapped from the CUDA IPC handles gathered over the group. Made by
-    every rank together (the gather is a collective), once per shape."""
+    """The mailboxes of the in-kernel exchange for one process group, one
+    statistics shape and one sharding: this rank's (``ace_b200_mailbox_alloc``)
+    and every other rank's, mapped from the CUDA IPC handles gathered over the
+    group, with every rank's samples (b_offset, B). Made by every rank together
+    (the gather is a collective), once per shape and sharding."""
 
-    def __init__(self, device: torch.device, group: Any, b_total: int, cl: int, k: int) -> None:
+    def __init__(self, device: torch.device, group: Any, b_total: int, cl: int, k: int,
+                 b_offset: int, b_count: int) -> None:
         lib = _lib.load()
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -94,12 +96,14 @@ class PeerExchange:
         with torch.cuda.device(device):
             _lib.check(lib.ace_b200_mailbox_alloc(nbytes, ctypes.byref(own)), "ace_b200_mailbox_alloc")
             _lib.check(lib.ace_b200_ipc_handle(own, handle), "ace_b200_ipc_handle")
-        handles: list[Any] = [None] * self.world
-        dist.all_gather_object(handles, bytes(handle), group=group)
+        gathered: list[Any] = [None] * self.world
+        dist.all_gather_object(gathered, (bytes(handle), b_offset, b_count), group=group)
         self.struct = _lib.Exchange(world=self.world, rank=self.rank)
         self.mapped: list[int] = []
         with torch.cuda.device(device):
-            for r, h in enumerate(handles):
+            for r, (h, first, count) in enumerate(gathered):
+                self.struct.first[r] = first
+                self.struct.count[r] = count
                 if r == self.rank:
                     self.struct.mailbox[r] = own.value
                     continue
@@ -119,10 +123,11 @@ last_forward_exchanged = False
 def _cuda_exchange_for(args: KernelArgs, group: Any) -> PeerExchange:
     s = args.setup
     device = args.x.device
-    key = (device.index, id(group), int(args.inputs.b_total), s.cl, s.num_bins)
+    shard = (int(args.inputs.b_offset), int(args.inputs.B))
+    key = (device.index, id(group), int(args.inputs.b_total), s.cl, s.num_bins, shard)
     ex = _exchanges.get(key)
     if ex is None:
-        ex = PeerExchange(device, group, int(args.inputs.b_total), s.cl, s.num_bins)
+        ex = PeerExchange(device, group, int(args.inputs.b_total), s.cl, s.num_bins, *shard)
         _exchanges[key] = ex
     return ex
 

@@ -172,15 +172,19 @@ int ace_b200_forward_static(const ace_b200_inputs* in, const ace_b200_options* o
  *
  * Each rank allocates one mailbox (ace_b200_mailbox_alloc, zero-filled), hands
  * its IPC handle (ace_b200_ipc_handle) to the others, and maps theirs
- * (ace_b200_ipc_open). The forward's last CTA then writes this rank's rows of W,
- * P, G into every rank's mailbox with plain stores over NVLink, raises a flag per
- * rank, waits (at most about 2 s) for every rank's flag, adds the ranks' rows in
- * rank order, and runs the epilogue on the global statistics: every rank ends
- * with the same loss, coef, d and jac. A wait that runs out writes a NaN loss.
- * All ranks must make the same sequence of these calls (the mailbox counts
- * them); the kernels of different ranks must run on different GPUs.
- *   world, rank  ranks (1..ACE_B200_MAX_PEERS) and this rank's index
- *   mailbox[r]   rank r's mailbox as mapped in this process (own one at [rank])
+ * (ace_b200_ipc_open). The forward's last CTA then stores this rank's rows of W,
+ * P, G into every rank's mailbox over NVLink, each value as one 64-bit word
+ * tagged with the call's number, reads the other ranks' rows from its own
+ * mailbox as their tagged words arrive (waiting at most about 2 s), adds the
+ * ranks' rows in rank order, and runs the epilogue on the global statistics:
+ * every rank ends with the same loss, coef, d and jac. A wait that runs out
+ * writes NaN statistics and loss. All ranks must make the same sequence of these
+ * calls (the mailbox counts them); the kernels of different ranks must run on
+ * different GPUs.
+ *   world, rank    ranks (1..ACE_B200_MAX_PEERS) and this rank's index
+ *   mailbox[r]     rank r's mailbox as mapped in this process (own one at [rank])
+ *   first[r]       rank r's first sample, and count[r] its number of samples: the
+ *   count[r]       b_offset and B of its inputs (own entry equal to this call's)
  * A rank's rows are samples b_offset .. b_offset + B - 1 (batch shards), or all
  * b_total samples of a spatial shard (b_offset 0, B = b_total). Cases whose
  * forward is not one of the pipelined kernels (soft binning with labels and a
@@ -192,6 +196,8 @@ typedef struct ace_b200_exchange {
   int32_t world;
   int32_t rank;
   void* mailbox[ACE_B200_MAX_PEERS];
+  int32_t first[ACE_B200_MAX_PEERS];
+  int32_t count[ACE_B200_MAX_PEERS];
 } ace_b200_exchange;
 
 /* Bytes of one mailbox for the statistics of b_total * cl rows, num_bins bins

@@ -48,10 +48,10 @@ def test_header_constants_match_binding() -> None:
 
 
 def test_mailbox_bytes() -> None:
-    """Header, then two parities of one slot per rank: {b_offset, B} and the
-    rank's W, P, G (up to all b_total rows)."""
+    """Header, then two parities of one slot per rank: the rank's W, P, G (up to
+    all b_total rows) as 64-bit tagged words."""
     lib = _lib.load()
-    slot = 16 + 12 * 8 * 4 * 20
+    slot = 24 * 8 * 4 * 20
     assert lib.ace_b200_mailbox_bytes(8, 4, 20, 2) == 256 + 2 * 2 * slot
     assert lib.ace_b200_mailbox_bytes(0, 4, 20, 2) == 0
     assert lib.ace_b200_mailbox_bytes(8, 4, 20, 0) == 0

@@ -30,6 +30,7 @@ def test_wait_without_peer_runs_out_and_returns_nan() -> None:
         _lib.check(lib.ace_b200_mailbox_alloc(nbytes, ctypes.byref(b)), "ace_b200_mailbox_alloc")
     ex = _lib.Exchange(world=2, rank=0)
     ex.mailbox[0], ex.mailbox[1] = boxes[0].value, boxes[1].value
+    ex.first[0], ex.count[0], ex.first[1], ex.count[1] = 0, 2, 2, 2
     try:
         torch.cuda.synchronize()
         t0 = time.perf_counter()
@@ -63,8 +64,15 @@ def test_exchange_rejects_bad_arguments_and_unpipelined_cases() -> None:
     _lib.check(lib.ace_b200_mailbox_alloc(lib.ace_b200_mailbox_bytes(4, s.cl, s.num_bins, 2),
                                           ctypes.byref(box)), "ace_b200_mailbox_alloc")
     try:
-        ex = _lib.Exchange(world=2, rank=0)
-        ex.mailbox[0] = ex.mailbox[1] = box.value
+        def exchange(world: int, rank: int, boxes: int = 2) -> _lib.Exchange:
+            e = _lib.Exchange(world=world, rank=rank)
+            for r in range(min(world, _lib.MAX_PEERS)):
+                e.first[r], e.count[r] = 2 * r, 2
+                if r < boxes:
+                    e.mailbox[r] = box.value
+            return e
+
+        ex = exchange(2, 0)
 
         def call(e: _lib.Exchange) -> int:
             return lib.ace_b200_forward_exchange(
@@ -74,11 +82,15 @@ def test_exchange_rejects_bad_arguments_and_unpipelined_cases() -> None:
 
         # hard binning over 3 channels runs hist_kernel: no in-kernel exchange
         assert call(ex) == _lib.EUNSUPPORTED
-        assert call(_lib.Exchange(world=2, rank=2)) == _lib.EINVAL
-        assert call(_lib.Exchange(world=9, rank=0)) == _lib.EINVAL
-        missing = _lib.Exchange(world=2, rank=0)
-        missing.mailbox[0] = box.value
-        assert call(missing) == _lib.EINVAL
+        assert call(exchange(2, 2)) == _lib.EINVAL
+        assert call(exchange(9, 0)) == _lib.EINVAL
+        assert call(exchange(2, 0, boxes=1)) == _lib.EINVAL  # rank 1's mailbox missing
+        outside = exchange(2, 0)
+        outside.count[1] = 3  # samples 2..4 of 4
+        assert call(outside) == _lib.EINVAL
+        mismatch = exchange(2, 0)
+        mismatch.first[0] = 1  # this call's b_offset is 0
+        assert call(mismatch) == _lib.EINVAL
     finally:
         torch.cuda.synchronize()
         lib.ace_b200_mailbox_free(box)
