@@ -537,6 +537,13 @@ int hist_impl(const ace_b200_inputs* in, const ace_b200_options* opt, float* his
     }
     if (xchg->first[xchg->rank] != in->b_offset || xchg->count[xchg->rank] != in->B)
       return fail(ACE_B200_EINVAL, "this rank's first/count differ from its b_offset/B");
+    // batch shards (disjoint samples): only each row's f crosses
+    p.xchg.own_rows = 1;
+    for (int a = 0; a < xchg->world; ++a)
+      for (int b = a + 1; b < xchg->world; ++b)
+        if (xchg->first[a] < xchg->first[b] + xchg->count[b] &&
+            xchg->first[b] < xchg->first[a] + xchg->count[a])
+          p.xchg.own_rows = 0;
   }
 
   // Soft binning with labels and a softmax over <= 4 channels: soft_fwd_kernel.

@@ -169,10 +169,15 @@ __device__ __forceinline__ void hard_finish(const FwdParams& P) {
       P.hist_out[m + e] = pv[qq];
       P.hist_out[2 * m + e] = gv[qq];
     }
-    if (xg) xchg_send_row(P, epoch, r, wv, pv, gv);
-    else if (P.do_epilogue) mine = ACE_FADD(mine, epilogue_row(P.epi, r, wv, pv, gv));
+    if (xg && P.xchg.own_rows) {
+      if (xchg_owns(P, r)) xchg_send_f(P, epoch, r, epilogue_row(P.epi, r, wv, pv, gv));
+    } else if (xg) {
+      xchg_send_row(P, epoch, r, wv, pv, gv);
+    } else if (P.do_epilogue) {
+      mine = ACE_FADD(mine, epilogue_row(P.epi, r, wv, pv, gv));
+    }
   }
-  if (xg) mine = xchg_finish(P, epoch);
+  if (xg) mine = P.xchg.own_rows ? xchg_finish_f(P, epoch) : xchg_finish(P, epoch);
   for (int i = tid; i < P.g.B; i += NT) P.pool_ctr[i] = 0u;
   if (P.do_epilogue) write_loss_if0(P.epi, cta_sum_in_warp_order(mine));
   __syncthreads();

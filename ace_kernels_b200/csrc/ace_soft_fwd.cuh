@@ -246,10 +246,15 @@ __device__ __forceinline__ void soft_finish(const FwdParams& P, const double4* s
       for (int o = 0; o < kSoftMoments; ++o)
 #pragma unroll
         for (int f = 0; f < 2; ++f) __stcg(acc + o * m + row_slot + 2 * j + f, 0ull);
-    if (xg) xchg_send_row(P, epoch, r, wv, pv, gv);
-    else if (P.do_epilogue) mine = ACE_FADD(mine, epilogue_row(P.epi, r, wv, pv, gv));
+    if (xg && P.xchg.own_rows) {
+      if (xchg_owns(P, r)) xchg_send_f(P, epoch, r, epilogue_row(P.epi, r, wv, pv, gv));
+    } else if (xg) {
+      xchg_send_row(P, epoch, r, wv, pv, gv);
+    } else if (P.do_epilogue) {
+      mine = ACE_FADD(mine, epilogue_row(P.epi, r, wv, pv, gv));
+    }
   }
-  if (xg) mine = xchg_finish(P, epoch);
+  if (xg) mine = P.xchg.own_rows ? xchg_finish_f(P, epoch) : xchg_finish(P, epoch);
   for (int i = tid; i < P.g.B; i += NT) P.pool_ctr[i] = 0u;
   if (P.do_epilogue) write_loss_if0(P.epi, cta_sum_in_warp_order(mine));
   __syncthreads();

@@ -77,6 +77,7 @@ struct XchgParams {
   unsigned char* mailbox[kMaxPeers];  // every rank's mailbox, mapped in this process
   int first[kMaxPeers];               // each rank's first sample (b_offset)
   int count[kMaxPeers];               // and its number of samples (B)
+  int own_rows;                       // 1: the ranks' samples are disjoint (batch shards)
 };
 
 struct FwdParams {

@@ -4,6 +4,14 @@
 // this rank's W, P, G; replaces an all-reduce between two launches and the
 // separate epilogue launch after it.
 //
+// What crosses depends on the sharding. Batch shards (the ranks' samples
+// disjoint, own_rows): a sample's rows are complete on the rank that holds it, so
+// that rank runs their epilogue itself (coef, d, jac, f) and only each row's f
+// crosses, for every rank to add the loss in the single-rank order (bit for bit
+// the single-GPU loss). Spatial shards (every rank holds partial sums of every
+// row): each rank's W, P, G cross, and every rank adds them in rank order and
+// runs the epilogue of every row.
+//
 // Low-latency protocol: every value crosses NVLink as one 64-bit store of {its
 // bits, the call's tag}, so a receiver that reads a word carrying the current tag
 // has the value: no fence, no separate flag, one one-way trip. The sender stores
@@ -15,7 +23,8 @@
 // CUDA IPC; plain loads and stores, no multicast):
 //   [0, 8)       calls completed so far (the epoch counter; its own rank only)
 //   [256, ...)   slots[2][world]: the source rank's rows, [3][rows][K] words
-//                {value bits, tag}, tag = the low 32 bits of the call number
+//                {value bits, tag} (batch shards: [rows] words of f), tag = the low
+//                32 bits of the call number
 // Call e (e = epoch counter + 1) uses parity e & 1: a rank writes call e's slot in
 // a peer only after finishing call e - 1, which needed that peer's call e - 1
 // data, sent after the peer finished call e - 2 (its last read of parity e & 1);
@@ -121,6 +130,68 @@ __device__ __forceinline__ float xchg_finish(const FwdParams& P, unsigned long l
       P.hist_out[2 * m + e] = v[2][q];
     }
     if (P.do_epilogue) mine = ACE_FADD(mine, epilogue_row(P.epi, r, v[0], v[1], v[2]));
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *reinterpret_cast<volatile unsigned long long*>(own) = epoch;
+  return mine;
+}
+
+// Batch shards: this rank's row r, whose epilogue gave f (on every lane), to every
+// rank (one lane per destination).
+__device__ __forceinline__ void xchg_send_f(const FwdParams& P, unsigned long long epoch, int r,
+                                            float f) {
+  const XchgParams& X = P.xchg;
+  const int lane = threadIdx.x & 31, CL = P.g.CL;
+  const int par = (int)(epoch & 1ull);
+  if (lane < X.world) {
+    unsigned long long* a = xchg_word(X, X.mailbox[lane], par, X.rank, 0, r, 0, CL, 1);
+    const unsigned long long word = ((epoch & 0xffffffffull) << 32) | __float_as_uint(f);
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(a), "l"(word) : "memory");
+  }
+}
+
+// Whether this rank holds row r.
+__device__ __forceinline__ bool xchg_owns(const FwdParams& P, int r) {
+  const XchgParams& X = P.xchg;
+  const int b = r / P.g.CL;
+  return b >= X.first[X.rank] && b < X.first[X.rank] + X.count[X.rank];
+}
+
+// Batch shards, all threads of the last CTA after every own row was sent: each
+// row's f from the rank that holds it, added per warp in the single-rank order
+// (rows warp, warp + warps, ...), and written to f for the rows of other ranks
+// (the "none" reduction returns f of every row). A wait that runs out gives NaN.
+// Returns this thread's share of the loss; advances the epoch counter.
+__device__ __forceinline__ float xchg_finish_f(const FwdParams& P, unsigned long long epoch) {
+  const XchgParams& X = P.xchg;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x / 32;
+  const int CL = P.g.CL, rows = P.B_total * CL;
+  const int par = (int)(epoch & 1ull);
+  const unsigned tag = (unsigned)(epoch & 0xffffffffull);
+  unsigned char* own = X.mailbox[X.rank];
+  const unsigned long long t0 = ace_now_ns();
+  float mine = 0.0f;
+  for (int r = warp; r < rows; r += nw) {
+    const int b = r / CL;
+    int src = 0;
+    while (src + 1 < X.world && !(b >= X.first[src] && b < X.first[src] + X.count[src])) ++src;
+    float f = __int_as_float(0x7fc00000);
+    if (lane == 0) {
+      const unsigned long long* a = xchg_word(X, own, par, src, 0, r, 0, CL, 1);
+      unsigned long long word;
+      asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(word) : "l"(a) : "memory");
+      bool ok = true;
+      while ((unsigned)(word >> 32) != tag) {
+        if (ace_now_ns() - t0 > kXchgWaitNs) {
+          ok = false;
+          break;
+        }
+        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(word) : "l"(a) : "memory");
+      }
+      if (ok) f = __uint_as_float((unsigned)word);
+      if (src != X.rank) P.epi.f[r] = f;
+    }
+    mine = ACE_FADD(mine, __shfl_sync(0xffffffffu, f, 0));
   }
   __syncthreads();
   if (threadIdx.x == 0) *reinterpret_cast<volatile unsigned long long*>(own) = epoch;
