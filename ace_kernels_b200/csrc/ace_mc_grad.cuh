@@ -16,9 +16,10 @@
 // Two phases per tile, the exponentials of all channels in registers: the first
 // computes p and gp per channel and the dot product sum p gp; the second writes
 // dx = p (gp - dot) with streaming stores. Up to 16 channels p and gp stay in
-// registers between the phases; above that the second phase recomputes them from
-// the exponentials (the 96 registers of a 544-thread CTA hold 2 C floats a lane,
-// not 4 C).
+// registers between the phases; above that (the 96 registers of a 544-thread CTA
+// hold 2 C floats a lane, not 4 C) the second phase recomputes p from the
+// exponentials and gp from the records, of the bins the first phase found and
+// packed (hard binning) or of the interval one FMA gives (soft binning).
 #pragma once
 
 namespace ace {
@@ -141,6 +142,23 @@ __global__ void __launch_bounds__(kPipeThreads, 1) mc_grad_kernel(const __grid_c
           return __ffma2_rn(__ffma2_rn(ns, q0, ec), y, q0);
         }
       };
+      // hard binning: the bins of the pair at p (mc_fwd_kernel's), and their records
+      auto bins = [&](float2 p) -> uint2 {
+        const float2 g = __fadd2_rn(__fadd2_rn(__fmul2_rn(p, K2), make_float2(-0.5f, -0.5f)), M2);
+        unsigned k0 = min(__float_as_uint(g.x) - kFixMagicBits, (unsigned)K);
+        unsigned k1 = min(__float_as_uint(g.y) - kFixMagicBits, (unsigned)K);
+        const float2 w = mc_offset(p, k0, k1, KR2);
+        if (!mc_proven(k0, w.x, K) && !ace_is_count(p.x, my_lohi[k0 * kTabCopies]))
+          k0 = (unsigned)ace_fix_count(p.x, (int)k0, K, my_lohi, kTabCopies).i;
+        if (!mc_proven(k1, w.y, K) && !ace_is_count(p.y, my_lohi[k1 * kTabCopies]))
+          k1 = (unsigned)ace_fix_count(p.y, (int)k1, K, my_lohi, kTabCopies).i;
+        return make_uint2(k0, k1);
+      };
+      auto records = [&](int c, uint2 k) -> float2 {
+        const unsigned cb = rbase + (unsigned)c * CS;
+        return make_float2(*reinterpret_cast<const float*>(smem_raw + (k.x * RS + cb)),
+                           *reinterpret_cast<const float*>(smem_raw + (k.y * RS + cb)));
+      };
       // gp of channel c >= OFF at p: its interval's record (soft) or its bin's
       // (hard: mc_fwd_kernel's bin)
       auto grad = [&](int c, float2 p) -> float2 {
@@ -155,24 +173,21 @@ __global__ void __launch_bounds__(kPipeThreads, 1) mc_grad_kernel(const __grid_c
           const float2 r1 = *reinterpret_cast<const float2*>(smem_raw + a1);
           return make_float2(__fmaf_rn(r0.y, p.x, r0.x), __fmaf_rn(r1.y, p.y, r1.x));
         } else {
-          const float2 g =
-              __fadd2_rn(__fadd2_rn(__fmul2_rn(p, K2), make_float2(-0.5f, -0.5f)), M2);
-          unsigned k0 = min(__float_as_uint(g.x) - kFixMagicBits, (unsigned)K);
-          unsigned k1 = min(__float_as_uint(g.y) - kFixMagicBits, (unsigned)K);
-          const float2 w = mc_offset(p, k0, k1, KR2);
-          if (!mc_proven(k0, w.x, K) && !ace_is_count(p.x, my_lohi[k0 * kTabCopies]))
-            k0 = (unsigned)ace_fix_count(p.x, (int)k0, K, my_lohi, kTabCopies).i;
-          if (!mc_proven(k1, w.y, K) && !ace_is_count(p.y, my_lohi[k1 * kTabCopies]))
-            k1 = (unsigned)ace_fix_count(p.y, (int)k1, K, my_lohi, kTabCopies).i;
-          return make_float2(*reinterpret_cast<const float*>(smem_raw + (k0 * RS + cb)),
-                             *reinterpret_cast<const float*>(smem_raw + (k1 * RS + cb)));
+          return records(c, bins(p));
         }
       };
       // channels in groups of four (one uniform branch each); a channel outside the
       // loss channels (dropped background, or past C) has gp = 0, its record read
-      // taken from the nearest loss channel's rows
+      // taken from the nearest loss channel's rows. Between the phases: p and gp
+      // (KEEP), or for hard binning the bins, 8 bits each, two channels' pairs a
+      // register (PACK: the second phase reads the records again but does not
+      // search), or nothing (soft: its record address is one FMA from p).
+      constexpr bool PACK = !KEEP && !SOFT;
       float2 dot = make_float2(0.0f, 0.0f);
       float2 gk[KEEP ? CM : 1];
+      unsigned kp[PACK ? (CM + 1) / 2 : 1];
+#pragma unroll
+      for (int i = 0; i < (PACK ? (CM + 1) / 2 : 1); ++i) kp[i] = 0u;
 #pragma unroll
       for (int c0 = 0; c0 < CM; c0 += 4) {
         if (c0 >= C) break;
@@ -180,7 +195,14 @@ __global__ void __launch_bounds__(kPipeThreads, 1) mc_grad_kernel(const __grid_c
         for (int j = 0; j < 4; ++j) {
           const int c = c0 + j;
           const float2 p = prob(e[c]);
-          const float2 g = grad(min(max(c, OFF), C - 1), p);
+          float2 g;
+          if constexpr (PACK) {
+            const uint2 k = bins(p);
+            kp[c >> 1] |= (k.x | (k.y << 8)) << (16 * (c & 1));
+            g = records(min(max(c, OFF), C - 1), k);
+          } else {
+            g = grad(min(max(c, OFF), C - 1), p);
+          }
           const float2 gp = c >= OFF && c < C ? g : make_float2(0.0f, 0.0f);
           dot = __ffma2_rn(p, gp, dot);
           if constexpr (KEEP) {
@@ -203,7 +225,13 @@ __global__ void __launch_bounds__(kPipeThreads, 1) mc_grad_kernel(const __grid_c
             gp = gk[c];
           } else {
             p = prob(e[c]);
-            const float2 g = grad(min(max(c, OFF), C - 1), p);
+            float2 g;
+            if constexpr (PACK) {
+              const unsigned w = kp[c >> 1] >> (16 * (c & 1));
+              g = records(min(max(c, OFF), C - 1), make_uint2(w & 0xffu, (w >> 8) & 0xffu));
+            } else {
+              g = grad(min(max(c, OFF), C - 1), p);
+            }
             gp = c >= OFF && c < C ? g : make_float2(0.0f, 0.0f);
           }
           if (c < C) stg_pair<T>(db + (int64_t)c * N, __fmul2_rn(p, __fadd2_rn(gp, nd)));
