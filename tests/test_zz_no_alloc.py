@@ -58,13 +58,14 @@ def test_static_matches_workspace_entry_point(name: str, spec: Spec, cfg: dict) 
     args = kernel_args(x, y, config)
     expected = outputs(args)
     forward_workspace(args, expected)
-    runs = []
-    for _ in range(2):  # two calls in a row: the second finds the scratch cleared
-        out = outputs(args)
+    runs = [outputs(args) for _ in range(2)]
+    torch.cuda.synchronize()
+    before = torch.cuda.memory_allocated()
+    for out in runs:  # two calls in a row: the second finds the scratch cleared
         rc = forward_static(args, out)
         _lib.check(rc, "ace_b200_forward_static")
-        runs.append(out)
     torch.cuda.synchronize()
+    assert torch.cuda.memory_allocated() == before  # nothing taken from torch's allocator
     for out in runs:
         for field in ("hist", "coef", "d", "jac", "f", "loss"):
             got, want = getattr(out, field), getattr(expected, field)
