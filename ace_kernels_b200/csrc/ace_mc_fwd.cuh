@@ -149,7 +149,8 @@ __device__ __forceinline__ void hard_finish(const FwdParams& P) {
   const bool xg = P.xchg.world > 1;  // ranks combined here (xchg_send_row, xchg_finish)
   const unsigned long long epoch = xg ? xchg_epoch(P.xchg) : 0ull;
   float mine = 0.0f;
-  for (int r = warp; r < rows; r += NT / 32) {
+  const int2 rr = xchg_rows(P);  // (batch shards: this rank's rows only)
+  for (int r = rr.x + warp; r < rr.y; r += NT / 32) {
     float wv[4], pv[4], gv[4];
 #pragma unroll
     for (int qq = 0; qq < 4; ++qq) {
@@ -170,7 +171,9 @@ __device__ __forceinline__ void hard_finish(const FwdParams& P) {
       P.hist_out[2 * m + e] = gv[qq];
     }
     if (xg && P.xchg.own_rows) {
-      if (xchg_owns(P, r)) xchg_send_f(P, epoch, r, epilogue_row(P.epi, r, wv, pv, gv));
+      const float f = epilogue_row(P.epi, r, wv, pv, gv);
+      xchg_send_f(P, epoch, r, f);
+      if (lane == 0) xchg_row_f()[r] = f;
     } else if (xg) {
       xchg_send_row(P, epoch, r, wv, pv, gv);
     } else if (P.do_epilogue) {

@@ -180,7 +180,8 @@ __device__ __forceinline__ void soft_finish(const FwdParams& P, const double4* s
   const bool failed = __ldcg(err) != 0u;  // a CTA's wait ran out: the sums are incomplete
   const float nan = __int_as_float(0x7fc00000);
   float mine = 0.0f;
-  for (int r = warp; r < rows; r += NT / 32) {
+  const int2 rr = xchg_rows(P);  // (batch shards: this rank's rows only)
+  for (int r = rr.x + warp; r < rr.y; r += NT / 32) {
     float wv[4], pv[4], gv[4];
     const int64_t row_slot = (int64_t)r * (K + 1) * 2;
 #pragma unroll
@@ -247,7 +248,9 @@ __device__ __forceinline__ void soft_finish(const FwdParams& P, const double4* s
 #pragma unroll
         for (int f = 0; f < 2; ++f) __stcg(acc + o * m + row_slot + 2 * j + f, 0ull);
     if (xg && P.xchg.own_rows) {
-      if (xchg_owns(P, r)) xchg_send_f(P, epoch, r, epilogue_row(P.epi, r, wv, pv, gv));
+      const float f = epilogue_row(P.epi, r, wv, pv, gv);
+      xchg_send_f(P, epoch, r, f);
+      if (lane == 0) xchg_row_f()[r] = f;
     } else if (xg) {
       xchg_send_row(P, epoch, r, wv, pv, gv);
     } else if (P.do_epilogue) {

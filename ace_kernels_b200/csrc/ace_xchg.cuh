@@ -6,9 +6,9 @@
 //
 // What crosses depends on the sharding. Batch shards (the ranks' samples
 // disjoint, own_rows): a sample's rows are complete on the rank that holds it, so
-// that rank runs their epilogue itself (coef, d, jac, f) and only each row's f
-// crosses, for every rank to add the loss in the single-rank order (bit for bit
-// the single-GPU loss). Spatial shards (every rank holds partial sums of every
+// that rank reconstructs and runs the epilogue of its own rows only (coef, d, jac,
+// f) and only each row's f crosses, for every rank to add the loss in the
+// single-rank order (bit for bit the single-GPU loss). Spatial shards (every rank holds partial sums of every
 // row): each rank's W, P, G cross, and every rank adds them in rank order and
 // runs the epilogue of every row.
 //
@@ -150,51 +150,68 @@ __device__ __forceinline__ void xchg_send_f(const FwdParams& P, unsigned long lo
   }
 }
 
-// Whether this rank holds row r.
-__device__ __forceinline__ bool xchg_owns(const FwdParams& P, int r) {
+// The rows the last CTA reconstructs: with batch shards only this rank's (the
+// other ranks' rows of its sums are empty), else all of them.
+__device__ __forceinline__ int2 xchg_rows(const FwdParams& P) {
   const XchgParams& X = P.xchg;
-  const int b = r / P.g.CL;
-  return b >= X.first[X.rank] && b < X.first[X.rank] + X.count[X.rank];
+  const int CL = P.g.CL;
+  if (X.world > 1 && X.own_rows)
+    return make_int2(X.first[X.rank] * CL, (X.first[X.rank] + X.count[X.rank]) * CL);
+  return make_int2(0, P.B_total * CL);
 }
 
-// Batch shards, all threads of the last CTA after every own row was sent: each
-// row's f from the rank that holds it, added per warp in the single-rank order
-// (rows warp, warp + warps, ...), and written to f for the rows of other ranks
-// (the "none" reduction returns f of every row). A wait that runs out gives NaN.
-// Returns this thread's share of the loss; advances the epoch counter.
+// Every row's f in the last CTA (batch shards; at most 256 rows, the limit of
+// the fused epilogue that the exchange requires).
+__device__ __forceinline__ float* xchg_row_f() {
+  __shared__ float s_f[8 * kEpiRowsPerCta];
+  return s_f;
+}
+
+// Batch shards, all threads of the last CTA after this rank's rows were sent and
+// their f put in xchg_row_f(): zeros into hist_out for the other ranks' rows, their
+// f from the ranks that hold them (one thread per row, waits bounded; NaN when one
+// runs out) into xchg_row_f() and f, then per warp the sum over rows warp,
+// warp + warps, ... in that order, as the single-rank path adds them. Returns this
+// warp's share of the loss; advances the epoch counter.
 __device__ __forceinline__ float xchg_finish_f(const FwdParams& P, unsigned long long epoch) {
   const XchgParams& X = P.xchg;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x / 32;
-  const int CL = P.g.CL, rows = P.B_total * CL;
+  const int tid = threadIdx.x, nt = blockDim.x, warp = tid >> 5, nw = nt / 32;
+  const int CL = P.g.CL, K = P.tab.K, rows = P.B_total * CL;
+  const int2 mine_rows = xchg_rows(P);
   const int par = (int)(epoch & 1ull);
   const unsigned tag = (unsigned)(epoch & 0xffffffffull);
   unsigned char* own = X.mailbox[X.rank];
+  float* s_f = xchg_row_f();
+  for (int64_t e = tid; e < 3 * (int64_t)rows * K; e += nt) {
+    const int r = (int)((e / K) % rows);
+    if (r < mine_rows.x || r >= mine_rows.y) P.hist_out[e] = 0.0f;
+  }
   const unsigned long long t0 = ace_now_ns();
-  float mine = 0.0f;
-  for (int r = warp; r < rows; r += nw) {
+  for (int r = tid; r < rows; r += nt) {
+    if (r >= mine_rows.x && r < mine_rows.y) continue;
     const int b = r / CL;
     int src = 0;
     while (src + 1 < X.world && !(b >= X.first[src] && b < X.first[src] + X.count[src])) ++src;
-    float f = __int_as_float(0x7fc00000);
-    if (lane == 0) {
-      const unsigned long long* a = xchg_word(X, own, par, src, 0, r, 0, CL, 1);
-      unsigned long long word;
-      asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(word) : "l"(a) : "memory");
-      bool ok = true;
-      while ((unsigned)(word >> 32) != tag) {
-        if (ace_now_ns() - t0 > kXchgWaitNs) {
-          ok = false;
-          break;
-        }
-        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(word) : "l"(a) : "memory");
+    const unsigned long long* a = xchg_word(X, own, par, src, 0, r, 0, CL, 1);
+    unsigned long long word;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(word) : "l"(a) : "memory");
+    bool ok = true;
+    while ((unsigned)(word >> 32) != tag) {
+      if (ace_now_ns() - t0 > kXchgWaitNs) {
+        ok = false;
+        break;
       }
-      if (ok) f = __uint_as_float((unsigned)word);
-      if (src != X.rank) P.epi.f[r] = f;
+      asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(word) : "l"(a) : "memory");
     }
-    mine = ACE_FADD(mine, __shfl_sync(0xffffffffu, f, 0));
+    const float f = ok ? __uint_as_float((unsigned)word) : __int_as_float(0x7fc00000);
+    s_f[r] = f;
+    P.epi.f[r] = f;
   }
   __syncthreads();
-  if (threadIdx.x == 0) *reinterpret_cast<volatile unsigned long long*>(own) = epoch;
+  float mine = 0.0f;
+  for (int r = warp; r < rows; r += nw) mine = ACE_FADD(mine, s_f[r]);
+  __syncthreads();
+  if (tid == 0) *reinterpret_cast<volatile unsigned long long*>(own) = epoch;
   return mine;
 }
 
