@@ -425,7 +425,9 @@ bool mc_fwd_setup(const ace_b200_inputs* in, const ace_b200_options* opt, Varian
   const int es = elem_size(in->x_dtype);
   if (!v.softmax || !v.labels || C > kMcMaxChannels || C < kMcMinChannels) return false;
   if (in->N % (16 / es) != 0 || !aligned(in->x, 16) || !aligned(in->target, 16)) return false;
-  const size_t stage_bytes = (size_t)kMcTileVoxels * (C * es + 8);
+  const int CM = C <= 8 ? 8 : C <= 16 ? 16 : 24;  // the instance's channel capacity
+  // a stage holds CM logit rows (the C of the tile, -inf padding) and the labels
+  const size_t stage_bytes = (size_t)kMcTileVoxels * (CM * es + 8);
   const size_t slot_bytes = (size_t)(soft ? (K + 1) * 2 : K) * C * 3 * 4;  // one replica
   const size_t lohi_bytes = soft ? 0 : (size_t)(K + 1) * kTabCopies * sizeof(float2);
   auto table = [&](int r) { return round_up(slot_bytes * r, 128); };
@@ -446,7 +448,7 @@ bool mc_fwd_setup(const ace_b200_inputs* in, const ace_b200_options* opt, Varian
   if (ctas > in->B * tiles) ctas = in->B * tiles;
   if (ctas < 1) ctas = 1;
   v.mc = true;
-  v.CM = C <= 8 ? 8 : C <= 16 ? 16 : 24;
+  v.CM = CM;
   smem = (int)need(R, stages);
   p.iacc = reinterpret_cast<unsigned long long*>(w.accum);
   p.pool_ctr = w.pool;
@@ -925,6 +927,7 @@ int ace_b200_backward(const ace_b200_inputs* in, const ace_b200_options* opt,
   if (v.softmax && (!soft || v.labels) && in->C >= kMcMinChannels && in->C <= kMcMaxChannels &&
       in->N % (16 / elem_size(in->x_dtype)) == 0 && aligned(in->x, 16) && aligned(dx, 16) &&
       (!soft || aligned(in->target, 16))) {
+    const int CM = in->C <= 8 ? 8 : in->C <= 16 ? 16 : 24;  // the instance's channel capacity
     const size_t stage_bytes =
         (size_t)kMcTileVoxels * (in->C * elem_size(in->x_dtype) + (soft ? 8 : 0));
     const size_t table_bytes = soft ? 0 : (size_t)(K + 1) * kTabCopies * sizeof(float2);
@@ -947,7 +950,7 @@ int ace_b200_backward(const ace_b200_inputs* in, const ace_b200_options* opt,
       if (ctas < 1) ctas = 1;
       v.mc = true;
       v.split = false;
-      v.CM = in->C <= 8 ? 8 : in->C <= 16 ? 16 : 24;
+      v.CM = CM;
       p.rec_copies = copies;
       p.stages = stages;
       p.stage_offset = (int)fixed(copies);

@@ -35,13 +35,13 @@ namespace ace {
 // CTA k mod grid), the sequence running from the batches' last tiles to their
 // first, the batches interleaved (k -> batch k % B, tile tpb - 1 - k / B). Each
 // tile's C logit rows (TV * sizeof(T) bytes apart) and, when `lab` is given, its
-// int64 labels (after the rows) go into stage i % S of the ring, with s_meta[s] =
+// int64 labels (after `rows` >= C row slots) go into stage i % S of the ring, with s_meta[s] =
 // {tile, batch, voxels, 0}; the last stage carries the end marker (tile -1). A
 // wait that runs out sets s_abort; the producer then waits (bounded) for its
 // copies still in flight.
 template <typename T, int TV>
 __device__ __forceinline__ void produce_round_robin(const T* x, const int64_t* lab, int C,
-                                                    int64_t N, int B, int64_t tpb,
+                                                    int rows, int64_t N, int B, int64_t tpb,
                                                     unsigned stage0, unsigned SB, int S,
                                                     unsigned long long* s_full,
                                                     unsigned long long* s_empty, int4* s_meta,
@@ -74,7 +74,7 @@ __device__ __forceinline__ void produce_round_robin(const T* x, const int64_t* l
     const unsigned dst = stage0 + (unsigned)s * SB;
     const T* gx = x + (int64_t)tb * C * N + v0;
     for (int c = 0; c < C; ++c) bulk_load(dst + c * XB, gx + (int64_t)c * N, xb, full);
-    if (lab) bulk_load(dst + C * XB, lab + (int64_t)tb * N + v0, (unsigned)cnt * 8u, full);
+    if (lab) bulk_load(dst + rows * XB, lab + (int64_t)tb * N + v0, (unsigned)cnt * 8u, full);
     issued = i + 1;
   }
   // after an abort, no copy may still be in flight when the CTA leaves
@@ -180,8 +180,8 @@ __global__ void __launch_bounds__(kPipeThreads, 1) grad_tma_kernel(const __grid_
     // kernel this one depends on: the copies may start before that kernel ends.
     if (lane == 0)
       produce_round_robin<T, TV>(static_cast<const T*>(P.x),
-                                 SOFT ? static_cast<const int64_t*>(P.target) : nullptr, C, N, B,
-                                 tpb, stage0, SB, S, s_full, s_empty, s_meta, &s_abort);
+                                 SOFT ? static_cast<const int64_t*>(P.target) : nullptr, C, C,
+                                 N, B, tpb, stage0, SB, S, s_full, s_empty, s_meta, &s_abort);
   } else {
     // ---------------- consumers ----------------
     // coef, d and jac come from the previous kernel: records only after it

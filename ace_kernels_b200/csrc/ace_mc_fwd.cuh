@@ -213,15 +213,50 @@ __device__ __forceinline__ void red_one_if(bool on, unsigned a, unsigned n) {
       "r"(a), "r"(n));
 }
 
+// A stage of mc_fwd_kernel holds CM logit rows: the tile's C rows, then
+// CM - C rows of -inf written once at kernel start (the bulk copies never touch
+// them). A padding row leaves a pair's maximum unchanged and its exponential is
+// exactly 0, so the channel loops need neither a clamp nor a select for them.
+template <typename T>
+struct NegInfWord;  // a 32-bit word of -inf values of type T
+template <>
+struct NegInfWord<float> {
+  static constexpr unsigned value = 0xff800000u;
+};
+template <>
+struct NegInfWord<__half> {
+  static constexpr unsigned value = 0xfc00fc00u;
+};
+template <>
+struct NegInfWord<__nv_bfloat16> {
+  static constexpr unsigned value = 0xff80ff80u;
+};
+
+template <typename T>
+__device__ __forceinline__ void fill_padding_rows(unsigned char* stage0, int S, unsigned SB,
+                                                  int C, int CM) {
+  constexpr unsigned XB = kMcTileVoxels * sizeof(T);
+  const unsigned neg_inf = NegInfWord<T>::value;
+  const int words = (int)(XB / 4) * (CM - C);
+  for (int s = 0; s < S; ++s) {
+    unsigned* w = reinterpret_cast<unsigned*>(stage0 + (size_t)s * SB + (size_t)C * XB);
+    for (int i = threadIdx.x; i < words; i += blockDim.x) w[i] = neg_inf;
+  }
+}
+
 // The pair's channel maximum and exponentials (ascending channels) and their sum,
 // from a stage: `my` is the lane's pair in channel row 0. Channels go in groups of
-// four with one (uniform) branch per group; inside a group a channel c >= C reads
-// row C - 1 (a repeated row leaves the maximum unchanged) and adds nothing to the
-// sum, so the group's four chains are straight-line code the compiler interleaves.
+// four with one (uniform) branch per group, so the group's four chains are
+// straight-line code the compiler interleaves. A channel c >= C of the last group
+// reads a -inf padding row (PAD: fill_padding_rows), or row C - 1 (a repeated row
+// leaves the maximum unchanged) and is then left out of the sum; e[c] is 0 or
+// unused. (The forward measured faster with the padding, the soft backward
+// slower: its extra registers spill.)
 // SOFT: ace_softmax_fast's 2^(x log2 e - m log2 e); else ace_softmax's expf(x - m).
-template <typename T, int CM, bool SOFT>
+template <typename T, int CM, bool SOFT, bool PAD>
 __device__ __forceinline__ float2 pair_exponentials(const unsigned char* my, int C, float2 (&e)[CM]) {
   constexpr unsigned XB = kMcTileVoxels * sizeof(T);
+  auto row = [&](int c) { return PAD ? c : min(c, C - 1); };
   float2 mx;
   if constexpr (sizeof(T) == 4) {
     mx = ld_pair<float>(my);
@@ -230,7 +265,7 @@ __device__ __forceinline__ float2 pair_exponentials(const unsigned char* my, int
       if (c0 >= C) break;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const float2 x = ld_pair<float>(my + min(c0 + j, C - 1) * XB);
+        const float2 x = ld_pair<float>(my + row(c0 + j) * XB);
         mx = make_float2(fmaxf(mx.x, x.x), fmaxf(mx.y, x.y));
       }
     }
@@ -241,7 +276,7 @@ __device__ __forceinline__ float2 pair_exponentials(const unsigned char* my, int
       if (c0 >= C) break;
 #pragma unroll
       for (int j = 0; j < 4; ++j)
-        mw = max2<T>(mw, *reinterpret_cast<const unsigned*>(my + min(c0 + j, C - 1) * XB));
+        mw = max2<T>(mw, *reinterpret_cast<const unsigned*>(my + row(c0 + j) * XB));
     }
     mx = widen2<T>(mw);
   }
@@ -254,7 +289,7 @@ __device__ __forceinline__ float2 pair_exponentials(const unsigned char* my, int
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int c = c0 + j;
-      const float2 x = ld_pair<T>(my + min(c, C - 1) * XB);
+      const float2 x = ld_pair<T>(my + row(c) * XB);
       if constexpr (SOFT) {
         const float2 arg = __ffma2_rn(x, make_float2(kLog2e, kLog2e), nm);
         e[c] = make_float2(ace_exp2_approx(arg.x), ace_exp2_approx(arg.y));
@@ -262,7 +297,7 @@ __device__ __forceinline__ float2 pair_exponentials(const unsigned char* my, int
         const float2 d = __fadd2_rn(x, nm);
         e[c] = make_float2(expf(d.x), expf(d.y));
       }
-      sum = __fadd2_rn(sum, c < C ? e[c] : make_float2(0.0f, 0.0f));
+      sum = __fadd2_rn(sum, PAD || c < C ? e[c] : make_float2(0.0f, 0.0f));
     }
   }
   return sum;
@@ -301,7 +336,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) mc_fwd_kernel(const __grid_co
   const int C = P.g.C, OFF = P.g.offset, CL = C - OFF;
   const int K = P.tab.K, R = P.R, S = P.stages;
   const int64_t N = P.g.N;
-  const unsigned SB = (unsigned)C * XB + TV * 8u;  // bytes of a stage (rows, then labels)
+  const unsigned SB = (unsigned)CM * XB + TV * 8u;  // bytes of a stage (CM rows, then labels)
   // shared memory: the table [slots][R][3] words, (hard) the bin-edge table
   // [K + 1][kTabCopies] float2, then the ring of stages
   unsigned* hist = reinterpret_cast<unsigned*>(smem_raw);
@@ -321,6 +356,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) mc_fwd_kernel(const __grid_co
   } else {
     for (int i = tid; i < (K + 1) * kTabCopies; i += NT) lohi_t[i] = P.tab.lohi[i / kTabCopies];
   }
+  fill_padding_rows<T>(smem_raw + P.stage_offset, S, SB, C, CM);
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(full_bar(s), 1u);
@@ -341,7 +377,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) mc_fwd_kernel(const __grid_co
     // ---------------- producer (one thread) ----------------
     if (lane == 0)
       produce_claimed<T, TV>(static_cast<const T*>(P.x), static_cast<const int64_t*>(P.target), C,
-                             N, P.g.B, P.wt_batch, P.pool_ctr, stage0, SB, S, s_full, s_empty,
+                             CM, N, P.g.B, P.wt_batch, P.pool_ctr, stage0, SB, S, s_full, s_empty,
                              s_meta, &s_abort, err);
   } else {
     // ---------------- consumers ----------------
@@ -412,9 +448,9 @@ __global__ void __launch_bounds__(kPipeThreads, 1) mc_fwd_kernel(const __grid_co
       ++since;
       const unsigned char* st = smem_raw + P.stage_offset + (size_t)s * SB;
       const unsigned char* my = st + (size_t)vo * sizeof(T);
-      const int2 lab = ld_labels2(st + (size_t)C * XB + (size_t)vo * 8);
+      const int2 lab = ld_labels2(st + (size_t)CM * XB + (size_t)vo * 8);
       float2 e[CM];
-      const float2 sum = pair_exponentials<T, CM, SOFT>(my, C, e);
+      const float2 sum = pair_exponentials<T, CM, SOFT, true>(my, C, e);
       __syncwarp();
       if (lane == 0) mbar_arrive(empty_bar(s));  // the stage may be refilled now
       if (warp * 32 * kMcLaneVoxels >= m.z) continue;  // the whole warp is past the batch's end

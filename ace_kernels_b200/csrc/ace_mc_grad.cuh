@@ -56,7 +56,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) mc_grad_kernel(const __grid_c
   const int C = P.g.C, OFF = P.g.offset, CL = C - OFF;
   const int K = P.tab.K, S = P.stages, B = P.g.B, copies = P.rec_copies;
   const int64_t N = P.g.N;
-  const unsigned SB = (unsigned)C * XB + (SOFT ? TV * 8u : 0u);  // rows, then labels
+  const unsigned SB = (unsigned)C * XB + (SOFT ? TV * 8u : 0u);  // C rows, then labels
   // shared memory: the records (see build_records), the bin table
   // [K + 1][kTabCopies] float2 (hard), then the ring of stages (128-aligned)
   float* rec = reinterpret_cast<float*>(smem_raw);
@@ -87,7 +87,8 @@ __global__ void __launch_bounds__(kPipeThreads, 1) mc_grad_kernel(const __grid_c
     // kernel this one depends on: the copies may start before that kernel ends.
     if (lane == 0)
       produce_round_robin<T, TV>(static_cast<const T*>(P.x),
-                                 SOFT ? static_cast<const int64_t*>(P.target) : nullptr, C, N, B,
+                                 SOFT ? static_cast<const int64_t*>(P.target) : nullptr, C, C,
+                                 N, B,
                                  P.tiles_per_batch, stage0, SB, S, s_full, s_empty, s_meta,
                                  &s_abort);
   } else {
@@ -125,7 +126,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) mc_grad_kernel(const __grid_c
       int2 lab = make_int2(-1, -1);
       if constexpr (SOFT) lab = ld_labels2(st + (size_t)C * XB + (size_t)vo * 8);
       float2 e[CM];  // the forward's exponentials (pair_exponentials)
-      const float2 sum = pair_exponentials<T, CM, SOFT>(my, C, e);
+      const float2 sum = pair_exponentials<T, CM, SOFT, false>(my, C, e);
       __syncwarp();
       if (lane == 0) mbar_arrive(empty_bar(s));  // the stage may be refilled now
       if (vo >= m.z) continue;                    // past the batch's last voxel (N is even)

@@ -320,7 +320,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) soft_fwd_kernel(const __grid_
     // ---------------- producer (one thread) ----------------
     if (lane == 0)
       produce_claimed<T, TV>(static_cast<const T*>(P.x), static_cast<const int64_t*>(P.target), C,
-                             N, B, tpb, P.pool_ctr, stage0, SB, S, s_full, s_empty, s_meta,
+                             C, N, B, tpb, P.pool_ctr, stage0, SB, S, s_full, s_empty, s_meta,
                              &s_abort, err);
   } else {
     // ---------------- consumers ----------------

@@ -188,11 +188,13 @@ __device__ __forceinline__ void lds_labels(unsigned a, int (&lab)[4]) {
 // blockIdx.x * B / gridDim.x and, when a batch runs out, takes tiles of another
 // one with tiles left. Each tile's C logit rows (TV * sizeof(T) bytes apart in
 // the stage) and its int64 labels (after the rows) are streamed into stage i % S
-// of the ring, with s_meta[s] = {tile, batch, voxels, 0}; the last stage carries
+// of the ring (the labels after `rows` >= C row slots), with s_meta[s] = {tile,
+// batch, voxels, 0}; the last stage carries
 // the end marker (tile -1, no copies). A wait that runs out sets s_abort and the
 // error word; the producer then waits (bounded) for its copies still in flight.
 template <typename T, int TV>
-__device__ __forceinline__ void produce_claimed(const T* x, const int64_t* lab, int C, int64_t N,
+__device__ __forceinline__ void produce_claimed(const T* x, const int64_t* lab, int C, int rows,
+                                                int64_t N,
                                                 int B, int64_t tpb, unsigned* ctr,
                                                 unsigned stage0, unsigned SB, int S,
                                                 unsigned long long* s_full,
@@ -245,7 +247,7 @@ __device__ __forceinline__ void produce_claimed(const T* x, const int64_t* lab, 
     const unsigned dst = stage0 + (unsigned)s * SB;
     const T* gx = x + (int64_t)tb * C * N + v0;
     for (int c = 0; c < C; ++c) bulk_load(dst + c * XB, gx + (int64_t)c * N, xb, full);
-    bulk_load(dst + C * XB, lab + (int64_t)tb * N + v0, lb, full);
+    bulk_load(dst + rows * XB, lab + (int64_t)tb * N + v0, lb, full);
     issued = i + 1;
   }
   // After an abort no copy may still be in flight when the CTA leaves: wait
