@@ -149,6 +149,7 @@ SIGNATURES: list[tuple[str, object, list[object]]] = [
         [POINTER(Inputs), POINTER(Options), c_void_p, EpilogueOut, c_void_p, c_size_t,
          POINTER(Exchange), c_void_p],
     ),
+    ("ace_b200_exchange_barrier", c_int, [POINTER(Exchange), c_void_p, c_void_p]),
     ("ace_b200_mailbox_bytes", c_size_t, [c_int64, c_int64, c_int32, c_int32]),
     ("ace_b200_mailbox_alloc", c_int, [c_size_t, POINTER(c_void_p)]),
     ("ace_b200_mailbox_free", c_int, [c_void_p]),

@@ -688,6 +688,52 @@ cudaError_t launch_epilogue(const float* hist, const EpiParams& e, unsigned* cou
   return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------
+// Barrier of the ranks of an exchange (ace_b200_exchange_barrier), one warp.
+// Barrier n (n = this rank's own barrier word + 1): lane d stores n into word
+// [rank] of rank d's mailbox header, then lane s waits until word [s] of this
+// rank's mailbox reaches n (rank s entered barrier n), at most kXchgWaitNs. The
+// words only grow, and each is written by one rank, so no reset is needed.
+// wait_ns: the longest lane's wait, or ~0 when a wait ran out.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(32) xchg_barrier_kernel(const __grid_constant__ XchgParams X,
+                                                          unsigned long long* wait_ns) {
+  const int lane = threadIdx.x;
+  unsigned long long* own =
+      reinterpret_cast<unsigned long long*>(X.mailbox[X.rank] + kXchgBarrierOffset);
+  unsigned long long n = 0ull;
+  if (lane == 0) asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(n) : "l"(own + X.rank) : "memory");
+  n = __shfl_sync(0xffffffffu, n, 0) + 1ull;
+  if (lane < X.world) {
+    unsigned long long* a =
+        reinterpret_cast<unsigned long long*>(X.mailbox[lane] + kXchgBarrierOffset) + X.rank;
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(a), "l"(n) : "memory");
+  }
+  const unsigned long long t0 = ace_now_ns();
+  unsigned long long waited = 0ull;
+  if (lane < X.world) {
+    for (;;) {
+      unsigned long long v;
+      asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(own + lane) : "memory");
+      const unsigned long long t = ace_now_ns() - t0;
+      if (v >= n) {
+        waited = t;
+        break;
+      }
+      if (t > kXchgWaitNs) {
+        waited = ~0ull;
+        break;
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long w = __shfl_xor_sync(0xffffffffu, waited, o);
+    waited = w > waited ? w : waited;
+  }
+  if (lane == 0 && wait_ns) *wait_ns = waited;
+}
+
 // Scratch of ace_b200_forward_static. A __device__ array has one instance per
 // device context, created when the module loads; the first call on each device
 // looks its address up (cudaGetSymbolAddress may load the module lazily, which a
@@ -793,6 +839,26 @@ int ace_b200_forward_exchange(const ace_b200_inputs* in, const ace_b200_options*
                               const ace_b200_exchange* xchg, void* stream) {
   if (!xchg) return fail(ACE_B200_EINVAL, "null exchange");
   return hist_impl(in, opt, hist, &out, workspace, workspace_bytes, stream, xchg);
+}
+
+int ace_b200_exchange_barrier(const ace_b200_exchange* xchg, uint64_t* wait_ns, void* stream) {
+  if (!xchg) return fail(ACE_B200_EINVAL, "null exchange");
+  if (xchg->world < 1 || xchg->world > kMaxPeers || xchg->rank < 0 || xchg->rank >= xchg->world)
+    return fail(ACE_B200_EINVAL, "bad exchange world=%d rank=%d", xchg->world, xchg->rank);
+  XchgParams x;
+  memset(&x, 0, sizeof(x));
+  x.world = xchg->world;
+  x.rank = xchg->rank;
+  for (int r = 0; r < xchg->world; ++r) {
+    if (!xchg->mailbox[r] || !aligned(xchg->mailbox[r], 16))
+      return fail(ACE_B200_EINVAL, "mailbox %d is null or misaligned", r);
+    x.mailbox[r] = static_cast<unsigned char*>(xchg->mailbox[r]);
+  }
+  if (wait_ns && !aligned(wait_ns, 8)) return fail(ACE_B200_EINVAL, "wait_ns is misaligned");
+  xchg_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, reinterpret_cast<unsigned long long*>(wait_ns));
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? ACE_B200_OK : cuda_fail(e, "barrier kernel launch");
 }
 
 int ace_b200_forward_static(const ace_b200_inputs* in, const ace_b200_options* opt, float* hist,

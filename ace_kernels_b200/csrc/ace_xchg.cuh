@@ -22,6 +22,8 @@
 // Mailbox of a rank (every rank's mailbox is mapped in every process through
 // CUDA IPC; plain loads and stores, no multicast):
 //   [0, 8)       calls completed so far (the epoch counter; its own rank only)
+//   [64, 128)    barrier words[world]: the number of barriers rank src has
+//                entered (xchg_barrier_kernel)
 //   [256, ...)   slots[2][world]: the source rank's rows, [3][rows][K] words
 //                {value bits, tag} (batch shards: [rows] words of f), tag = the low
 //                32 bits of the call number
@@ -35,6 +37,7 @@
 namespace ace {
 
 constexpr int kXchgHeaderBytes = 256;
+constexpr int kXchgBarrierOffset = 64;  // the barrier words of the header
 constexpr unsigned long long kXchgWaitNs = 2000000000ull;  // bound of the wait (2 s)
 
 // This call's number (the last CTA, any thread; the load overlaps the

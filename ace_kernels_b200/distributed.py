@@ -113,6 +113,31 @@ class PeerExchange:
                 self.struct.mailbox[r] = ptr.value
                 self.mapped.append(int(ptr.value))
 
+    def barrier(self, wait_ns: torch.Tensor | None = None) -> None:
+        """A device barrier of the group's ranks on the current stream
+        (``ace_b200_exchange_barrier``): every rank's later kernels start after
+        every rank has reached it. ``wait_ns``: a one-element int64 CUDA tensor
+        that receives this rank's wait (-1: a rank did not arrive within 2 s)."""
+        lib = _lib.load()
+        ptr = wait_ns.data_ptr() if wait_ns is not None else None
+        stream = torch.cuda.current_stream().cuda_stream
+        _lib.check(lib.ace_b200_exchange_barrier(ctypes.byref(self.struct), ptr, stream),
+                   "ace_b200_exchange_barrier")
+
+
+_barriers: dict[tuple[Any, ...], PeerExchange] = {}
+
+
+def device_barrier_for(device: torch.device, group: Any = None) -> PeerExchange:
+    """A PeerExchange used only for its barrier (the smallest mailbox), made by
+    all ranks of ``group`` together on first use and kept."""
+    key = (device.index, id(group))
+    ex = _barriers.get(key)
+    if ex is None:
+        ex = PeerExchange(device, group, 1, 1, 1, 0, 1)
+        _barriers[key] = ex
+    return ex
+
 
 _exchanges: dict[tuple[Any, ...], PeerExchange] = {}
 # Whether the last sharded forward of this process combined the ranks in-kernel

@@ -238,12 +238,68 @@ def flush_l2(flush: torch.Tensor) -> None:
     flush.view(torch.int64).sum()
 
 
+class Aligner:
+    """Lines the ranks up after each flush (N > 1), so that every rank's step
+    starts when the slowest rank's flush has ended (otherwise a rank whose flush
+    ended early would count its wait for the other ranks inside the step). It is
+    a device barrier over NVLink (``ace_b200_exchange_barrier``: one store into
+    every rank's mailbox, then a bounded wait for the others'), whose ranks leave
+    it within one NVLink trip of each other; where the ranks cannot map each
+    other's memory, a one-float NCCL all-reduce (whose ranks leave it further
+    apart). With the barrier, each call's wait on this rank is kept on the device
+    for the report."""
+
+    def __init__(self, dev: torch.device, slots: int = 4096) -> None:
+        from ace_kernels_b200.distributed import device_barrier_for
+
+        self.token = torch.zeros(1, device=dev)
+        self.waits = torch.zeros(slots, dtype=torch.int64, device=dev)
+        self.n = 0
+        try:
+            self.ex = device_barrier_for(dev)
+            ok = 1.0
+        except (RuntimeError, ValueError) as exc:
+            self.ex, ok, self.why = None, 0.0, str(exc)
+        flag = torch.tensor([ok], device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)  # every rank takes the same way
+        if flag.item() < 1.0:
+            self.ex = None
+        self.method = ("device barrier over NVLink (ace_b200_exchange_barrier)" if self.ex is not None
+                       else "NCCL all-reduce of one float")
+
+    def reset(self) -> None:
+        self.n = 0
+
+    def __call__(self) -> None:
+        if self.ex is None:
+            dist.all_reduce(self.token)
+            return
+        i = self.n % self.waits.numel()
+        self.ex.barrier(self.waits[i:i + 1])
+        self.n += 1
+
+    def summary(self, world: int, dev: torch.device) -> dict:
+        """The method and, for the barrier, this rank's waits since reset() (how
+        long it waited for the last rank to arrive), median and max, each the
+        max over ranks; timeouts counted."""
+        info: dict = {"method": self.method}
+        if self.ex is None or self.n == 0:
+            return info
+        w = self.waits[: min(self.n, self.waits.numel())].double()
+        timeouts = float((w < 0).sum().item())
+        ok = w[w >= 0]
+        med = float(ok.median().item()) / 1e3 if ok.numel() else float("nan")
+        mx = float(ok.max().item()) / 1e3 if ok.numel() else float("nan")
+        info["wait_us_median"] = max_over_ranks(med, world, dev)
+        info["wait_us_max"] = max_over_ranks(mx, world, dev)
+        info["timeouts"] = max_over_ranks(timeouts, world, dev)
+        return info
+
+
 def time_events(fn, flush: torch.Tensor, reps: int, align=None) -> float:  # type: ignore[no-untyped-def]
     """Summed device milliseconds of ``reps`` calls, L2 flushed before each.
-    ``align`` (N > 1): a tiny all-reduce after the flush, so that every rank's
-    step starts when the slowest rank's flush has ended (otherwise a rank whose
-    flush ended early would count its wait for the other ranks inside the step's
-    collective)."""
+    ``align`` (N > 1): an :class:`Aligner`, called after the flush and before
+    the step's start event."""
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
     for i in range(reps):
@@ -375,12 +431,7 @@ def run_ours(args: argparse.Namespace) -> None:
         return g
 
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
-    align = None
-    if world > 1:
-        token = torch.zeros(1, device=dev)
-
-        def align() -> None:
-            dist.all_reduce(token)
+    align = Aligner(dev) if world > 1 else None
 
     for _ in range(max(3, args.warmup)):
         step()
@@ -402,9 +453,12 @@ def run_ours(args: argparse.Namespace) -> None:
         dist.barrier()
     torch.cuda.synchronize()
     sampler = ClockSampler(local)
+    if align is not None:
+        align.reset()
     with sampler:
         total_ms = time_events(run, flush, args.steps, align)
     torch.cuda.synchronize()
+    align_info = align.summary(world, dev) if align is not None else None
     total_ms = max_over_ranks(total_ms, world, dev)
     ms_per_step = total_ms / args.steps
     value = voxels_all / (ms_per_step * 1e-3)
@@ -516,6 +570,8 @@ def run_ours(args: argparse.Namespace) -> None:
             "pipeline": "two input buffers; the next step's host-to-device copy overlaps this step's kernels",
         },
     }
+    if align_info is not None:
+        line["align"] = align_info
     if phases is not None:
         line["phases_us"] = phases
     if parity is not None:

@@ -220,6 +220,19 @@ int ace_b200_forward_exchange(const ace_b200_inputs* in, const ace_b200_options*
                               void* stream);
 
 /*
+ * A barrier of the ranks of an exchange on the device, over the same mailboxes
+ * (one warp: a 64-bit store into every rank's mailbox, then a wait until every
+ * rank's store has arrived in this rank's). It orders the ranks' kernels in time
+ * only, not memory. No counterpart in the reference; it lines the ranks up
+ * before a timed step more tightly than an all-reduce, whose ranks leave it at
+ * different times. `wait_ns` (device, optional) receives how long this rank
+ * waited, or UINT64_MAX when a rank did not arrive within about 2 s (the kernel
+ * then returns). All ranks must make the same number of these calls; their
+ * kernels must run on different GPUs. Only world, rank and mailbox are used.
+ */
+int ace_b200_exchange_barrier(const ace_b200_exchange* xchg, uint64_t* wait_ns, void* stream);
+
+/*
  * Statistics only (the first half of ace_b200_forward), for callers that reduce
  * the statistics across ranks (NCCL all-reduce of `hist`) before the epilogue.
  * Replaces hard_hist_fused / soft_hist_fused (ace_kernels/kernels/hard_hist.py:186-233,

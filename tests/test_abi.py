@@ -145,6 +145,15 @@ def test_errors_are_reported() -> None:
     opts = _lib.Options(num_bins=20)
     rc = lib.ace_b200_forward(None, ctypes.byref(opts), None, _lib.EpilogueOut(), None, 0, None)
     assert rc == _lib.EINVAL
+    # the barrier checks its exchange before launching anything
+    assert lib.ace_b200_exchange_barrier(None, None, None) == _lib.EINVAL
+    for world, rank in ((0, 0), (_lib.MAX_PEERS + 1, 0), (2, 2), (2, -1)):
+        ex = _lib.Exchange(world=world, rank=rank)
+        assert lib.ace_b200_exchange_barrier(ctypes.byref(ex), None, None) == _lib.EINVAL
+    ex = _lib.Exchange(world=2, rank=0)
+    ex.mailbox[0] = 4096  # rank 1's mailbox missing
+    assert lib.ace_b200_exchange_barrier(ctypes.byref(ex), None, None) == _lib.EINVAL
+    assert b"mailbox 1" in lib.ace_b200_last_error()
 
 
 def test_last_plan_before_any_launch() -> None:

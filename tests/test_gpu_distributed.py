@@ -127,3 +127,47 @@ def test_two_gpus_match_single_gpu(name: str, mode: str) -> None:
     for p in procs:
         p.join(timeout=120)
     assert results == {0: "ok", 1: "ok"}, results
+
+
+def _barrier_worker(rank: int, world: int, port: int, q) -> None:  # type: ignore[no-untyped-def]
+    import datetime
+
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                                timeout=datetime.timedelta(seconds=60))
+        ex = dd.device_barrier_for(dev)
+        waits = torch.full((4,), -7, dtype=torch.int64, device=dev)
+        for i in range(4):
+            if rank == 1:
+                torch.cuda._sleep(50_000_000)  # rank 1 arrives tens of ms late
+            ex.barrier(waits[i:i + 1])
+        torch.cuda.synchronize()
+        got = [int(v) for v in waits.tolist()]
+        assert all(v >= 0 for v in got), got  # nobody timed out
+        if rank == 0:  # rank 0 waited for rank 1's sleep each time
+            assert min(got) > 5_000_000, got
+        else:
+            assert max(got) < 5_000_000, got
+        q.put((rank, "ok"))
+    except Exception:  # reported to the parent, which fails the test
+        q.put((rank, traceback.format_exc()))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_gpu_device_barrier_waits_for_the_late_rank() -> None:
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_barrier_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+    assert results == {0: "ok", 1: "ok"}, results

@@ -1,6 +1,7 @@
-"""The in-kernel exchange's bounded wait, on one GPU: a forward told it has a
-second rank whose flag nothing ever sets gives up after about two seconds,
-returns a NaN loss, and leaves the context usable (no fault, no hang)."""
+"""The in-kernel exchange's bounded waits, on one GPU: a forward (or a barrier)
+told it has a second rank whose flag nothing ever sets gives up after about two
+seconds, returns a NaN loss (reports the timeout), and leaves the context usable
+(no fault, no hang)."""
 
 import ctypes
 import time
@@ -94,3 +95,47 @@ def test_exchange_rejects_bad_arguments_and_unpipelined_cases() -> None:
     finally:
         torch.cuda.synchronize()
         lib.ace_b200_mailbox_free(box)
+
+
+def test_barrier_alone_passes_and_without_peer_runs_out() -> None:
+    """ace_b200_exchange_barrier: a single rank passes at once; a rank told of a
+    second rank that never arrives gives up after about two seconds and reports
+    the timeout (-1), and the context stays usable."""
+    lib = _lib.load()
+    nbytes = lib.ace_b200_mailbox_bytes(1, 1, 1, 2)
+    boxes = [ctypes.c_void_p(), ctypes.c_void_p()]
+    for b in boxes:
+        _lib.check(lib.ace_b200_mailbox_alloc(nbytes, ctypes.byref(b)), "ace_b200_mailbox_alloc")
+    wait = torch.full((2,), -7, dtype=torch.int64, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    try:
+        alone = _lib.Exchange(world=1, rank=0)
+        alone.mailbox[0] = boxes[0].value
+        for _ in range(3):
+            _lib.check(lib.ace_b200_exchange_barrier(ctypes.byref(alone), wait.data_ptr(), stream),
+                       "ace_b200_exchange_barrier")
+        torch.cuda.synchronize()
+        assert 0 <= int(wait[0].item()) < 100_000_000  # ns
+        pair = _lib.Exchange(world=2, rank=0)
+        pair.mailbox[0], pair.mailbox[1] = boxes[0].value, boxes[1].value
+        t0 = time.perf_counter()
+        _lib.check(lib.ace_b200_exchange_barrier(ctypes.byref(pair), wait[1:].data_ptr(), stream),
+                   "ace_b200_exchange_barrier")
+        torch.cuda.synchronize()
+        waited = time.perf_counter() - t0
+        assert int(wait[1].item()) == -1  # UINT64_MAX: rank 1 never arrived
+        assert 1.5 < waited < 30.0, waited
+        x, y = make(Spec(2, 3, (16, 16, 16), seed=1), 20, "cuda")
+        cfg = to_config({"binning": "soft", "to_onehot_y": True})
+        assert torch.isfinite(ace_loss(x, y, cfg, impl="b200_cuda")).item()
+        # argument checks (nothing launched)
+        assert lib.ace_b200_exchange_barrier(None, None, stream) == _lib.EINVAL
+        assert lib.ace_b200_exchange_barrier(
+            ctypes.byref(_lib.Exchange(world=2, rank=2)), None, stream) == _lib.EINVAL
+        missing = _lib.Exchange(world=2, rank=0)
+        missing.mailbox[0] = boxes[0].value
+        assert lib.ace_b200_exchange_barrier(ctypes.byref(missing), None, stream) == _lib.EINVAL
+    finally:
+        torch.cuda.synchronize()
+        for b in boxes:
+            lib.ace_b200_mailbox_free(b)
