@@ -192,23 +192,67 @@ __global__ void __launch_bounds__(kPipeThreads, 1) mc_grad_kernel(const __grid_c
 #pragma unroll
       for (int c0 = 0; c0 < CM; c0 += 4) {
         if (c0 >= C) break;
+        if constexpr (SOFT) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int c = c0 + j;
-          const float2 p = prob(e[c]);
-          float2 g;
-          if constexpr (PACK) {
-            const uint2 k = bins(p);
-            kp[c >> 1] |= (k.x | (k.y << 8)) << (16 * (c & 1));
-            g = records(min(max(c, OFF), C - 1), k);
-          } else {
-            g = grad(min(max(c, OFF), C - 1), p);
+          for (int j = 0; j < 4; ++j) {
+            const int c = c0 + j;
+            const float2 p = prob(e[c]);
+            const float2 g = grad(min(max(c, OFF), C - 1), p);
+            const float2 gp = c >= OFF && c < C ? g : make_float2(0.0f, 0.0f);
+            dot = __ffma2_rn(p, gp, dot);
+            if constexpr (KEEP) {
+              e[c] = p;
+              gk[c] = gp;
+            }
           }
-          const float2 gp = c >= OFF && c < C ? g : make_float2(0.0f, 0.0f);
-          dot = __ffma2_rn(p, gp, dot);
-          if constexpr (KEEP) {
-            e[c] = p;
-            gk[c] = gp;
+        } else {
+          // hard binning, as mc_fwd_kernel: the guesses and their proofs of a
+          // group of G channels first, then one (rarely taken) branch for the
+          // table search of the values near an edge; a channel outside the loss
+          // channels keeps its guess (in 0..K, a valid record index; its gp is 0).
+          // With PACK the exponentials stay in registers for the second phase, so
+          // the groups are halves (fewer values live at once).
+          constexpr int G = PACK ? 2 : 4;
+#pragma unroll
+          for (int h = 0; h < 4; h += G) {
+          float2 p[G];
+          unsigned k0[G], k1[G];
+          bool ok = true;
+#pragma unroll
+          for (int j = 0; j < G; ++j) {
+            const int c = c0 + h + j;
+            p[j] = prob(e[c]);
+            const float2 g =
+                __fadd2_rn(__fadd2_rn(__fmul2_rn(p[j], K2), make_float2(-0.5f, -0.5f)), M2);
+            k0[j] = min(__float_as_uint(g.x) - kFixMagicBits, (unsigned)K);
+            k1[j] = min(__float_as_uint(g.y) - kFixMagicBits, (unsigned)K);
+            const float2 w = mc_offset(p[j], k0[j], k1[j], KR2);
+            const bool act = c >= OFF && c < C;
+            ok = ok & (!act | (mc_proven(k0[j], w.x, K) & mc_proven(k1[j], w.y, K)));
+          }
+          if (!ok) {
+#pragma unroll
+            for (int j = 0; j < G; ++j) {
+              const int c = c0 + h + j;
+              if (c < OFF || c >= C) continue;
+              if (!ace_is_count(p[j].x, my_lohi[k0[j] * kTabCopies]))
+                k0[j] = (unsigned)ace_fix_count(p[j].x, (int)k0[j], K, my_lohi, kTabCopies).i;
+              if (!ace_is_count(p[j].y, my_lohi[k1[j] * kTabCopies]))
+                k1[j] = (unsigned)ace_fix_count(p[j].y, (int)k1[j], K, my_lohi, kTabCopies).i;
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < G; ++j) {
+            const int c = c0 + h + j;
+            if constexpr (PACK) kp[c >> 1] |= (k0[j] | (k1[j] << 8)) << (16 * (c & 1));
+            const float2 g = records(min(max(c, OFF), C - 1), make_uint2(k0[j], k1[j]));
+            const float2 gp = c >= OFF && c < C ? g : make_float2(0.0f, 0.0f);
+            dot = __ffma2_rn(p[j], gp, dot);
+            if constexpr (KEEP) {
+              e[c] = p[j];
+              gk[c] = gp;
+            }
+          }
           }
         }
       }
