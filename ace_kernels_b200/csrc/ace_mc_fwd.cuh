@@ -497,7 +497,8 @@ __global__ void __launch_bounds__(kPipeThreads, 1) mc_fwd_kernel(const __grid_co
         const float2 ns = make_float2(-sum.x, -sum.y);
         const float2 KR2 = make_float2(Kf * kMcRScale, Kf * kMcRScale);
         unsigned kt0 = (unsigned)K, kt1 = (unsigned)K;  // the true class's bin (K: none)
-        // Channels in groups of four. The bin of a value is the guess k of
+        // Channels in groups of four (two above 8 channels, where the exponentials
+        // of all channels fill most registers). The bin of a value is the guess k of
         // ace_guess; w = magic + round((p K - k) 2^20) is its in-bin offset, from one
         // fused multiply-add. An offset at least kMcEdgeMargin units inside (0, 2^20)
         // (for k = 0 only below the top) proves k: every edge of the bin table lies
@@ -505,7 +506,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) mc_fwd_kernel(const __grid_co
         // The rare values that fail (within the margin of an edge, or k = K) take
         // the table search of ace_locate, and their w is recomputed. A lane past the
         // batch's end, and a channel outside the loss channels, get bin K (no bin).
-        constexpr int G = 4;
+        constexpr int G = CM > 8 ? 2 : 4;
 #pragma unroll
         for (int c0 = 0; c0 < CM; c0 += G) {
           if (c0 >= C) break;
