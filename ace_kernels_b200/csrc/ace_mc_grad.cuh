@@ -143,39 +143,25 @@ __global__ void __launch_bounds__(kPipeThreads, 1) mc_grad_kernel(const __grid_c
           return __ffma2_rn(__ffma2_rn(ns, q0, ec), y, q0);
         }
       };
-      // hard binning: the bins of the pair at p (mc_fwd_kernel's), and their records
-      auto bins = [&](float2 p) -> uint2 {
-        const float2 g = __fadd2_rn(__fadd2_rn(__fmul2_rn(p, K2), make_float2(-0.5f, -0.5f)), M2);
-        unsigned k0 = min(__float_as_uint(g.x) - kFixMagicBits, (unsigned)K);
-        unsigned k1 = min(__float_as_uint(g.y) - kFixMagicBits, (unsigned)K);
-        const float2 w = mc_offset(p, k0, k1, KR2);
-        if (!mc_proven(k0, w.x, K) && !ace_is_count(p.x, my_lohi[k0 * kTabCopies]))
-          k0 = (unsigned)ace_fix_count(p.x, (int)k0, K, my_lohi, kTabCopies).i;
-        if (!mc_proven(k1, w.y, K) && !ace_is_count(p.y, my_lohi[k1 * kTabCopies]))
-          k1 = (unsigned)ace_fix_count(p.y, (int)k1, K, my_lohi, kTabCopies).i;
-        return make_uint2(k0, k1);
-      };
+      // hard binning: the records of the pair's bins k in channel c's row
       auto records = [&](int c, uint2 k) -> float2 {
         const unsigned cb = rbase + (unsigned)c * CS;
         return make_float2(*reinterpret_cast<const float*>(smem_raw + (k.x * RS + cb)),
                            *reinterpret_cast<const float*>(smem_raw + (k.y * RS + cb)));
       };
-      // gp of channel c >= OFF at p: its interval's record (soft) or its bin's
-      // (hard: mc_fwd_kernel's bin)
+      // soft binning: gp of channel c >= OFF at p, from its interval's record (the
+      // interval one FMA gives, as in mc_fwd_kernel). Hard binning finds its bins
+      // in the grouped search below.
       auto grad = [&](int c, float2 p) -> float2 {
         const unsigned cb = rbase + (unsigned)c * CS;
-        if constexpr (SOFT) {
-          const float2 t = __ffma2_rn(p, K2, M2);
-          const unsigned a0 =
-              __float_as_uint(t.x) * RS + cb + (lab.x == c ? (unsigned)copies * 8u : 0u);
-          const unsigned a1 =
-              __float_as_uint(t.y) * RS + cb + (lab.y == c ? (unsigned)copies * 8u : 0u);
-          const float2 r0 = *reinterpret_cast<const float2*>(smem_raw + a0);
-          const float2 r1 = *reinterpret_cast<const float2*>(smem_raw + a1);
-          return make_float2(__fmaf_rn(r0.y, p.x, r0.x), __fmaf_rn(r1.y, p.y, r1.x));
-        } else {
-          return records(c, bins(p));
-        }
+        const float2 t = __ffma2_rn(p, K2, M2);
+        const unsigned a0 =
+            __float_as_uint(t.x) * RS + cb + (lab.x == c ? (unsigned)copies * 8u : 0u);
+        const unsigned a1 =
+            __float_as_uint(t.y) * RS + cb + (lab.y == c ? (unsigned)copies * 8u : 0u);
+        const float2 r0 = *reinterpret_cast<const float2*>(smem_raw + a0);
+        const float2 r1 = *reinterpret_cast<const float2*>(smem_raw + a1);
+        return make_float2(__fmaf_rn(r0.y, p.x, r0.x), __fmaf_rn(r1.y, p.y, r1.x));
       };
       // channels in groups of four (one uniform branch each); a channel outside the
       // loss channels (dropped background, or past C) has gp = 0, its record read
