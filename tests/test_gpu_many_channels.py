@@ -99,6 +99,13 @@ def test_many_channel_background_dropped(binning: str) -> None:
     x = x.to(torch.float16)
     plan = _stats_and_plan(x, y, cfg)
     assert plan.kernel == _lib.KERNEL_MC_PIPE
+    # the backward with channel 0 outside the loss channels (its gp is 0, its
+    # softmax term still in every other channel's gradient)
+    assert _backward_kernel(x, y, cfg) == _lib.KERNEL_MC_GRAD
+    res = run("b200_cuda", x, y, cfg)
+    loss, grad = oracle.loss_and_grad(x.float(), y, cfg)
+    torch.testing.assert_close(res.loss.cpu(), loss, rtol=LOSS_RTOL, atol=LOSS_ATOL)
+    torch.testing.assert_close(res.grad.float().cpu(), grad, rtol=1e-2, atol=1e-6)
 
 
 def test_many_channel_fallbacks() -> None:
